@@ -1,0 +1,111 @@
+/* gem-b200: a B200 (sm_100a) implementation of the per-token scoring path of prefix-head's `gem`
+ * Gemma 3 runtime, behind a C ABI.
+ *
+ * The reference has no FFI layer: its boundary is gem's internal Rust API (crates/gem/src/model.rs,
+ * q8.rs, main.rs). Each entry point below names the Rust function it stands in for, so a Rust host
+ * can bind this header with an `extern "C"` block and keep its call sites.
+ *
+ * Conventions
+ *   - Every function returns int: 0 (GEM_OK) or a negative gem_status; gem_last_error() returns a
+ *     thread-local message for the last failure. Nothing panics, throws or aborts across the ABI.
+ *   - A gem_model owns all of its device memory, one CUDA stream and its CUDA graphs. Host buffers are
+ *     caller-owned and are filled before a call returns. A handle is not thread-safe (the reference's
+ *     &mut self): use one handle per host thread and GPU.
+ *   - Device-pointer variants (suffix _dev) take device buffers, enqueue on the model's stream and
+ *     return without synchronising; gem_sync() waits for them.
+ */
+#ifndef GEM_B200_H
+#define GEM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum gem_status {
+  GEM_OK = 0,
+  GEM_E_ARG = -1,      /* invalid argument (null pointer, bad size, unsupported option) */
+  GEM_E_IO = -2,       /* file missing, unreadable or truncated */
+  GEM_E_FORMAT = -3,   /* GGUF or class-file content the runtime does not support */
+  GEM_E_CUDA = -4,     /* CUDA runtime error */
+  GEM_E_NOMEM = -5,    /* device or host allocation failed */
+  GEM_E_STATE = -6,    /* call out of order (e.g. a head before any forward) */
+  GEM_E_RANGE = -7,    /* token id >= vocab, pos >= ctx, sequence index out of range */
+  GEM_E_NCCL = -8,     /* collective setup or communication failed */
+  GEM_E_TIMEOUT = -9,  /* a bounded device-side wait gave up; the kernel returned an error flag */
+} gem_status;
+
+typedef struct gem_model gem_model;
+
+typedef struct gem_info {
+  int64_t d, vocab, layers, n_heads, n_kv_heads, head_dim, ffn, ctx, window;
+  int64_t bos;              /* -1 when tokenizer.ggml.add_bos_token is false */
+  int64_t body_bits;        /* 8 or 4 (after requantization) */
+  int64_t head_bits;        /* 8, 4 or 16 */
+  int64_t classes, per;     /* two-level head: k classes of `per` rows (0 when not loaded) */
+  int64_t max_seqs;         /* sequences with their own KV cache */
+  int64_t body_bytes;       /* canonical (GGUF block size) bytes of the 7 projections x layers */
+  int64_t head_bytes;       /* canonical bytes of the output matrix */
+  int64_t device;
+} gem_info;
+
+const char* gem_last_error(void);
+int gem_version(void);
+
+/* Gemma::load(&Gguf, ctx, tie = false) + requantize(body_bits == 4, false) + requantize_head(head_bits)
+ * (crates/gem/src/model.rs:154, 268, 259; called as in crates/gem/src/main.rs:203-210). head_bits 0
+ * keeps the file's type. max_seqs > 1 allocates independent KV caches for batched scoring. */
+int gem_open(const char* gguf_path, int ctx, int body_bits, int head_bits, int device, int max_seqs,
+             gem_model** out);
+/* TwoLevel::load(&Gemma, prefix) (crates/gem/src/main.rs:57-76): reads prefix.order, prefix.A and
+ * prefix.b, and lays the output matrix out class by class on the device (rows permuted as
+ * Gemma::permute_head, model.rs:242-249), so a class is a contiguous block of rows. */
+int gem_open_twolevel(gem_model* m, const char* prefix);
+/* Drop (the reference frees on scope exit). */
+void gem_close(gem_model* m);
+int gem_get_info(const gem_model* m, gem_info* out);
+/* Clears a sequence's KV cache (the reference rebuilds its cache per run; bench reuses it). */
+int gem_reset(gem_model* m, int seq);
+int gem_sync(gem_model* m);
+
+/* Gemma::forward(tok, pos) (model.rs:286-430) on sequence 0: runs one token, appends to the KV
+ * cache, keeps the final-norm hidden state on the device for the head calls below and copies it to
+ * h_out (d floats) when h_out is not NULL. */
+int gem_forward(gem_model* m, uint32_t tok, uint32_t pos, float* h_out);
+/* Full::run + Full::logprob(target) (main.rs:30-37) on the last forward's hidden state; argmax is the
+ * first maximum of the logits (lean.rs:36-38). Either output may be NULL. */
+int gem_full_logprob(gem_model* m, uint32_t target, float* logprob, uint32_t* argmax);
+/* TwoLevel::logprob(target, h) (main.rs:101-107) on the last forward's hidden state. argmax: the
+ * greedy token of screening with the single most likely class (lean.rs:46-76 with top = 1). */
+int gem_twolevel_logprob(gem_model* m, uint32_t target, float* logprob, uint32_t* argmax);
+
+/* gem bench / gem check's scoring loop (main.rs:270-289) on sequence 0: BOS forward when the model
+ * has one, then for i < n: forward(toks[i], i + off), head logprob of toks[i + 1]. toks has n + 1
+ * entries; logprob_out / argmax_out have n (argmax_out may be NULL). head: 0 full, 1 two-level.
+ * Host buffers; the whole loop runs on the device as one CUDA graph per token. */
+int gem_score(gem_model* m, const uint32_t* toks, size_t n, int head, float* logprob_out,
+              uint32_t* argmax_out);
+/* Same loop on device buffers (toks_dev n + 1, outputs n), enqueued on the model's stream. */
+int gem_score_dev(gem_model* m, const uint32_t* toks_dev, size_t n, int head, float* logprob_dev,
+                  uint32_t* argmax_dev);
+
+/* Kernel-level entry points on caller-provided DEVICE buffers, enqueued on the model's stream.
+ * They stand in for q8::matvec (q8.rs:439-461) with Act::quantize (q8.rs:187-246) fused in front,
+ * Full::run/logprob (main.rs:30-37) and TwoLevel::logprob (main.rs:101-107), for a batch of hidden
+ * states. */
+/* y = layer matrix `which` of layer `layer` (0 q, 1 k, 2 v, 3 o, 4 gate, 5 up, 6 down; layer -1 = the
+ * output matrix in token order) times x: x has cols floats, y rows floats. */
+int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float* y_dev);
+/* Full head for `batch` hidden states h_dev[batch][d] with targets_dev[batch]. */
+int gem_head_full_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
+                      float* logprob_dev, uint32_t* argmax_dev);
+/* Two-level head for `batch` hidden states. */
+int gem_head_twolevel_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
+                          float* logprob_dev, uint32_t* argmax_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GEM_B200_H */

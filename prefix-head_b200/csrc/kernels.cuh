@@ -1,0 +1,92 @@
+// Kernel argument structs and launchers shared by the host runtime (runtime.cpp) and the kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+#ifdef __CUDACC__
+#include "common.cuh"
+#endif
+
+namespace gem {
+
+// A weight matrix on the device (crates/gem/src/q8.rs:9-15, repacked): bits 8 = int8 plane
+// [rows][cols]; bits 4 = GGUF Q4_0 nibble bytes [rows][cols/2]; bits 16 = f16 [rows][cols]. Scales
+// (bits 8/4) are one per 32 weights, [rows][cols/32], f16 as stored in the GGUF or f32 after
+// requantization (to_q8 / to_q4 produce f32 scales).
+struct MatView {
+  const void* q = nullptr;
+  const void* s = nullptr;
+  int rows = 0, cols = 0, bits = 8, scale_f32 = 0;
+};
+
+// Token, position, target and output slot of the step being run; written by k_begin_step (scoring
+// loop) or by a host copy (single-token calls).
+struct StepCur {
+  uint32_t tok, pos, target, slot;
+};
+
+struct AttnArgs {
+  const float* qkv;          // [nh*hd | nkv*hd | nkv*hd] raw projections
+  const float* bqkv;         // biases in the same layout (qwen2) or null
+  const float* q_norm;       // hd or null
+  const float* k_norm;       // hd or null
+  const float* rope_sin;     // [ctx][hd/2] for this layer's base
+  const float* rope_cos;
+  float* kcache;             // [ctx][nkv*hd]
+  float* vcache;
+  float* part;               // [nkv][nsplit][G][hd+2]
+  float* att_out;            // nh*hd (optional, for tests)
+  const StepCur* cur;
+  int nh, nkv, hd, window, chunk, nsplit;
+  float eps, qscale;
+};
+
+struct HeadArgs {
+  MatView w;                 // output matrix (rows in token order, or class-permuted)
+  const uint32_t* row_of;    // token -> row (null = identity)
+  const uint32_t* row_tok;   // row -> token (null = identity)
+  const int8_t* aq;          // [batch][d] quantized hidden states
+  const float* as;           // [batch][d/32]
+  const float* h;            // [batch][d] fp32 hidden states (F16 heads)
+  const uint32_t* targets;   // [batch] or null (then cur->target)
+  const StepCur* cur;
+  float* part;               // [batch][parts] x float4
+  float* tlogit;             // [batch]
+  float* lp_out;             // indexed by batch item, or cur->slot
+  uint32_t* am_out;
+};
+
+struct TwoLevelArgs {
+  MatView w;                 // class-permuted output matrix: class c = rows [c*per, c*per + n_c)
+  const float* A;            // [k][d] fp32
+  const float* b;            // [k]
+  const uint32_t* cls_of;    // token -> class
+  const uint32_t* pos_of;    // token -> position inside its class
+  const uint32_t* order;     // row -> token
+  const int8_t* aq;
+  const float* as;
+  const float* h;
+  const uint32_t* targets;
+  const StepCur* cur;
+  float* cl;                 // [batch][k]
+  float* inner;              // [batch][per]
+  float* lp_out;
+  uint32_t* am_out;
+  int k, per, class_ctas;
+};
+
+void launch_embed(const MatView& head, const uint32_t* row_of, const StepCur* cur, float scale, float* x, cudaStream_t st);
+void launch_dequant_rows(const MatView& w, size_t r0, int nrows, float* out, cudaStream_t st);
+void launch_residual_norm_quant(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d,
+                                int8_t* aq, float* as, float* xn_out, cudaStream_t st);
+void launch_quantize(const float* x, int n, int8_t* aq, float* as, cudaStream_t st);
+void launch_gemv(const MatView& w, const int8_t* aq, const float* as, const float* x, float* y, int sms, cudaStream_t st);
+void launch_attn(const AttnArgs& A, int8_t* aq, float* as, cudaStream_t st);
+void launch_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float* as, float* gout, cudaStream_t st);
+void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, StepCur* cur, cudaStream_t st);
+void launch_end_step(uint32_t* step, cudaStream_t st);
+int head_full_parts(int sms);
+void launch_head_full(const HeadArgs& H, int batch, int sms, cudaStream_t st);
+void launch_head_twolevel(const TwoLevelArgs& T, int batch, int sms, cudaStream_t st);
+
+}  // namespace gem

@@ -1,0 +1,701 @@
+// The C ABI of include/gem.h: model handle, load + upload, the per-token forward and heads as kernel
+// sequences on one stream, and the scoring loop as a CUDA graph per token.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/gem.h"
+#include "host.hpp"
+#include "kernels.cuh"
+
+using namespace gem;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw Error(e == cudaErrorMemoryAllocation ? GEM_E_NOMEM : GEM_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <typename T>
+T* dev_alloc(size_t n) {
+  void* p = nullptr;
+  if (n == 0) n = 1;
+  ck(cudaMalloc(&p, n * sizeof(T)), "cudaMalloc");
+  return (T*)p;
+}
+template <typename T>
+T* dev_upload(const std::vector<T>& v) {
+  T* p = dev_alloc<T>(v.size());
+  if (!v.empty()) ck(cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice), "upload");
+  return p;
+}
+
+struct DevMat {
+  MatView v;
+  size_t bytes = 0;  // q plane + scale plane as stored
+};
+
+DevMat upload_mat(const HostMat& m, std::vector<void*>& owned) {
+  DevMat d;
+  d.v.rows = (int)m.rows;
+  d.v.cols = (int)m.cols;
+  d.v.bits = m.bits;
+  d.v.scale_f32 = m.scale_f32() ? 1 : 0;
+  void* q = dev_upload(m.q);
+  owned.push_back(q);
+  d.v.q = q;
+  if (m.bits != 16) {
+    void* s = m.scale_f32() ? (void*)dev_upload(m.s32) : (void*)dev_upload(m.s16);
+    owned.push_back(s);
+    d.v.s = s;
+  }
+  d.bytes = canonical_bytes(m);
+  return d;
+}
+
+struct Layer {
+  DevMat qkv, o, gu, down;
+  float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn = nullptr, *ffn_norm = nullptr,
+        *post_ffw = nullptr, *bqkv = nullptr;
+  bool swa = false;
+  DevMat q_only, k_only, v_only, gate_only, up_only;  // views into qkv / gu for gem_matvec_dev
+};
+
+}  // namespace
+
+struct gem_model {
+  int device = 0, sms = 148;
+  cudaStream_t st = nullptr;
+  std::vector<void*> owned;
+  // geometry (model.rs:32-69)
+  int d = 0, vocab = 0, nl = 0, nh = 0, nkv = 0, hd = 0, ff = 0, window = 0, ctx = 0, max_seqs = 1;
+  float eps = 0, embed_scale = 1, rope_base = 10000;
+  bool silu = false, untied = false, gemma = true;
+  int64_t bos = -1;
+  int body_bits = 8, head_bits = 8;
+  size_t body_bytes = 0;
+  std::vector<Layer> layers;
+  DevMat head, emb;  // emb used only when the file has a separate output matrix
+  float* out_norm = nullptr;
+  float *rope_sin[2] = {nullptr, nullptr}, *rope_cos[2] = {nullptr, nullptr};
+  float *kc = nullptr, *vc = nullptr;  // [seq][layer][ctx][nkv*hd]
+  int chunk = 64, nsplit_swa = 1, nsplit_glob = 1;
+  // activations
+  float *x, *xn, *qkv, *att, *o, *gu, *g, *dn, *h, *part;
+  int8_t *aq_d, *aq_att, *aq_ff, *haq;
+  float *as_d, *as_att, *as_ff, *has;
+  // step state and outputs
+  StepCur* cur = nullptr;
+  StepCur* cur_host = nullptr;  // pinned
+  uint32_t *step = nullptr, *toks = nullptr, *am = nullptr;
+  float* lp = nullptr;
+  // heads
+  int hbatch = 0;
+  float *head_part = nullptr, *tlogit = nullptr, *cl = nullptr, *inner = nullptr;
+  // two-level (main.rs:40-51)
+  bool two = false;
+  int k = 0, per = 0;
+  DevMat blocks;
+  float *A = nullptr, *b = nullptr;
+  uint32_t *cls_of = nullptr, *pos_of = nullptr, *order = nullptr;
+  // graphs
+  cudaGraphExec_t score_graph[2] = {nullptr, nullptr};
+  bool have_h = false;
+
+  ~gem_model() {
+    if (st) cudaStreamSynchronize(st);
+    for (auto& g : score_graph)
+      if (g) cudaGraphExecDestroy(g);
+    for (void* p : owned) cudaFree(p);
+    if (cur_host) cudaFreeHost(cur_host);
+    if (st) cudaStreamDestroy(st);
+  }
+
+  template <typename T>
+  T* alloc(size_t n) {
+    T* p = dev_alloc<T>(n);
+    owned.push_back(p);
+    return p;
+  }
+  template <typename T>
+  T* upload(const std::vector<T>& v) {
+    T* p = dev_upload(v);
+    owned.push_back(p);
+    return p;
+  }
+  float* upload_or_null(const std::vector<float>& v) { return v.empty() ? nullptr : upload(v); }
+
+  void ensure_head_batch(int batch) {
+    if (batch <= hbatch) return;
+    int parts = head_full_parts(sms);
+    head_part = alloc<float>((size_t)batch * parts * 4);
+    tlogit = alloc<float>(batch);
+    if (two) {
+      cl = alloc<float>((size_t)batch * k);
+      inner = alloc<float>((size_t)batch * per);
+    }
+    hbatch = batch;
+  }
+
+  AttnArgs attn_args(int l, int seq) const {
+    const Layer& L = layers[l];
+    AttnArgs A{};
+    A.qkv = qkv;
+    A.bqkv = L.bqkv;
+    A.q_norm = L.q_norm;
+    A.k_norm = L.k_norm;
+    int tb = L.swa ? 0 : 1;
+    A.rope_sin = rope_sin[tb];
+    A.rope_cos = rope_cos[tb];
+    size_t layer_elems = (size_t)ctx * nkv * hd;
+    A.kcache = kc + ((size_t)seq * nl + l) * layer_elems;
+    A.vcache = vc + ((size_t)seq * nl + l) * layer_elems;
+    A.part = part;
+    A.att_out = att;
+    A.cur = cur;
+    A.nh = nh, A.nkv = nkv, A.hd = hd;
+    A.window = L.swa ? window : 0;
+    A.chunk = chunk;
+    A.nsplit = L.swa ? nsplit_swa : nsplit_glob;
+    A.eps = eps;
+    A.qscale = 1.0f / std::sqrt((float)hd);
+    return A;
+  }
+
+  // Gemma::forward (model.rs:286-430) for the token in *cur, KV cache of `seq`; leaves the final-norm
+  // hidden state in h and its quantization in (haq, has).
+  void enqueue_body(int seq) {
+    const DevMat& E = untied ? emb : head;
+    launch_embed(E.v, nullptr, cur, embed_scale, x, st);
+    for (int l = 0; l < nl; ++l) {
+      const Layer& L = layers[l];
+      const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
+      launch_residual_norm_quant(x, P ? dn : nullptr, P ? P->post_ffw : nullptr, L.attn_norm, eps, d, aq_d, as_d, xn, st);
+      launch_gemv(L.qkv.v, aq_d, as_d, xn, qkv, sms, st);
+      AttnArgs A = attn_args(l, seq);
+      launch_attn(A, aq_att, as_att, st);
+      launch_gemv(L.o.v, aq_att, as_att, att, o, sms, st);
+      launch_residual_norm_quant(x, o, L.post_attn, L.ffn_norm, eps, d, aq_d, as_d, xn, st);
+      launch_gemv(L.gu.v, aq_d, as_d, xn, gu, sms, st);
+      launch_glu_quant(gu, ff, silu ? 1 : 0, aq_ff, as_ff, g, st);
+      launch_gemv(L.down.v, aq_ff, as_ff, g, dn, sms, st);
+    }
+    launch_residual_norm_quant(x, dn, layers[nl - 1].post_ffw, out_norm, eps, d, haq, has, h, st);
+  }
+
+  HeadArgs head_args(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, float* lpo, uint32_t* amo) {
+    HeadArgs H{};
+    H.w = head.v;
+    H.aq = qa, H.as = sa, H.h = hh;
+    H.targets = targets;
+    H.cur = cur;
+    H.part = head_part;
+    H.tlogit = tlogit;
+    H.lp_out = lpo;
+    H.am_out = amo;
+    return H;
+  }
+  TwoLevelArgs tl_args(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, float* lpo, uint32_t* amo) {
+    TwoLevelArgs T{};
+    T.w = blocks.v;
+    T.A = A, T.b = b, T.cls_of = cls_of, T.pos_of = pos_of, T.order = order;
+    T.aq = qa, T.as = sa, T.h = hh;
+    T.targets = targets;
+    T.cur = cur;
+    T.cl = cl, T.inner = inner;
+    T.lp_out = lpo, T.am_out = amo;
+    T.k = k, T.per = per;
+    return T;
+  }
+  void enqueue_head(int which, float* lpo, uint32_t* amo) {
+    ensure_head_batch(1);
+    if (which == 0) launch_head_full(head_args(haq, has, h, nullptr, lpo, amo), 1, sms, st);
+    else launch_head_twolevel(tl_args(haq, has, h, nullptr, lpo, amo), 1, sms, st);
+  }
+
+  void check_launch() { ck(cudaGetLastError(), "kernel launch"); }
+  void sync() { ck(cudaStreamSynchronize(st), "stream sync"); }
+};
+
+namespace {
+
+int fail_with(const std::exception& e) {
+  g_last_error = e.what();
+  if (auto* ge = dynamic_cast<const Error*>(&e)) return ge->code;
+  return GEM_E_ARG;
+}
+#define API_BEGIN try {
+#define API_END                        \
+  }                                    \
+  catch (const std::exception& e) {    \
+    return fail_with(e);               \
+  }                                    \
+  return GEM_OK;
+
+void rope_tables(gem_model* m, float base_model) {  // model.rs:228, 297-301
+  float bases[2] = {10000.0f, base_model};
+  int half = m->hd / 2;
+  for (int t = 0; t < 2; ++t) {
+    std::vector<float> inv(half), sn((size_t)m->ctx * half), cs((size_t)m->ctx * half);
+    for (int i = 0; i < half; ++i) inv[i] = std::pow(bases[t], -2.0f * (float)i / (float)m->hd);
+    for (int p = 0; p < m->ctx; ++p)
+      for (int i = 0; i < half; ++i) {
+        float a = (float)p * inv[i];
+        sn[(size_t)p * half + i] = std::sin(a);
+        cs[(size_t)p * half + i] = std::cos(a);
+      }
+    m->rope_sin[t] = m->upload(sn);
+    m->rope_cos[t] = m->upload(cs);
+  }
+}
+
+// Gemma::load's metadata (model.rs:154-170, 191, 207-209); host-only, so a bad file fails before
+// any device work.
+void read_meta(gem_model* m, const Gguf& g, int ctx) {
+  std::string a = g.text("general.architecture");
+  bool gemma = a == "gemma3";
+  if (!gemma && a != "qwen2") throw Error(GEM_E_FORMAT, "unsupported architecture " + a);
+  m->gemma = gemma;
+  m->d = (int)g.u(a + ".embedding_length");
+  m->nl = (int)g.u(a + ".block_count");
+  m->nh = (int)g.u(a + ".attention.head_count");
+  m->nkv = (int)g.u(a + ".attention.head_count_kv");
+  m->hd = (int)g.u_or(a + ".attention.key_length", m->d / std::max(1, m->nh));
+  m->ff = (int)g.u(a + ".feed_forward_length");
+  m->eps = g.f(a + ".attention.layer_norm_rms_epsilon");
+  m->window = (int)g.u_or(a + ".attention.sliding_window", 0);
+  m->rope_base = g.f(a + ".rope.freq_base");
+  m->bos = g.flag("tokenizer.ggml.add_bos_token") ? (int64_t)g.u("tokenizer.ggml.bos_token_id") : -1;
+  m->embed_scale = gemma ? std::sqrt((float)m->d) : 1.0f;
+  m->silu = !gemma;
+  m->ctx = ctx;
+  if (m->nl <= 0 || m->nh <= 0 || m->nkv <= 0 || m->nh % m->nkv) throw Error(GEM_E_FORMAT, "bad head counts");
+  if (m->nh / m->nkv > 8) throw Error(GEM_E_FORMAT, "more than 8 query heads per kv head");
+  if (m->hd % 32 || m->hd > 256 || m->d % 32 || m->ff % 32) throw Error(GEM_E_FORMAT, "unsupported dimensions");
+  if (ctx <= 0) throw Error(GEM_E_ARG, "ctx must be positive");
+  const char* need[] = {"output_norm.weight", "blk.0.attn_q.weight", "blk.0.ffn_down.weight"};
+  for (const char* n : need) (void)g.info(n);
+  if (!g.has("token_embd.weight") && !g.has("output.weight")) throw Error(GEM_E_FORMAT, "no output matrix");
+}
+
+void load_model(gem_model* m, const Gguf& g, int body_bits, int head_bits) {
+  bool has_out = g.has("output.weight");
+  bool gemma = m->gemma;
+  float base = m->rope_base;
+  // output matrix (head) and embedding
+  HostMat head = load_mat(g, has_out ? "output.weight" : "token_embd.weight");
+  if (has_out) {  // tie = false: the embedding is its own matrix (model.rs:155-157, 255-257)
+    m->untied = true;
+    HostMat e = load_mat(g, "token_embd.weight");
+    m->emb = upload_mat(e, m->owned);
+  }
+  // requantize_head (model.rs:259-266); body_bits requantizes only the projections (main.rs:209)
+  if (head_bits == 8) head = to_q8(head);
+  else if (head_bits == 4) head = to_q4(head);
+  else if (head_bits != 0) throw Error(GEM_E_ARG, "head_bits must be 0, 4 or 8");
+  if (body_bits != 8 && body_bits != 4) throw Error(GEM_E_ARG, "body_bits must be 8 or 4");
+  m->head = upload_mat(head, m->owned);
+  m->vocab = (int)head.rows;
+  m->head_bits = head.bits;
+  if (head.cols != (size_t)m->d) throw Error(GEM_E_FORMAT, "output matrix width != embedding_length");
+
+  m->layers.resize(m->nl);
+  m->body_bytes = 0;
+  for (int l = 0; l < m->nl; ++l) {
+    auto p = [&](const char* s) { return "blk." + std::to_string(l) + "." + s; };
+    HostMat mq = load_mat(g, p("attn_q.weight")), mk = load_mat(g, p("attn_k.weight")), mv = load_mat(g, p("attn_v.weight"));
+    HostMat mo = load_mat(g, p("attn_output.weight"));
+    HostMat mg = load_mat(g, p("ffn_gate.weight")), mu = load_mat(g, p("ffn_up.weight")), md = load_mat(g, p("ffn_down.weight"));
+    if (body_bits == 4)  // requantize(body4) (model.rs:268-279)
+      for (HostMat* x : {&mq, &mk, &mv, &mo, &mg, &mu, &md}) *x = to_q4(*x);
+    if ((int)mq.rows != m->nh * m->hd || (int)mk.rows != m->nkv * m->hd || (int)mv.rows != m->nkv * m->hd ||
+        (int)mo.rows != m->d || (int)mo.cols != m->nh * m->hd || (int)mg.rows != m->ff || (int)md.cols != m->ff)
+      throw Error(GEM_E_FORMAT, "layer " + std::to_string(l) + ": projection shapes do not match the metadata");
+    for (HostMat* x : {&mq, &mk, &mv, &mo, &mg, &mu, &md}) m->body_bytes += canonical_bytes(*x);
+    Layer& L = m->layers[l];
+    L.qkv = upload_mat(concat_rows({&mq, &mk, &mv}), m->owned);
+    L.o = upload_mat(mo, m->owned);
+    L.gu = upload_mat(concat_rows({&mg, &mu}), m->owned);
+    L.down = upload_mat(md, m->owned);
+    L.attn_norm = m->upload_or_null(g.f32s(p("attn_norm.weight")));
+    L.q_norm = m->upload_or_null(g.f32s_or_empty(p("attn_q_norm.weight")));
+    L.k_norm = m->upload_or_null(g.f32s_or_empty(p("attn_k_norm.weight")));
+    L.post_attn = m->upload_or_null(g.f32s_or_empty(p("post_attention_norm.weight")));
+    L.ffn_norm = m->upload_or_null(g.f32s(p("ffn_norm.weight")));
+    L.post_ffw = m->upload_or_null(g.f32s_or_empty(p("post_ffw_norm.weight")));
+    std::vector<float> bq = g.f32s_or_empty(p("attn_q.bias")), bk = g.f32s_or_empty(p("attn_k.bias")), bv = g.f32s_or_empty(p("attn_v.bias"));
+    if (!bq.empty() || !bk.empty() || !bv.empty()) {
+      std::vector<float> all(mq.rows + mk.rows + mv.rows, 0.0f);
+      std::copy(bq.begin(), bq.end(), all.begin());
+      std::copy(bk.begin(), bk.end(), all.begin() + mq.rows);
+      std::copy(bv.begin(), bv.end(), all.begin() + mq.rows + mk.rows);
+      L.bqkv = m->upload(all);
+    }
+    L.swa = gemma && l % 6 < 5;  // model.rs:191
+    auto sub = [](const DevMat& M, int r0, int rows) {
+      DevMat v = M;
+      size_t rb = (size_t)M.v.cols * M.v.bits / 8;
+      v.v.q = (const uint8_t*)M.v.q + (size_t)r0 * rb;
+      if (M.v.s) v.v.s = (const uint8_t*)M.v.s + (size_t)r0 * (M.v.cols / 32) * (M.v.scale_f32 ? 4 : 2);
+      v.v.rows = rows;
+      return v;
+    };
+    L.q_only = sub(L.qkv, 0, (int)mq.rows);
+    L.k_only = sub(L.qkv, (int)mq.rows, (int)mk.rows);
+    L.v_only = sub(L.qkv, (int)(mq.rows + mk.rows), (int)mv.rows);
+    L.gate_only = sub(L.gu, 0, (int)mg.rows);
+    L.up_only = sub(L.gu, (int)mg.rows, (int)mu.rows);
+  }
+  m->body_bits = m->layers[0].qkv.v.bits;
+  std::vector<float> on = g.f32s("output_norm.weight");
+  if ((int)on.size() != m->d) throw Error(GEM_E_FORMAT, "output_norm size");
+  m->out_norm = m->upload(on);
+  rope_tables(m, base);
+
+  // KV caches and scratch
+  size_t kv = (size_t)m->max_seqs * m->nl * m->ctx * m->nkv * m->hd;
+  m->kc = m->alloc<float>(kv);
+  m->vc = m->alloc<float>(kv);
+  ck(cudaMemset(m->kc, 0, kv * 4), "memset");
+  ck(cudaMemset(m->vc, 0, kv * 4), "memset");
+  int max_npos_swa = m->window > 0 ? std::min(m->window, m->ctx) : m->ctx;
+  m->chunk = 64;
+  while ((m->ctx + m->chunk - 1) / m->chunk > 64) m->chunk *= 2;
+  m->nsplit_swa = (max_npos_swa + m->chunk - 1) / m->chunk;
+  m->nsplit_glob = (m->ctx + m->chunk - 1) / m->chunk;
+  int G = m->nh / m->nkv;
+  int qkv_rows = (m->nh + 2 * m->nkv) * m->hd;
+  int wide = std::max({m->d, m->nh * m->hd, m->ff});
+  m->x = m->alloc<float>(m->d);
+  m->xn = m->alloc<float>(m->d);
+  m->qkv = m->alloc<float>(qkv_rows);
+  m->att = m->alloc<float>(m->nh * m->hd);
+  m->o = m->alloc<float>(m->d);
+  m->gu = m->alloc<float>(2 * (size_t)m->ff);
+  m->g = m->alloc<float>(m->ff);
+  m->dn = m->alloc<float>(m->d);
+  m->h = m->alloc<float>(m->d);
+  m->part = m->alloc<float>((size_t)m->nkv * m->nsplit_glob * G * (m->hd + 2));
+  m->aq_d = m->alloc<int8_t>(wide);
+  m->aq_att = m->alloc<int8_t>(wide);
+  m->aq_ff = m->alloc<int8_t>(wide);
+  m->haq = m->alloc<int8_t>(m->d);
+  m->as_d = m->alloc<float>(wide / 32);
+  m->as_att = m->alloc<float>(wide / 32);
+  m->as_ff = m->alloc<float>(wide / 32);
+  m->has = m->alloc<float>(m->d / 32);
+  m->cur = m->alloc<StepCur>(1);
+  ck(cudaMallocHost(&m->cur_host, sizeof(StepCur)), "cudaMallocHost");
+  m->step = m->alloc<uint32_t>(1);
+  m->toks = m->alloc<uint32_t>((size_t)m->ctx + 1);
+  m->lp = m->alloc<float>(m->ctx);
+  m->am = m->alloc<uint32_t>(m->ctx);
+  m->ensure_head_batch(1);
+}
+
+std::vector<uint8_t> read_all(const std::string& p) {
+  std::ifstream f(p, std::ios::binary);
+  if (!f) throw Error(GEM_E_IO, p + ": cannot open");
+  return std::vector<uint8_t>((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gem_last_error(void) { return g_last_error.c_str(); }
+int gem_version(void) { return 1; }
+
+int gem_open(const char* gguf_path, int ctx, int body_bits, int head_bits, int device, int max_seqs, gem_model** out) {
+  API_BEGIN
+  if (!gguf_path || !out) throw Error(GEM_E_ARG, "null argument");
+  *out = nullptr;
+  if (max_seqs < 1) throw Error(GEM_E_ARG, "max_seqs must be >= 1");
+  if (body_bits != 8 && body_bits != 4) throw Error(GEM_E_ARG, "body_bits must be 8 or 4");
+  if (head_bits != 0 && head_bits != 8 && head_bits != 4) throw Error(GEM_E_ARG, "head_bits must be 0, 4 or 8");
+  auto m = std::make_unique<gem_model>();
+  Gguf g(gguf_path);
+  read_meta(m.get(), g, ctx);
+  ck(cudaSetDevice(device), "cudaSetDevice");
+  m->device = device;
+  m->max_seqs = max_seqs;
+  ck(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device), "device attribute");
+  ck(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking), "stream");
+  load_model(m.get(), g, body_bits, head_bits);
+  ck(cudaDeviceSynchronize(), "load");
+  *out = m.release();
+  API_END
+}
+
+int gem_open_twolevel(gem_model* m, const char* prefix) {
+  API_BEGIN
+  if (!m || !prefix) throw Error(GEM_E_ARG, "null argument");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  std::string p(prefix);
+  auto ob = read_all(p + ".order"), ab = read_all(p + ".A"), bb = read_all(p + ".b");
+  if (ob.size() % 4 || ab.size() % 4 || bb.size() % 4) throw Error(GEM_E_FORMAT, "class files are not whole 32-bit words");
+  std::vector<uint32_t> order(ob.size() / 4);
+  std::memcpy(order.data(), ob.data(), ob.size());
+  std::vector<float> A(ab.size() / 4), b(bb.size() / 4);
+  std::memcpy(A.data(), ab.data(), ab.size());
+  std::memcpy(b.data(), bb.data(), bb.size());
+  // TwoLevel::load (main.rs:57-76)
+  size_t k = b.size();
+  if (k == 0) throw Error(GEM_E_FORMAT, ".b is empty");
+  size_t per = (order.size() + k - 1) / k;
+  size_t chunks = (order.size() + per - 1) / per;
+  if (chunks != k) throw Error(GEM_E_FORMAT, ".order does not cut into as many classes as .b has entries");
+  if (A.size() != k * (size_t)m->d) throw Error(GEM_E_FORMAT, ".A is not classes x d floats");
+  std::vector<uint32_t> cls_of(m->vocab, 0), pos_of(m->vocab, 0);
+  for (size_t i = 0; i < order.size(); ++i) {
+    if (order[i] >= (uint32_t)m->vocab) throw Error(GEM_E_FORMAT, ".order holds a token id >= vocab");
+    cls_of[order[i]] = (uint32_t)(i / per);
+    pos_of[order[i]] = (uint32_t)(i % per);
+  }
+  // Gather the class blocks (main.rs:74) from the device head into a class-ordered copy.
+  HostMat hm;
+  hm.bits = m->head.v.bits, hm.rows = (size_t)m->head.v.rows, hm.cols = (size_t)m->head.v.cols;
+  hm.q.resize(hm.rows * hm.row_bytes());
+  ck(cudaMemcpy(hm.q.data(), m->head.v.q, hm.q.size(), cudaMemcpyDeviceToHost), "download head");
+  if (hm.bits != 16) {
+    size_t ns = hm.rows * hm.cols / 32;
+    if (m->head.v.scale_f32) {
+      hm.s32.resize(ns);
+      ck(cudaMemcpy(hm.s32.data(), m->head.v.s, ns * 4, cudaMemcpyDeviceToHost), "download scales");
+    } else {
+      hm.s16.resize(ns);
+      ck(cudaMemcpy(hm.s16.data(), m->head.v.s, ns * 2, cudaMemcpyDeviceToHost), "download scales");
+    }
+  }
+  HostMat blocks = gather_rows(hm, order);
+  m->blocks = upload_mat(blocks, m->owned);
+  m->A = m->upload(A);
+  m->b = m->upload(b);
+  m->cls_of = m->upload(cls_of);
+  m->pos_of = m->upload(pos_of);
+  m->order = m->upload(order);
+  m->k = (int)k;
+  m->per = (int)per;
+  m->two = true;
+  m->hbatch = 0;
+  m->ensure_head_batch(1);
+  if (m->score_graph[1]) {
+    cudaGraphExecDestroy(m->score_graph[1]);
+    m->score_graph[1] = nullptr;
+  }
+  ck(cudaDeviceSynchronize(), "twolevel load");
+  API_END
+}
+
+void gem_close(gem_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  delete m;
+}
+
+int gem_get_info(const gem_model* m, gem_info* o) {
+  API_BEGIN
+  if (!m || !o) throw Error(GEM_E_ARG, "null argument");
+  o->d = m->d, o->vocab = m->vocab, o->layers = m->nl, o->n_heads = m->nh, o->n_kv_heads = m->nkv;
+  o->head_dim = m->hd, o->ffn = m->ff, o->ctx = m->ctx, o->window = m->window, o->bos = m->bos;
+  o->body_bits = m->body_bits, o->head_bits = m->head_bits, o->classes = m->two ? m->k : 0, o->per = m->two ? m->per : 0;
+  o->max_seqs = m->max_seqs, o->body_bytes = (int64_t)m->body_bytes, o->head_bytes = (int64_t)m->head.bytes, o->device = m->device;
+  API_END
+}
+
+int gem_reset(gem_model* m, int seq) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  if (seq < 0 || seq >= m->max_seqs) throw Error(GEM_E_RANGE, "sequence index out of range");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  size_t per_seq = (size_t)m->nl * m->ctx * m->nkv * m->hd;
+  ck(cudaMemsetAsync(m->kc + (size_t)seq * per_seq, 0, per_seq * 4, m->st), "memset");
+  ck(cudaMemsetAsync(m->vc + (size_t)seq * per_seq, 0, per_seq * 4, m->st), "memset");
+  m->sync();
+  API_END
+}
+
+int gem_sync(gem_model* m) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  m->sync();
+  API_END
+}
+
+int gem_forward(gem_model* m, uint32_t tok, uint32_t pos, float* h_out) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  if (tok >= (uint32_t)m->vocab) throw Error(GEM_E_RANGE, "token id >= vocab");
+  if (pos >= (uint32_t)m->ctx) throw Error(GEM_E_RANGE, "pos >= ctx");  // model.rs:287
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  *m->cur_host = StepCur{tok, pos, 0, 0};
+  ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+  m->enqueue_body(0);
+  m->check_launch();
+  if (h_out) ck(cudaMemcpyAsync(h_out, m->h, (size_t)m->d * 4, cudaMemcpyDeviceToHost, m->st), "h");
+  m->sync();
+  m->have_h = true;
+  API_END
+}
+
+static int single_head(gem_model* m, int which, uint32_t target, float* logprob, uint32_t* argmax) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  if (!m->have_h) throw Error(GEM_E_STATE, "no hidden state: call gem_forward first");
+  if (which == 1 && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  if (target >= (uint32_t)m->vocab) throw Error(GEM_E_RANGE, "target id >= vocab");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  StepCur c = *m->cur_host;
+  *m->cur_host = StepCur{c.tok, c.pos, target, 0};
+  ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+  m->enqueue_head(which, m->lp, m->am);
+  m->check_launch();
+  float lp;
+  uint32_t am;
+  ck(cudaMemcpyAsync(&lp, m->lp, 4, cudaMemcpyDeviceToHost, m->st), "lp");
+  ck(cudaMemcpyAsync(&am, m->am, 4, cudaMemcpyDeviceToHost, m->st), "am");
+  m->sync();
+  if (logprob) *logprob = lp;
+  if (argmax) *argmax = am;
+  API_END
+}
+
+int gem_full_logprob(gem_model* m, uint32_t target, float* logprob, uint32_t* argmax) {
+  return single_head(m, 0, target, logprob, argmax);
+}
+int gem_twolevel_logprob(gem_model* m, uint32_t target, float* logprob, uint32_t* argmax) {
+  return single_head(m, 1, target, logprob, argmax);
+}
+
+static void run_score(gem_model* m, size_t n, int head) {
+  if (head != 0 && head != 1) throw Error(GEM_E_ARG, "head must be 0 (full) or 1 (two-level)");
+  if (head == 1 && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  size_t off = m->bos >= 0 ? 1 : 0;
+  if (n + off > (size_t)m->ctx) throw Error(GEM_E_RANGE, "sequence longer than ctx");
+  if (m->bos >= 0) {  // main.rs:270-272
+    *m->cur_host = StepCur{(uint32_t)m->bos, 0, 0, 0};
+    ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+    m->enqueue_body(0);
+  }
+  ck(cudaMemsetAsync(m->step, 0, 4, m->st), "step");
+  if (!m->score_graph[head]) {
+    cudaGraph_t g;
+    ck(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "capture");
+    try {
+      launch_begin_step(m->toks, m->step, (uint32_t)off, m->cur, m->st);
+      m->enqueue_body(0);
+      m->enqueue_head(head, m->lp, m->am);
+      launch_end_step(m->step, m->st);
+    } catch (...) {
+      cudaStreamEndCapture(m->st, &g);
+      throw;
+    }
+    ck(cudaStreamEndCapture(m->st, &g), "end capture");
+    cudaGraphExec_t ge;
+    cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    ck(e, "graph instantiate");
+    m->score_graph[head] = ge;
+  }
+  for (size_t i = 0; i < n; ++i) ck(cudaGraphLaunch(m->score_graph[head], m->st), "graph launch");
+  m->have_h = true;
+}
+
+int gem_score(gem_model* m, const uint32_t* toks, size_t n, int head, float* logprob_out, uint32_t* argmax_out) {
+  API_BEGIN
+  if (!m || !toks || !logprob_out) throw Error(GEM_E_ARG, "null argument");
+  if (n == 0) return GEM_OK;
+  for (size_t i = 0; i <= n; ++i)
+    if (toks[i] >= (uint32_t)m->vocab) throw Error(GEM_E_RANGE, "token id >= vocab");
+  if (n + 1 > (size_t)m->ctx + 1) throw Error(GEM_E_RANGE, "sequence longer than ctx");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  ck(cudaMemcpyAsync(m->toks, toks, (n + 1) * 4, cudaMemcpyHostToDevice, m->st), "toks");
+  run_score(m, n, head);
+  ck(cudaMemcpyAsync(logprob_out, m->lp, n * 4, cudaMemcpyDeviceToHost, m->st), "lp");
+  if (argmax_out) ck(cudaMemcpyAsync(argmax_out, m->am, n * 4, cudaMemcpyDeviceToHost, m->st), "am");
+  m->sync();
+  API_END
+}
+
+int gem_score_dev(gem_model* m, const uint32_t* toks_dev, size_t n, int head, float* logprob_dev, uint32_t* argmax_dev) {
+  API_BEGIN
+  if (!m || !toks_dev || !logprob_dev) throw Error(GEM_E_ARG, "null argument");
+  if (n == 0) return GEM_OK;
+  if (n > (size_t)m->ctx) throw Error(GEM_E_RANGE, "sequence longer than ctx");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  ck(cudaMemcpyAsync(m->toks, toks_dev, (n + 1) * 4, cudaMemcpyDeviceToDevice, m->st), "toks");
+  run_score(m, n, head);
+  ck(cudaMemcpyAsync(logprob_dev, m->lp, n * 4, cudaMemcpyDeviceToDevice, m->st), "lp");
+  if (argmax_dev) ck(cudaMemcpyAsync(argmax_dev, m->am, n * 4, cudaMemcpyDeviceToDevice, m->st), "am");
+  API_END
+}
+
+int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float* y_dev) {
+  API_BEGIN
+  if (!m || !x_dev || !y_dev) throw Error(GEM_E_ARG, "null argument");
+  const DevMat* M = nullptr;
+  if (layer == -1) M = &m->head;
+  else if (layer >= 0 && layer < m->nl) {
+    const Layer& L = m->layers[layer];
+    const DevMat* all[7] = {&L.q_only, &L.k_only, &L.v_only, &L.o, &L.gate_only, &L.up_only, &L.down};
+    if (which < 0 || which > 6) throw Error(GEM_E_ARG, "which must be 0..6");
+    M = all[which];
+  } else {
+    throw Error(GEM_E_RANGE, "layer out of range");
+  }
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  int cols = M->v.cols;
+  int8_t* q = m->alloc<int8_t>(cols);
+  float* s = m->alloc<float>(cols / 32);
+  launch_quantize(x_dev, cols, q, s, m->st);
+  launch_gemv(M->v, q, s, x_dev, y_dev, m->sms, m->st);
+  m->check_launch();
+  m->sync();
+  m->owned.pop_back();
+  m->owned.pop_back();
+  cudaFree(q);
+  cudaFree(s);
+  API_END
+}
+
+static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_t* targets_dev, int batch, float* lp_dev,
+                      uint32_t* am_dev) {
+  API_BEGIN
+  if (!m || !h_dev || !targets_dev || batch <= 0) throw Error(GEM_E_ARG, "bad argument");
+  if (which == 1 && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->ensure_head_batch(batch);
+  int8_t* q = m->alloc<int8_t>((size_t)batch * m->d);
+  float* s = m->alloc<float>((size_t)batch * m->d / 32);
+  launch_quantize(h_dev, batch * m->d, q, s, m->st);
+  if (which == 0) launch_head_full(m->head_args(q, s, h_dev, targets_dev, lp_dev, am_dev), batch, m->sms, m->st);
+  else launch_head_twolevel(m->tl_args(q, s, h_dev, targets_dev, lp_dev, am_dev), batch, m->sms, m->st);
+  m->check_launch();
+  m->sync();
+  m->owned.pop_back();
+  m->owned.pop_back();
+  cudaFree(q);
+  cudaFree(s);
+  API_END
+}
+
+int gem_head_full_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch, float* lp_dev, uint32_t* am_dev) {
+  return batch_head(m, 0, h_dev, targets_dev, batch, lp_dev, am_dev);
+}
+int gem_head_twolevel_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch, float* lp_dev,
+                          uint32_t* am_dev) {
+  return batch_head(m, 1, h_dev, targets_dev, batch, lp_dev, am_dev);
+}
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+"""Python mirror of gem's model/head API over the C ABI of include/gem.h (libgem_b200.so).
+
+Names follow crates/gem: `Gemma` (model.rs: load / forward), the full head and the two-level head
+(main.rs: Full::run + logprob, TwoLevel::load + logprob) and the `bench`/`check` scoring loop. Every
+call runs the sm_100a kernels of the shared library; there is no CPU path. If the library is missing
+and cannot be built, importing a model raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parents[1]          # prefix-head_b200/
+LIB = PKG / "_build" / "libgem_b200.so"
+SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "common.cuh", "kernels.cuh", "host.cpp", "host.hpp", "runtime.cpp")]
+
+GEM_OK = 0
+STATUS = {-1: "GEM_E_ARG", -2: "GEM_E_IO", -3: "GEM_E_FORMAT", -4: "GEM_E_CUDA", -5: "GEM_E_NOMEM",
+          -6: "GEM_E_STATE", -7: "GEM_E_RANGE", -8: "GEM_E_NCCL", -9: "GEM_E_TIMEOUT"}
+
+
+class GemError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Info(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in ("d", "vocab", "layers", "n_heads", "n_kv_heads", "head_dim", "ffn", "ctx",
+                                         "window", "bos", "body_bits", "head_bits", "classes", "per", "max_seqs",
+                                         "body_bytes", "head_bytes", "device")]
+
+
+def build(force: bool = False) -> Path:
+    """Compiles the CUDA kernels (sm_100a) and the host runtime into prefix-head_b200/_build."""
+    if force or not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in SOURCES if s.exists()):
+        subprocess.run(["make", "-s", "-C", str(PKG)], check=True)
+    return LIB
+
+
+_lib = None
+_u32p = C.POINTER(C.c_uint32)
+_f32p = C.POINTER(C.c_float)
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB.exists():
+        build()
+    L = C.CDLL(str(LIB))
+    vp = C.c_void_p
+    L.gem_last_error.restype = C.c_char_p
+    L.gem_version.restype = C.c_int
+    L.gem_open.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]
+    L.gem_open_twolevel.argtypes = [vp, C.c_char_p]
+    L.gem_close.argtypes = [vp]
+    L.gem_close.restype = None
+    L.gem_get_info.argtypes = [vp, C.POINTER(Info)]
+    L.gem_reset.argtypes = [vp, C.c_int]
+    L.gem_sync.argtypes = [vp]
+    L.gem_forward.argtypes = [vp, C.c_uint32, C.c_uint32, _f32p]
+    L.gem_full_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
+    L.gem_twolevel_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
+    L.gem_score.argtypes = [vp, _u32p, C.c_size_t, C.c_int, _f32p, _u32p]
+    L.gem_score_dev.argtypes = [vp, vp, C.c_size_t, C.c_int, vp, vp]
+    L.gem_matvec_dev.argtypes = [vp, C.c_int, C.c_int, vp, vp]
+    L.gem_head_full_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
+    L.gem_head_twolevel_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != GEM_OK:
+        raise GemError(rc, lib().gem_last_error().decode())
+
+
+def _p(a: np.ndarray, t):
+    return a.ctypes.data_as(t)
+
+
+FULL, TWO_LEVEL = 0, 1
+
+
+class Gemma:
+    """Gemma::load + requantize + requantize_head (model.rs:154-279, main.rs:203-210) on one GPU."""
+
+    def __init__(self, gguf: str | os.PathLike, ctx: int = 2048, body_bits: int = 8, head_bits: int = 0,
+                 device: int = 0, max_seqs: int = 1):
+        L = lib()
+        h = C.c_void_p()
+        _check(L.gem_open(str(gguf).encode(), ctx, body_bits, head_bits, device, max_seqs, C.byref(h)))
+        self._h = h
+        info = Info()
+        _check(L.gem_get_info(self._h, C.byref(info)))
+        self.info = {n: int(getattr(info, n)) for n, _ in Info._fields_}
+        self.d, self.vocab, self.ctx, self.bos = (self.info[k] for k in ("d", "vocab", "ctx", "bos"))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().gem_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def handle(self):
+        return self._h
+
+    def load_twolevel(self, prefix: str | os.PathLike):
+        """TwoLevel::load (main.rs:57-76)."""
+        _check(lib().gem_open_twolevel(self._h, str(prefix).encode()))
+        info = Info()
+        _check(lib().gem_get_info(self._h, C.byref(info)))
+        self.info = {n: int(getattr(info, n)) for n, _ in Info._fields_}
+
+    def reset(self, seq: int = 0):
+        _check(lib().gem_reset(self._h, seq))
+
+    def forward(self, tok: int, pos: int) -> np.ndarray:
+        """Gemma::forward (model.rs:286-430); returns the final-norm hidden state."""
+        h = np.zeros(self.d, np.float32)
+        _check(lib().gem_forward(self._h, tok, pos, _p(h, _f32p)))
+        return h
+
+    def full_logprob(self, target: int):
+        """Full::run + Full::logprob (main.rs:30-37) on the last forward's hidden state."""
+        lp, am = C.c_float(), C.c_uint32()
+        _check(lib().gem_full_logprob(self._h, target, C.byref(lp), C.byref(am)))
+        return lp.value, am.value
+
+    def twolevel_logprob(self, target: int):
+        """TwoLevel::logprob (main.rs:101-107) on the last forward's hidden state."""
+        lp, am = C.c_float(), C.c_uint32()
+        _check(lib().gem_twolevel_logprob(self._h, target, C.byref(lp), C.byref(am)))
+        return lp.value, am.value
+
+    def score(self, toks: np.ndarray, head: int = TWO_LEVEL):
+        """The bench/check loop (main.rs:270-289): len(toks) - 1 scored tokens -> (logprob, argmax)."""
+        toks = np.ascontiguousarray(toks, np.uint32)
+        n = len(toks) - 1
+        lp = np.zeros(n, np.float32)
+        am = np.zeros(n, np.uint32)
+        _check(lib().gem_score(self._h, _p(toks, _u32p), n, head, _p(lp, _f32p), _p(am, _u32p)))
+        return lp, am
+
+    def score_dev(self, toks_ptr: int, n: int, head: int, lp_ptr: int, am_ptr: int | None):
+        """Same loop on device buffers (ints: device addresses); asynchronous on the model's stream."""
+        _check(lib().gem_score_dev(self._h, toks_ptr, n, head, lp_ptr, am_ptr))
+
+    def sync(self):
+        _check(lib().gem_sync(self._h))
+
+    def matvec_dev(self, layer: int, which: int, x_ptr: int, y_ptr: int):
+        _check(lib().gem_matvec_dev(self._h, layer, which, x_ptr, y_ptr))
+
+    def head_full_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
+        _check(lib().gem_head_full_dev(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
+
+    def head_twolevel_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
+        _check(lib().gem_head_twolevel_dev(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
