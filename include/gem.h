@@ -59,13 +59,23 @@ int gem_version(void);
  * keeps the file's type. max_seqs > 1 allocates independent KV caches for batched scoring. */
 int gem_open(const char* gguf_path, int ctx, int body_bits, int head_bits, int device, int max_seqs,
              gem_model** out);
-/* TwoLevel::load(&Gemma, prefix) (crates/gem/src/main.rs:57-76): reads prefix.order, prefix.A and
- * prefix.b, and lays the output matrix out class by class on the device (rows permuted as
- * Gemma::permute_head, model.rs:242-249), so a class is a contiguous block of rows. */
+/* TwoLevel::load(&Gemma, prefix) (crates/gem/src/main.rs:57-76): reads prefix.order (u32 token ids),
+ * prefix.A (f32 classes x d) and prefix.b (f32 classes), cuts the order into classes of
+ * ceil(vocab / classes) tokens and gathers each class's rows of the output matrix into one
+ * contiguous block on the device (main.rs:74). */
 int gem_open_twolevel(gem_model* m, const char* prefix);
 /* Drop (the reference frees on scope exit). */
 void gem_close(gem_model* m);
 int gem_get_info(const gem_model* m, gem_info* out);
+/* Numerics of every later call.
+ * GEM_NUMERICS_EXACT (the default, ref_threads 8): bit-identical hidden states and logits to the
+ *   reference's AVX-512 path (q8.rs dot_avx512 / dot4_avx512 / dot16_avx512, model.rs dot512 and
+ *   axpy512) run with a pool of ref_threads threads (gem bench --threads, main.rs:197); log-sum-exps
+ *   differ only in summation order.
+ * GEM_NUMERICS_FAST: tree reductions. The forward then differs from the reference by int8
+ *   quantization flips, within the spread between the reference's own AVX2 and AVX-512 paths. */
+enum { GEM_NUMERICS_EXACT = 0, GEM_NUMERICS_FAST = 1 };
+int gem_set_numerics(gem_model* m, int mode, int ref_threads);
 /* Clears a sequence's KV cache (the reference rebuilds its cache per run; bench reuses it). */
 int gem_reset(gem_model* m, int seq);
 int gem_sync(gem_model* m);

@@ -116,8 +116,4 @@ __device__ __forceinline__ int4 ldg_stream(const int4* p) {
   return v;
 }
 
-// Device error word: kernels that give up a bounded wait or find an impossible input record a code
-// here; the host reads and clears it after synchronising.
-enum : int { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_RANGE = 2 };
-
 }  // namespace gem

@@ -362,10 +362,17 @@ __global__ void k_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float
 }
 
 // Step bookkeeping for the scoring loop: token, position and target of step `step`.
-__global__ void k_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, StepCur* cur) {
+// Token ids come from caller memory: ids >= vocab are recorded in *err and replaced by 0.
+__global__ void k_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, uint32_t vocab, StepCur* cur, int* err) {
   uint32_t i = *step;
-  cur->tok = toks[i];
-  cur->target = toks[i + 1];
+  uint32_t t = toks[i], u = toks[i + 1];
+  if (t >= vocab || u >= vocab) {
+    atomicExch(err, ERR_RANGE);
+    t = t >= vocab ? 0 : t;
+    u = u >= vocab ? 0 : u;
+  }
+  cur->tok = t;
+  cur->target = u;
   cur->pos = base_pos + i;
   cur->slot = i;
 }
@@ -388,7 +395,11 @@ __global__ void k_head_full(HeadArgs H) {
   float* sx = (float*)smem_raw;
   stage_act(w.cols, H.aq + (size_t)bi * w.cols, H.as + (size_t)bi * (w.cols / 32), H.h + (size_t)bi * w.cols, saq, sas,
             sx, BITS == 16);
-  const uint32_t target = H.targets ? H.targets[bi] : H.cur->target;
+  uint32_t target = H.targets ? H.targets[bi] : H.cur->target;
+  if (target >= (uint32_t)w.rows) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(H.err, ERR_RANGE);
+    target = 0;
+  }
   const uint32_t trow = H.row_of ? H.row_of[target] : target;
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   Lse L{-INFINITY, 0.0f};
@@ -480,7 +491,8 @@ __global__ void k_tl_stage1(TwoLevelArgs T) {
   float* sas = (float*)(smem_raw + d);
   float* sx = (float*)smem_raw;
   stage_act(d, T.aq + (size_t)bi * d, T.as + (size_t)bi * (d / 32), h, saq, sas, sx, BITS == 16);
-  const uint32_t target = T.targets ? T.targets[bi] : T.cur->target;
+  uint32_t target = T.targets ? T.targets[bi] : T.cur->target;
+  if (target >= (uint32_t)T.vocab) target = 0;  // recorded by stage 2
   const uint32_t c = T.cls_of[target];
   const uint32_t first = c * T.per;
   const uint32_t n = min((uint32_t)T.per, (uint32_t)T.w.rows - first);
@@ -503,7 +515,11 @@ __global__ void k_tl_stage2(TwoLevelArgs T) {
   int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const float* cl = T.cl + (size_t)bi * T.k;
   const float* inner = T.inner + (size_t)bi * T.per;
-  const uint32_t target = T.targets ? T.targets[bi] : T.cur->target;
+  uint32_t target = T.targets ? T.targets[bi] : T.cur->target;
+  if (target >= (uint32_t)T.vocab) {
+    if (threadIdx.x == 0) atomicExch(T.err, ERR_RANGE);
+    target = 0;
+  }
   const uint32_t ct = T.cls_of[target];
   const uint32_t nt = min((uint32_t)T.per, (uint32_t)T.w.rows - ct * T.per);
   // class lse + first argmax
@@ -534,7 +550,7 @@ __global__ void k_tl_stage2(TwoLevelArgs T) {
       if (s_bv[i] > bv || (s_bv[i] == bv && redi[i] < bc)) { bv = s_bv[i]; bc = redi[i]; }
     }
     s_lse_cl = L.m + logf(L.s);
-    s_top = bc;
+    s_top = bc < (uint32_t)T.k ? bc : 0;  // only NaN logits leave no candidate
   }
   __syncthreads();
   // inner lse over the target block
@@ -579,6 +595,79 @@ __global__ void k_tl_stage2(TwoLevelArgs T) {
       if (sco[j] > sco[bj]) bj = j;
     uint32_t slot = T.targets ? (uint32_t)bi : T.cur->slot;
     T.am_out[slot] = T.order[first + bj];
+  }
+}
+
+// Two-level head, split form used by the exact path: select = class lse, most likely class (first
+// maximum), target logprob (main.rs:101-107); argmax = best raw logit inside the top class block
+// (lean.rs:46-76 with top = 1), whose logits another kernel wrote to top_inner.
+__global__ void k_tl_select(TwoLevelArgs T, uint32_t* top_of) {
+  __shared__ float rm[32], rs[32], rv[32];
+  __shared__ uint32_t rc[32];
+  __shared__ float s_lse_cl;
+  const int bi = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const float* cl = T.cl + (size_t)bi * T.k;
+  const float* inner = T.inner + (size_t)bi * T.per;
+  uint32_t target = T.targets ? T.targets[bi] : T.cur->target;
+  if (target >= (uint32_t)T.vocab) {
+    if (threadIdx.x == 0) atomicExch(T.err, ERR_RANGE);
+    target = 0;
+  }
+  const uint32_t ct = T.cls_of[target];
+  const uint32_t nt = min((uint32_t)T.per, (uint32_t)T.w.rows - ct * T.per);
+  Lse L{-INFINITY, 0.0f};
+  Best B{-INFINITY, 0xffffffffu};
+  for (int c = threadIdx.x; c < T.k; c += blockDim.x) {
+    L = lse_add(L, cl[c]);
+    B = best_merge(B, Best{cl[c], (uint32_t)c});
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    L = lse_merge(L, Lse{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)});
+    B = best_merge(B, Best{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)});
+  }
+  if (lane == 0) { rm[warp] = L.m; rs[warp] = L.s; rv[warp] = B.v; rc[warp] = B.tok; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i) {
+      L = lse_merge(L, Lse{rm[i], rs[i]});
+      B = best_merge(B, Best{rv[i], rc[i]});
+    }
+    s_lse_cl = L.m + logf(L.s);
+    top_of[bi] = B.tok < (uint32_t)T.k ? B.tok : 0;  // only NaN logits leave no candidate
+  }
+  __syncthreads();
+  Lse Li{-INFINITY, 0.0f};
+  for (uint32_t j = threadIdx.x; j < nt; j += blockDim.x) Li = lse_add(Li, inner[j]);
+  for (int o = 16; o > 0; o >>= 1)
+    Li = lse_merge(Li, Lse{__shfl_xor_sync(0xffffffffu, Li.m, o), __shfl_xor_sync(0xffffffffu, Li.s, o)});
+  if (lane == 0) { rm[warp] = Li.m; rs[warp] = Li.s; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i) Li = lse_merge(Li, Lse{rm[i], rs[i]});
+    uint32_t slot = T.targets ? (uint32_t)bi : T.cur->slot;
+    if (T.lp_out) T.lp_out[slot] = cl[ct] - s_lse_cl + inner[T.pos_of[target]] - (Li.m + logf(Li.s));
+  }
+}
+
+__global__ void k_tl_argmax(TwoLevelArgs T, const uint32_t* top_of, const float* top_inner) {
+  __shared__ float rv[32];
+  __shared__ uint32_t rj[32];
+  const int bi = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const uint32_t top = top_of[bi], first = top * T.per;
+  const uint32_t n = min((uint32_t)T.per, (uint32_t)T.w.rows - first);
+  const float* z = top_inner + (size_t)bi * T.per;
+  Best B{-INFINITY, 0xffffffffu};
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) B = best_merge(B, Best{z[j], j});
+  for (int o = 16; o > 0; o >>= 1)
+    B = best_merge(B, Best{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)});
+  if (lane == 0) { rv[warp] = B.v; rj[warp] = B.tok; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i) B = best_merge(B, Best{rv[i], rj[i]});
+    uint32_t slot = T.targets ? (uint32_t)bi : T.cur->slot;
+    if (T.am_out) T.am_out[slot] = T.order[first + (B.tok < n ? B.tok : 0)];
   }
 }
 
@@ -641,8 +730,9 @@ void launch_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float* as, 
   int blocks = (ff / 32 + 7) / 8;
   k_glu_quant<<<blocks, 256, 0, st>>>(gu, ff, silu, aq, as, gout);
 }
-void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, StepCur* cur, cudaStream_t st) {
-  k_begin_step<<<1, 1, 0, st>>>(toks, step, base_pos, cur);
+void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, uint32_t vocab, StepCur* cur, int* err,
+                       cudaStream_t st) {
+  k_begin_step<<<1, 1, 0, st>>>(toks, step, base_pos, vocab, cur, err);
 }
 void launch_end_step(uint32_t* step, cudaStream_t st) { k_end_step<<<1, 1, 0, st>>>(step); }
 
@@ -660,7 +750,18 @@ void launch_head_full(const HeadArgs& H, int batch, int sms, cudaStream_t st) {
   } while (0)
   GEM_DISPATCH(H.w.bits, H.w.scale_f32, F);
 #undef F
+  launch_head_full_merge(H, batch, parts, st);
+}
+
+void launch_head_full_merge(const HeadArgs& H, int batch, int parts, cudaStream_t st) {
   k_head_full_merge<<<batch, 256, 0, st>>>(H, parts);
+}
+
+void launch_tl_select(const TwoLevelArgs& T, int batch, uint32_t* top_of, cudaStream_t st) {
+  k_tl_select<<<batch, 256, 0, st>>>(T, top_of);
+}
+void launch_tl_argmax(const TwoLevelArgs& T, int batch, const uint32_t* top_of, const float* top_inner, cudaStream_t st) {
+  k_tl_argmax<<<batch, 256, 0, st>>>(T, top_of, top_inner);
 }
 
 void launch_head_twolevel(const TwoLevelArgs& T, int batch, int sms, cudaStream_t st) {

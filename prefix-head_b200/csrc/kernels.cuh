@@ -9,6 +9,10 @@
 
 namespace gem {
 
+// Device error word: kernels that give up a bounded wait or meet an out-of-range caller id record a
+// code here; the host reads and clears it after synchronising.
+enum : int { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_RANGE = 2 };
+
 // A weight matrix on the device (crates/gem/src/q8.rs:9-15, repacked): bits 8 = int8 plane
 // [rows][cols]; bits 4 = GGUF Q4_0 nibble bytes [rows][cols/2]; bits 16 = f16 [rows][cols]. Scales
 // (bits 8/4) are one per 32 weights, [rows][cols/32], f16 as stored in the GGUF or f32 after
@@ -54,6 +58,7 @@ struct HeadArgs {
   float* tlogit;             // [batch]
   float* lp_out;             // indexed by batch item, or cur->slot
   uint32_t* am_out;
+  int* err;                  // device error word
 };
 
 struct TwoLevelArgs {
@@ -72,7 +77,8 @@ struct TwoLevelArgs {
   float* inner;              // [batch][per]
   float* lp_out;
   uint32_t* am_out;
-  int k, per, class_ctas;
+  int* err;
+  int k, per, class_ctas, vocab;
 };
 
 void launch_embed(const MatView& head, const uint32_t* row_of, const StepCur* cur, float scale, float* x, cudaStream_t st);
@@ -83,10 +89,25 @@ void launch_quantize(const float* x, int n, int8_t* aq, float* as, cudaStream_t 
 void launch_gemv(const MatView& w, const int8_t* aq, const float* as, const float* x, float* y, int sms, cudaStream_t st);
 void launch_attn(const AttnArgs& A, int8_t* aq, float* as, cudaStream_t st);
 void launch_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float* as, float* gout, cudaStream_t st);
-void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, StepCur* cur, cudaStream_t st);
+void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, uint32_t vocab, StepCur* cur, int* err,
+                       cudaStream_t st);
 void launch_end_step(uint32_t* step, cudaStream_t st);
 int head_full_parts(int sms);
 void launch_head_full(const HeadArgs& H, int batch, int sms, cudaStream_t st);
 void launch_head_twolevel(const TwoLevelArgs& T, int batch, int sms, cudaStream_t st);
+void launch_head_full_merge(const HeadArgs& H, int batch, int parts, cudaStream_t st);
+void launch_tl_select(const TwoLevelArgs& T, int batch, uint32_t* top_of, cudaStream_t st);
+void launch_tl_argmax(const TwoLevelArgs& T, int batch, const uint32_t* top_of, const float* top_inner, cudaStream_t st);
+
+// Exact numerics (kernels_exact.cu): bit-identical to the reference's AVX-512 path.
+void launch_gemv_exact(const MatView& w, const int8_t* aq, const float* as, const float* x, float* y, int sms,
+                       cudaStream_t st);
+void launch_residual_norm_quant_exact(float* x, const float* delta, const float* w_post, const float* w_pre, float eps,
+                                      int d, int8_t* aq, float* as, float* xn_out, cudaStream_t st);
+void launch_attn_exact(const AttnArgs& A, float* qn, float* scores, int sstride, int threads, int8_t* aq, float* as,
+                       int sms, cudaStream_t st);
+void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t st);
+void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, int block_ctas, cudaStream_t st);
+void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_of, float* top_inner, cudaStream_t st);
 
 }  // namespace gem

@@ -1,0 +1,547 @@
+// Exact-numerics kernels: bit-identical to the reference's AVX-512 path (crates/gem/src/q8.rs,
+// model.rs with Isa::Avx512) for a given CPU thread-pool size.
+//
+// Int8 activation quantization makes the forward chaotic: a last-bit difference in any value that is
+// quantized later can flip an int8 code and grow to ~1e-2 nats per token, which is also how far the
+// reference's own AVX2 and AVX-512 paths disagree. So these kernels reproduce the reference's
+// summation orders exactly:
+//   - row dots (dot_avx512, dot4_avx512, dot16_avx512): 16 fp32 lanes, lane i holds
+//     w[2i]*a[2i] + w[2i+1]*a[2i+1] per 32-block, accumulated with one FMA per block, then reduced in
+//     _mm512_reduce_add_ps's halving order (i + 8, i + 4, i + 2, i + 1). Two threads hold a row's 16
+//     lanes, 8 each.
+//   - dot512 (attention scores, class logits): 16 lanes over 16-float chunks, same reduction.
+//   - rmsnorm / softmax sums: sequential fp32 additions (Rust's Iterator::sum), one thread.
+//   - P.V: the pool's per-thread position ranges, FMA per element (axpy512), partials summed in
+//     thread order.
+#include "kernels.cuh"
+
+namespace gem {
+
+// _mm512_reduce_add_ps over 16 lanes held as 8 + 8 by the two threads of a lane pair (lane ^ 1).
+__device__ __forceinline__ float reduce16_pair(const float (&a)[8]) {
+  float b[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) b[i] = add(a[i], __shfl_xor_sync(0xffffffffu, a[i], 1));  // a_i + a_(i+8)
+  float c0 = add(b[0], b[4]), c1 = add(b[1], b[5]), c2 = add(b[2], b[6]), c3 = add(b[3], b[7]);
+  return add(add(c0, c2), add(c1, c3));
+}
+
+// Low / high int16 pair of a packed word as one madd_epi16 lane: w0*a0 + w1*a1 (exact).
+__device__ __forceinline__ float madd_lo(int w, int a) { return (float)__dp4a(w & 0x0000ffff, a, 0); }
+__device__ __forceinline__ float madd_hi(int w, int a) { return (float)__dp4a(w & (int)0xffff0000, a, 0); }
+
+// One row's dot with the reference's lane structure. `half` selects lanes 8*half .. 8*half + 7.
+// Returns the reduced value in both threads of the pair.
+template <int BITS, typename ST>
+__device__ __forceinline__ float row_dot_exact(const MatView& w, size_t r, int half, const int8_t* saq, const float* sas,
+                                               const float* sx) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  const int nb = w.cols / 32;
+  if constexpr (BITS == 16) {  // dot16_avx512 (q8.rs:358-369): lane i sums w[16c+i]*x[16c+i]
+    const int4* row = (const int4*)((const __half*)w.q + r * w.cols);
+    for (int c = 0; c < w.cols / 16; ++c) {
+      int4 v = ldg_stream(row + 2 * c + half);
+      const __half2* h2 = (const __half2*)&v;
+      const float* xv = sx + c * 16 + half * 8;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 f = __half22float2(h2[k]);
+        acc[2 * k] = fmaf(f.x, xv[2 * k], acc[2 * k]);
+        acc[2 * k + 1] = fmaf(f.y, xv[2 * k + 1], acc[2 * k + 1]);
+      }
+    }
+  } else {
+    const ST* srow = (const ST*)w.s + r * nb;
+    for (int b = 0; b < nb; ++b) {
+      int4 wv;
+      if constexpr (BITS == 8) {  // dot_avx512 (q8.rs:257-270)
+        wv = ldg_stream((const int4*)((const int8_t*)w.q + r * w.cols) + 2 * b + half);
+      } else {  // dot4_avx512 (q8.rs:307-326): bytes 0..15 low nibbles, 16..31 high nibbles, minus 8
+        int4 raw = ldg_stream((const int4*)((const uint8_t*)w.q + r * (w.cols / 2)) + b);
+        const unsigned m = 0x0f0f0f0fu, e = 0x08080808u;
+        int sh = half * 4;
+        wv.x = (int)__vsub4(((unsigned)raw.x >> sh) & m, e);
+        wv.y = (int)__vsub4(((unsigned)raw.y >> sh) & m, e);
+        wv.z = (int)__vsub4(((unsigned)raw.z >> sh) & m, e);
+        wv.w = (int)__vsub4(((unsigned)raw.w >> sh) & m, e);
+      }
+      const int4 av = *(const int4*)(saq + b * 32 + half * 16);
+      const float s = mul(ld_scale(srow, b), sas[b]);
+      acc[0] = fmaf(madd_lo(wv.x, av.x), s, acc[0]);
+      acc[1] = fmaf(madd_hi(wv.x, av.x), s, acc[1]);
+      acc[2] = fmaf(madd_lo(wv.y, av.y), s, acc[2]);
+      acc[3] = fmaf(madd_hi(wv.y, av.y), s, acc[3]);
+      acc[4] = fmaf(madd_lo(wv.z, av.z), s, acc[4]);
+      acc[5] = fmaf(madd_hi(wv.z, av.z), s, acc[5]);
+      acc[6] = fmaf(madd_lo(wv.w, av.w), s, acc[6]);
+      acc[7] = fmaf(madd_hi(wv.w, av.w), s, acc[7]);
+    }
+  }
+  return reduce16_pair(acc);
+}
+
+// dot512 (model.rs:106-120) of two fp32 vectors of length n (a multiple of 16): lane i sums
+// a[16c+i]*b[16c+i] with FMA, then the halving reduction. Lane pair as above.
+__device__ __forceinline__ float dot512_pair(const float* a, const float* b, int n, int half) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int c = 0; c < n / 16; ++c) {
+    const float4 a0 = *(const float4*)(a + c * 16 + half * 8), a1 = *(const float4*)(a + c * 16 + half * 8 + 4);
+    const float4 b0 = *(const float4*)(b + c * 16 + half * 8), b1 = *(const float4*)(b + c * 16 + half * 8 + 4);
+    acc[0] = fmaf(a0.x, b0.x, acc[0]); acc[1] = fmaf(a0.y, b0.y, acc[1]);
+    acc[2] = fmaf(a0.z, b0.z, acc[2]); acc[3] = fmaf(a0.w, b0.w, acc[3]);
+    acc[4] = fmaf(a1.x, b1.x, acc[4]); acc[5] = fmaf(a1.y, b1.y, acc[5]);
+    acc[6] = fmaf(a1.z, b1.z, acc[6]); acc[7] = fmaf(a1.w, b1.w, acc[7]);
+  }
+  return reduce16_pair(acc);
+}
+
+// Rust `iter().map(|v| v * v).sum::<f32>()`: one thread, in order.
+__device__ __forceinline__ float seq_sumsq(const float* v, int n) {
+  float s = 0.0f;
+  for (int i = 0; i < n; i += 4) {
+    float4 t = *(const float4*)(v + i);
+    s = add(s, mul(t.x, t.x));
+    s = add(s, mul(t.y, t.y));
+    s = add(s, mul(t.z, t.z));
+    s = add(s, mul(t.w, t.w));
+  }
+  return s;
+}
+__device__ __forceinline__ float rms_r_exact(float ss, int n, float eps) {
+  return div(1.0f, __fsqrt_rn(add(div(ss, (float)n), eps)));
+}
+
+__device__ __forceinline__ void quant_block_warp_x(float v, int lane, int8_t* q, float* s) {
+  float amax = warp_max(fabsf(v));
+  float d = div(amax, 127.0f);
+  float inv = d > 0.0f ? div(1.0f, d) : 0.0f;
+  q[lane] = (int8_t)__float2int_rn(mul(v, inv));
+  if (lane == 0) *s = d;
+}
+
+// ------------------------------------------------------------------------------------------------
+// GEMV, exact: a warp covers 16 rows per step (lane pair per row).
+// ------------------------------------------------------------------------------------------------
+template <int BITS, typename ST>
+__global__ void k_gemv_exact(MatView w, const int8_t* aq, const float* as, const float* x, float* y) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int8_t* saq = (int8_t*)smem_raw;
+  float* sas = (float*)(smem_raw + w.cols);
+  float* sx = (float*)smem_raw;
+  if (BITS == 16) {
+    for (int j = threadIdx.x; j < w.cols; j += blockDim.x) sx[j] = x[j];
+  } else {
+    for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)aq)[j];
+    for (int j = threadIdx.x; j < w.cols / 32; j += blockDim.x) sas[j] = as[j];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int half = lane & 1;
+  for (int base = (blockIdx.x * nw + warp) * 16; base < w.rows; base += gridDim.x * nw * 16) {
+    int r = base + (lane >> 1);
+    bool ok = r < w.rows;
+    float v = row_dot_exact<BITS, ST>(w, ok ? r : w.rows - 1, half, saq, sas, sx);
+    if (ok && half == 0) y[r] = v;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Residual + norms + quantize with sequential sums (see k_residual_norm_quant).
+// ------------------------------------------------------------------------------------------------
+__global__ void k_residual_norm_quant_exact(float* x, const float* delta, const float* w_post, const float* w_pre,
+                                            float eps, int d, int8_t* aq, float* as, float* xn_out) {
+  extern __shared__ __align__(16) float smx[];
+  float* xs = smx;       // d
+  float* tv = smx + d;   // d
+  __shared__ float s_r;
+  int tid = threadIdx.x;
+  if (delta) {
+    for (int j = tid; j < d; j += blockDim.x) tv[j] = delta[j];
+    __syncthreads();
+    if (w_post) {
+      if (tid == 0) s_r = rms_r_exact(seq_sumsq(tv, d), d, eps);
+      __syncthreads();
+    }
+    float r = s_r;
+    for (int j = tid; j < d; j += blockDim.x) {
+      float t = tv[j];
+      if (w_post) t = mul(t, mul(r, w_post[j]));  // rmsnorm_inplace (model.rs:89-95): v *= r * w
+      xs[j] = add(x[j], t);
+    }
+  } else {
+    for (int j = tid; j < d; j += blockDim.x) xs[j] = x[j];
+  }
+  __syncthreads();
+  if (tid == 0) s_r = rms_r_exact(seq_sumsq(xs, d), d, eps);
+  __syncthreads();
+  float r = s_r;
+  if (delta)
+    for (int j = tid; j < d; j += blockDim.x) x[j] = xs[j];
+  for (int j = tid; j < d; j += blockDim.x) xs[j] = mul(mul(xs[j], r), w_pre[j]);  // rmsnorm (model.rs:81-87)
+  __syncthreads();
+  if (xn_out)
+    for (int j = tid; j < d; j += blockDim.x) xn_out[j] = xs[j];
+  if (aq) {
+    int lane = tid & 31;
+    for (int b = tid >> 5; b < d / 32; b += blockDim.x >> 5) quant_block_warp_x(xs[b * 32 + lane], lane, aq + b * 32, as + b);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Attention, exact (model.rs:316-383).
+// ------------------------------------------------------------------------------------------------
+// QK-norm, RoPE, q scale, KV append. One CTA per kv group; writes normalised q to qn.
+__global__ void k_attn_prep_exact(AttnArgs A, float* qn) {
+  extern __shared__ __align__(16) float smp[];
+  const int hd = A.hd, G = A.nh / A.nkv, g = blockIdx.x;
+  float* sq = smp;           // G*hd
+  float* sk = sq + G * hd;   // hd
+  float* sv = sk + hd;       // hd
+  __shared__ float s_r[9];
+  const uint32_t pos = A.cur->pos;
+  const int rw = A.nkv * hd;
+  const float* bq = A.bqkv;
+  for (int j = threadIdx.x; j < G * hd; j += blockDim.x) {
+    size_t i = (size_t)g * G * hd + j;
+    sq[j] = bq ? add(A.qkv[i], bq[i]) : A.qkv[i];
+  }
+  for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+    size_t ik = (size_t)A.nh * hd + g * hd + j, iv = (size_t)A.nh * hd + rw + g * hd + j;
+    sk[j] = bq ? add(A.qkv[ik], bq[ik]) : A.qkv[ik];
+    sv[j] = bq ? add(A.qkv[iv], bq[iv]) : A.qkv[iv];
+  }
+  __syncthreads();
+  // per-head sequential sums of squares, one thread per head (+1 for k)
+  if ((int)threadIdx.x <= G) {
+    const float* v = threadIdx.x < (unsigned)G ? sq + threadIdx.x * hd : sk;
+    const float* nw = threadIdx.x < (unsigned)G ? A.q_norm : A.k_norm;
+    s_r[threadIdx.x] = nw ? rms_r_exact(seq_sumsq(v, hd), hd, A.eps) : 1.0f;
+  }
+  __syncthreads();
+  const float* sn = A.rope_sin + (size_t)pos * (hd / 2);
+  const float* cs = A.rope_cos + (size_t)pos * (hd / 2);
+  const int half = hd / 2;
+  for (int t = threadIdx.x; t < (G + 1) * half; t += blockDim.x) {
+    int h = t / half, i = t % half;
+    float* v = h < G ? sq + h * hd : sk;
+    const float* nw = h < G ? A.q_norm : A.k_norm;
+    float r = s_r[h];
+    float a = v[i], b = v[i + half];
+    if (nw) {  // rmsnorm_inplace: v *= r * w
+      a = mul(a, mul(r, nw[i]));
+      b = mul(b, mul(r, nw[i + half]));
+    }
+    float na = sub(mul(a, cs[i]), mul(b, sn[i]));  // rope (model.rs:97-104)
+    float nb = add(mul(a, sn[i]), mul(b, cs[i]));
+    if (h < G) {  // q * 1/sqrt(hd) (model.rs:317-324)
+      na = mul(na, A.qscale);
+      nb = mul(nb, A.qscale);
+      qn[(size_t)(g * G + h) * hd + i] = na;
+      qn[(size_t)(g * G + h) * hd + i + half] = nb;
+    } else {
+      A.kcache[(size_t)pos * rw + g * hd + i] = na;  // KV append (model.rs:333-335)
+      A.kcache[(size_t)pos * rw + g * hd + i + half] = nb;
+    }
+  }
+  for (int j = threadIdx.x; j < hd; j += blockDim.x) A.vcache[(size_t)pos * rw + g * hd + j] = sv[j];
+}
+
+// scores[h][i] = dot512(q_h, k_(lo+i)) for every head and position (model.rs:344-353).
+__global__ void k_attn_scores_exact(AttnArgs A, const float* qn, float* scores, int sstride) {
+  const int hd = A.hd, G = A.nh / A.nkv;
+  const uint32_t pos = A.cur->pos;
+  const uint32_t lo = (A.window > 0 && pos + 1 > (uint32_t)A.window) ? pos + 1 - A.window : 0;
+  const uint32_t n_pos = pos + 1 - lo;
+  const int rw = A.nkv * hd;
+  const int lane = threadIdx.x & 31, half = lane & 1;
+  const int pairs = (blockDim.x * gridDim.x) / 2;
+  const uint32_t total = n_pos * A.nh;
+  for (uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) / 2; t < ((total + 15) / 16) * 16; t += pairs) {
+    bool ok = t < total;
+    uint32_t tt = ok ? t : 0;
+    uint32_t i = tt / A.nh, h = tt % A.nh;
+    const float* k = A.kcache + (size_t)(lo + i) * rw + (h / G) * hd;
+    float s = dot512_pair(qn + (size_t)h * hd, k, hd, half);
+    if (ok && half == 0) scores[(size_t)h * sstride + i] = s;
+  }
+}
+
+// Softmax per head with the reference's order (model.rs:354-361): max, subtract, exp_fast,
+// sequential sum, multiply by 1/sum. One CTA per head.
+__global__ void k_attn_softmax_exact(AttnArgs A, float* scores, int sstride) {
+  __shared__ float red[32];
+  __shared__ float s_inv;
+  const uint32_t pos = A.cur->pos;
+  const uint32_t lo = (A.window > 0 && pos + 1 > (uint32_t)A.window) ? pos + 1 - A.window : 0;
+  const int n_pos = (int)(pos + 1 - lo);
+  float* s = scores + (size_t)blockIdx.x * sstride;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n_pos; i += blockDim.x) m = fmaxf(m, s[i]);
+  m = block_max(m, red);
+  for (int i = threadIdx.x; i < n_pos; i += blockDim.x) s[i] = exp_fast(sub(s[i], m));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sum = 0.0f;
+    for (int i = 0; i < n_pos; ++i) sum = add(sum, s[i]);
+    s_inv = div(1.0f, sum);
+  }
+  __syncthreads();
+  float inv = s_inv;
+  for (int i = threadIdx.x; i < n_pos; i += blockDim.x) s[i] = mul(s[i], inv);
+}
+
+// P.V with the pool's partition (model.rs:362-382): positions split into `threads` ranges of
+// per = ceil(n_pos / threads); each range accumulates acc = fma(p, v, acc) in order; att = partials
+// summed in thread order. Then Act::quantize of the head's blocks. Grid (nh, hd / 32), block 32 * T.
+__global__ void k_attn_pv_exact(AttnArgs A, const float* scores, int sstride, int threads, int8_t* aq, float* as) {
+  extern __shared__ float part[];  // [threads][32]
+  const int hd = A.hd, G = A.nh / A.nkv, h = blockIdx.x, j0 = blockIdx.y * 32;
+  const uint32_t pos = A.cur->pos;
+  const uint32_t lo = (A.window > 0 && pos + 1 > (uint32_t)A.window) ? pos + 1 - A.window : 0;
+  const int n_pos = (int)(pos + 1 - lo);
+  const int per = (n_pos + threads - 1) / threads;
+  const int rw = A.nkv * hd;
+  const int lane = threadIdx.x & 31, t = threadIdx.x >> 5;
+  const float* p = scores + (size_t)h * sstride;
+  const float* vc = A.vcache + (h / G) * hd + j0 + lane;
+  for (int tt = t; tt < threads; tt += blockDim.x >> 5) {
+    float acc = 0.0f;
+    int i0 = min(tt * per, n_pos), i1 = min((tt + 1) * per, n_pos);
+    for (int i = i0; i < i1; ++i) acc = fmaf(p[i], vc[(size_t)(lo + i) * rw], acc);
+    part[tt * 32 + lane] = acc;
+  }
+  __syncthreads();
+  if (t == 0) {
+    float a = 0.0f;
+    for (int tt = 0; tt < threads; ++tt) a = add(a, part[tt * 32 + lane]);
+    if (A.att_out) A.att_out[h * hd + j0 + lane] = a;
+    quant_block_warp_x(a, lane, aq + h * hd + j0, as + (h * hd + j0) / 32);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Heads, exact logits.
+// ------------------------------------------------------------------------------------------------
+template <int BITS, typename ST>
+__global__ void k_head_full_exact(HeadArgs H) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ float red_m[32], red_s[32], red_v[32];
+  __shared__ uint32_t red_t[32];
+  const int bi = blockIdx.y;
+  const MatView& w = H.w;
+  int8_t* saq = (int8_t*)smem_raw;
+  float* sas = (float*)(smem_raw + w.cols);
+  float* sx = (float*)smem_raw;
+  if (BITS == 16) {
+    for (int j = threadIdx.x; j < w.cols; j += blockDim.x) sx[j] = H.h[(size_t)bi * w.cols + j];
+  } else {
+    for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)(H.aq + (size_t)bi * w.cols))[j];
+    for (int j = threadIdx.x; j < w.cols / 32; j += blockDim.x) sas[j] = H.as[(size_t)bi * (w.cols / 32) + j];
+  }
+  __syncthreads();
+  uint32_t target = H.targets ? H.targets[bi] : H.cur->target;
+  if (target >= (uint32_t)w.rows) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(H.err, ERR_RANGE);
+    target = 0;
+  }
+  const uint32_t trow = H.row_of ? H.row_of[target] : target;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, half = lane & 1;
+  Lse L{-INFINITY, 0.0f};
+  Best B{-INFINITY, 0xffffffffu};
+  for (int base = (blockIdx.x * nw + warp) * 16; base < w.rows; base += gridDim.x * nw * 16) {
+    int r = base + (lane >> 1);
+    bool ok = r < w.rows;
+    float z = row_dot_exact<BITS, ST>(w, ok ? r : w.rows - 1, half, saq, sas, sx);
+    if (ok && half == 0) {
+      uint32_t tok = H.row_tok ? H.row_tok[r] : (uint32_t)r;
+      L = lse_add(L, z);
+      B = best_merge(B, Best{z, tok});
+      if ((uint32_t)r == trow) H.tlogit[bi] = z;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
+    Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
+    L = lse_merge(L, l2);
+    B = best_merge(B, b2);
+  }
+  if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i) {
+      L = lse_merge(L, Lse{red_m[i], red_s[i]});
+      B = best_merge(B, Best{red_v[i], red_t[i]});
+    }
+    float4* p = (float4*)(H.part + ((size_t)bi * gridDim.x + blockIdx.x) * 4);
+    *p = make_float4(L.m, L.s, B.v, __uint_as_float(B.tok));
+  }
+}
+
+// Two-level stage 1, exact: class logits dot512(A[c], h) + b[c] (main.rs:82-93) and the target
+// class's block rows.
+template <int BITS, typename ST>
+__global__ void k_tl_stage1_exact(TwoLevelArgs T) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int bi = blockIdx.y;
+  const int d = T.w.cols;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, half = lane & 1;
+  const float* h = T.h + (size_t)bi * d;
+  if ((int)blockIdx.x < T.class_ctas) {
+    float* sh = (float*)smem_raw;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) sh[j] = h[j];
+    __syncthreads();
+    for (int base = (blockIdx.x * nw + warp) * 16; base < T.k; base += T.class_ctas * nw * 16) {
+      int c = base + (lane >> 1);
+      bool ok = c < T.k;
+      float z = dot512_pair(T.A + (size_t)(ok ? c : 0) * d, sh, d, half);
+      if (ok && half == 0) T.cl[(size_t)bi * T.k + c] = add(z, T.b[c]);
+    }
+    return;
+  }
+  int8_t* saq = (int8_t*)smem_raw;
+  float* sas = (float*)(smem_raw + d);
+  float* sx = (float*)smem_raw;
+  if (BITS == 16) {
+    for (int j = threadIdx.x; j < d; j += blockDim.x) sx[j] = h[j];
+  } else {
+    for (int j = threadIdx.x; j < d / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)(T.aq + (size_t)bi * d))[j];
+    for (int j = threadIdx.x; j < d / 32; j += blockDim.x) sas[j] = T.as[(size_t)bi * (d / 32) + j];
+  }
+  __syncthreads();
+  uint32_t target = T.targets ? T.targets[bi] : T.cur->target;
+  if (target >= (uint32_t)T.vocab) target = 0;
+  const uint32_t c = T.cls_of[target];
+  const uint32_t first = c * T.per;
+  const int n = (int)min((uint32_t)T.per, (uint32_t)T.w.rows - first);
+  const int bctas = gridDim.x - T.class_ctas;
+  for (int base = ((blockIdx.x - T.class_ctas) * nw + warp) * 16; base < n; base += bctas * nw * 16) {
+    int j = base + (lane >> 1);
+    bool ok = j < n;
+    float z = row_dot_exact<BITS, ST>(T.w, first + (ok ? j : 0), half, saq, sas, sx);
+    if (ok && half == 0) T.inner[(size_t)bi * T.per + j] = z;
+  }
+}
+
+// Stage 2 reuses the fast kernel's logic but recomputes the top class block with exact rows.
+template <int BITS, typename ST>
+__global__ void k_tl_top_exact(TwoLevelArgs T, const uint32_t* top_of, float* top_inner) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int bi = blockIdx.y;
+  const int d = T.w.cols;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5, half = lane & 1;
+  int8_t* saq = (int8_t*)smem_raw;
+  float* sas = (float*)(smem_raw + d);
+  float* sx = (float*)smem_raw;
+  if (BITS == 16) {
+    for (int j = threadIdx.x; j < d; j += blockDim.x) sx[j] = T.h[(size_t)bi * d + j];
+  } else {
+    for (int j = threadIdx.x; j < d / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)(T.aq + (size_t)bi * d))[j];
+    for (int j = threadIdx.x; j < d / 32; j += blockDim.x) sas[j] = T.as[(size_t)bi * (d / 32) + j];
+  }
+  __syncthreads();
+  const uint32_t c = top_of[bi];
+  const uint32_t first = c * T.per;
+  const int n = (int)min((uint32_t)T.per, (uint32_t)T.w.rows - first);
+  for (int base = (blockIdx.x * nw + warp) * 16; base < n; base += gridDim.x * nw * 16) {
+    int j = base + (lane >> 1);
+    bool ok = j < n;
+    float z = row_dot_exact<BITS, ST>(T.w, first + (ok ? j : 0), half, saq, sas, sx);
+    if (ok && half == 0) top_inner[(size_t)bi * T.per + j] = z;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+#define GEM_DISPATCH_X(bits, scale_f32, F)                    \
+  do {                                                        \
+    if ((bits) == 8 && !(scale_f32)) { F(8, __half); }        \
+    else if ((bits) == 8) { F(8, float); }                    \
+    else if ((bits) == 4 && !(scale_f32)) { F(4, __half); }   \
+    else if ((bits) == 4) { F(4, float); }                    \
+    else { F(16, __half); }                                   \
+  } while (0)
+
+static size_t act_smem_x(int cols, int bits) {
+  return bits == 16 ? (size_t)cols * 4 : (size_t)cols + (size_t)cols / 32 * 4;
+}
+
+void launch_gemv_exact(const MatView& w, const int8_t* aq, const float* as, const float* x, float* y, int sms,
+                       cudaStream_t st) {
+  const int threads = 256, nw = threads / 32;
+  int blocks = (w.rows + nw * 16 - 1) / (nw * 16);
+  blocks = min(blocks, sms * 8);
+  size_t sm = act_smem_x(w.cols, w.bits);
+#define F(B, S)                                                                                     \
+  do {                                                                                              \
+    static bool init = false;                                                                       \
+    if (!init) { cudaFuncSetAttribute(k_gemv_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
+    k_gemv_exact<B, S><<<blocks, threads, sm, st>>>(w, aq, as, x, y);                               \
+  } while (0)
+  GEM_DISPATCH_X(w.bits, w.scale_f32, F);
+#undef F
+}
+
+void launch_residual_norm_quant_exact(float* x, const float* delta, const float* w_post, const float* w_pre, float eps,
+                                      int d, int8_t* aq, float* as, float* xn_out, cudaStream_t st) {
+  k_residual_norm_quant_exact<<<1, 1024, (size_t)2 * d * 4, st>>>(x, delta, w_post, w_pre, eps, d, aq, as, xn_out);
+}
+
+void launch_attn_exact(const AttnArgs& A, float* qn, float* scores, int sstride, int threads, int8_t* aq, float* as,
+                       int sms, cudaStream_t st) {
+  int G = A.nh / A.nkv;
+  k_attn_prep_exact<<<A.nkv, 256, (size_t)(G * A.hd + 2 * A.hd) * 4, st>>>(A, qn);
+  int max_npos = A.window > 0 ? A.window : A.chunk * A.nsplit;
+  int pairs = max_npos * A.nh;
+  int blocks = min(sms * 4, max(1, (pairs * 2 + 255) / 256));
+  k_attn_scores_exact<<<blocks, 256, 0, st>>>(A, qn, scores, sstride);
+  k_attn_softmax_exact<<<A.nh, 256, 0, st>>>(A, scores, sstride);
+  int tb = min(threads, 32) * 32;
+  k_attn_pv_exact<<<dim3(A.nh, A.hd / 32), tb, (size_t)threads * 32 * 4, st>>>(A, scores, sstride, threads, aq, as);
+}
+
+void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t st) {
+  int parts = head_full_parts(sms);
+  dim3 grid(parts, batch);
+  size_t sm = act_smem_x(H.w.cols, H.w.bits);
+#define F(B, S)                                                                                     \
+  do {                                                                                              \
+    static bool init = false;                                                                       \
+    if (!init) { cudaFuncSetAttribute(k_head_full_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
+    k_head_full_exact<B, S><<<grid, 512, sm, st>>>(H);                                              \
+  } while (0)
+  GEM_DISPATCH_X(H.w.bits, H.w.scale_f32, F);
+#undef F
+  launch_head_full_merge(H, batch, parts, st);
+}
+
+void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, int block_ctas, cudaStream_t st) {
+  dim3 grid(class_ctas + block_ctas, batch);
+  size_t sm = max(act_smem_x(T.w.cols, T.w.bits), (size_t)T.w.cols * 4);
+#define F(B, S)                                                                                     \
+  do {                                                                                              \
+    static bool init = false;                                                                       \
+    if (!init) { cudaFuncSetAttribute(k_tl_stage1_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
+    k_tl_stage1_exact<B, S><<<grid, 256, sm, st>>>(T);                                              \
+  } while (0)
+  GEM_DISPATCH_X(T.w.bits, T.w.scale_f32, F);
+#undef F
+}
+
+void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_of, float* top_inner, cudaStream_t st) {
+  int ctas = max(1, min(8, (T.per + 63) / 64));
+  dim3 grid(ctas, batch);
+  size_t sm = act_smem_x(T.w.cols, T.w.bits);
+#define F(B, S)                                                                                     \
+  do {                                                                                              \
+    static bool init = false;                                                                       \
+    if (!init) { cudaFuncSetAttribute(k_tl_top_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
+    k_tl_top_exact<B, S><<<grid, 128, sm, st>>>(T, top_of, top_inner);                              \
+  } while (0)
+  GEM_DISPATCH_X(T.w.bits, T.w.scale_f32, F);
+#undef F
+}
+
+}  // namespace gem

@@ -95,6 +95,7 @@ struct gem_model {
   float *as_d, *as_att, *as_ff, *has;
   // step state and outputs
   StepCur* cur = nullptr;
+  int* err = nullptr;  // device error word (kernels record out-of-range caller ids here)
   StepCur* cur_host = nullptr;  // pinned
   uint32_t *step = nullptr, *toks = nullptr, *am = nullptr;
   float* lp = nullptr;
@@ -107,8 +108,20 @@ struct gem_model {
   DevMat blocks;
   float *A = nullptr, *b = nullptr;
   uint32_t *cls_of = nullptr, *pos_of = nullptr, *order = nullptr;
+  // numerics: exact = bit-identical to the reference's AVX-512 path with a pool of ref_threads
+  bool exact = true;
+  int ref_threads = 8;
+  float *qn = nullptr, *scores = nullptr, *top_inner = nullptr;
+  uint32_t* top_of = nullptr;
   // graphs
   cudaGraphExec_t score_graph[2] = {nullptr, nullptr};
+  void drop_graphs() {
+    for (auto& g : score_graph)
+      if (g) {
+        cudaGraphExecDestroy(g);
+        g = nullptr;
+      }
+  }
   bool have_h = false;
 
   ~gem_model() {
@@ -142,6 +155,8 @@ struct gem_model {
     if (two) {
       cl = alloc<float>((size_t)batch * k);
       inner = alloc<float>((size_t)batch * per);
+      top_inner = alloc<float>((size_t)batch * per);
+      top_of = alloc<uint32_t>(batch);
     }
     hbatch = batch;
   }
@@ -176,20 +191,23 @@ struct gem_model {
   void enqueue_body(int seq) {
     const DevMat& E = untied ? emb : head;
     launch_embed(E.v, nullptr, cur, embed_scale, x, st);
+    auto norm = exact ? launch_residual_norm_quant_exact : launch_residual_norm_quant;
+    auto gemv = exact ? launch_gemv_exact : launch_gemv;
     for (int l = 0; l < nl; ++l) {
       const Layer& L = layers[l];
       const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
-      launch_residual_norm_quant(x, P ? dn : nullptr, P ? P->post_ffw : nullptr, L.attn_norm, eps, d, aq_d, as_d, xn, st);
-      launch_gemv(L.qkv.v, aq_d, as_d, xn, qkv, sms, st);
+      norm(x, P ? dn : nullptr, P ? P->post_ffw : nullptr, L.attn_norm, eps, d, aq_d, as_d, xn, st);
+      gemv(L.qkv.v, aq_d, as_d, xn, qkv, sms, st);
       AttnArgs A = attn_args(l, seq);
-      launch_attn(A, aq_att, as_att, st);
-      launch_gemv(L.o.v, aq_att, as_att, att, o, sms, st);
-      launch_residual_norm_quant(x, o, L.post_attn, L.ffn_norm, eps, d, aq_d, as_d, xn, st);
-      launch_gemv(L.gu.v, aq_d, as_d, xn, gu, sms, st);
+      if (exact) launch_attn_exact(A, qn, scores, ctx, ref_threads, aq_att, as_att, sms, st);
+      else launch_attn(A, aq_att, as_att, st);
+      gemv(L.o.v, aq_att, as_att, att, o, sms, st);
+      norm(x, o, L.post_attn, L.ffn_norm, eps, d, aq_d, as_d, xn, st);
+      gemv(L.gu.v, aq_d, as_d, xn, gu, sms, st);
       launch_glu_quant(gu, ff, silu ? 1 : 0, aq_ff, as_ff, g, st);
-      launch_gemv(L.down.v, aq_ff, as_ff, g, dn, sms, st);
+      gemv(L.down.v, aq_ff, as_ff, g, dn, sms, st);
     }
-    launch_residual_norm_quant(x, dn, layers[nl - 1].post_ffw, out_norm, eps, d, haq, has, h, st);
+    norm(x, dn, layers[nl - 1].post_ffw, out_norm, eps, d, haq, has, h, st);
   }
 
   HeadArgs head_args(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, float* lpo, uint32_t* amo) {
@@ -202,6 +220,7 @@ struct gem_model {
     H.tlogit = tlogit;
     H.lp_out = lpo;
     H.am_out = amo;
+    H.err = err;
     return H;
   }
   TwoLevelArgs tl_args(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, float* lpo, uint32_t* amo) {
@@ -213,17 +232,45 @@ struct gem_model {
     T.cur = cur;
     T.cl = cl, T.inner = inner;
     T.lp_out = lpo, T.am_out = amo;
-    T.k = k, T.per = per;
+    T.k = k, T.per = per, T.vocab = vocab;
+    T.err = err;
     return T;
   }
-  void enqueue_head(int which, float* lpo, uint32_t* amo) {
-    ensure_head_batch(1);
-    if (which == 0) launch_head_full(head_args(haq, has, h, nullptr, lpo, amo), 1, sms, st);
-    else launch_head_twolevel(tl_args(haq, has, h, nullptr, lpo, amo), 1, sms, st);
+  void run_head(int which, const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, int batch,
+                float* lpo, uint32_t* amo) {
+    ensure_head_batch(batch);
+    if (which == 0) {
+      HeadArgs H = head_args(qa, sa, hh, targets, lpo, amo);
+      if (exact) launch_head_full_exact(H, batch, sms, st);
+      else launch_head_full(H, batch, sms, st);
+      return;
+    }
+    TwoLevelArgs T = tl_args(qa, sa, hh, targets, lpo, amo);
+    if (!exact) {
+      launch_head_twolevel(T, batch, sms, st);
+      return;
+    }
+    int class_ctas = std::max(1, std::min(sms, (k + 127) / 128));
+    int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
+    T.class_ctas = class_ctas;
+    launch_tl_stage1_exact(T, batch, class_ctas, block_ctas, st);
+    launch_tl_select(T, batch, top_of, st);
+    launch_tl_top_exact(T, batch, top_of, top_inner, st);
+    launch_tl_argmax(T, batch, top_of, top_inner, st);
   }
+  void enqueue_head(int which, float* lpo, uint32_t* amo) { run_head(which, haq, has, h, nullptr, 1, lpo, amo); }
 
   void check_launch() { ck(cudaGetLastError(), "kernel launch"); }
-  void sync() { ck(cudaStreamSynchronize(st), "stream sync"); }
+  void sync() {
+    ck(cudaStreamSynchronize(st), "stream sync");
+    int e = 0;
+    ck(cudaMemcpy(&e, err, sizeof(int), cudaMemcpyDeviceToHost), "error word");
+    if (e != 0) {
+      ck(cudaMemset(err, 0, sizeof(int)), "error word");
+      if (e == ERR_RANGE) throw Error(GEM_E_RANGE, "a token or target id in device memory was >= vocab (replaced by 0)");
+      throw Error(GEM_E_TIMEOUT, "a device-side wait gave up");
+    }
+  }
 };
 
 namespace {
@@ -393,7 +440,11 @@ void load_model(gem_model* m, const Gguf& g, int body_bits, int head_bits) {
   m->as_att = m->alloc<float>(wide / 32);
   m->as_ff = m->alloc<float>(wide / 32);
   m->has = m->alloc<float>(m->d / 32);
+  m->qn = m->alloc<float>((size_t)m->nh * m->hd);
+  m->scores = m->alloc<float>((size_t)m->nh * m->ctx);
   m->cur = m->alloc<StepCur>(1);
+  m->err = m->alloc<int>(1);
+  ck(cudaMemset(m->err, 0, sizeof(int)), "memset");
   ck(cudaMallocHost(&m->cur_host, sizeof(StepCur)), "cudaMallocHost");
   m->step = m->alloc<uint32_t>(1);
   m->toks = m->alloc<uint32_t>((size_t)m->ctx + 1);
@@ -488,10 +539,7 @@ int gem_open_twolevel(gem_model* m, const char* prefix) {
   m->two = true;
   m->hbatch = 0;
   m->ensure_head_batch(1);
-  if (m->score_graph[1]) {
-    cudaGraphExecDestroy(m->score_graph[1]);
-    m->score_graph[1] = nullptr;
-  }
+  m->drop_graphs();
   ck(cudaDeviceSynchronize(), "twolevel load");
   API_END
 }
@@ -521,6 +569,19 @@ int gem_reset(gem_model* m, int seq) {
   ck(cudaMemsetAsync(m->kc + (size_t)seq * per_seq, 0, per_seq * 4, m->st), "memset");
   ck(cudaMemsetAsync(m->vc + (size_t)seq * per_seq, 0, per_seq * 4, m->st), "memset");
   m->sync();
+  API_END
+}
+
+int gem_set_numerics(gem_model* m, int mode, int ref_threads) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  if (mode != GEM_NUMERICS_EXACT && mode != GEM_NUMERICS_FAST) throw Error(GEM_E_ARG, "unknown numerics mode");
+  if (ref_threads < 1 || ref_threads > 1024) throw Error(GEM_E_ARG, "ref_threads must be in 1..1024");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  m->exact = mode == GEM_NUMERICS_EXACT;
+  m->ref_threads = ref_threads;
+  m->drop_graphs();
   API_END
 }
 
@@ -593,7 +654,7 @@ static void run_score(gem_model* m, size_t n, int head) {
     cudaGraph_t g;
     ck(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal), "capture");
     try {
-      launch_begin_step(m->toks, m->step, (uint32_t)off, m->cur, m->st);
+      launch_begin_step(m->toks, m->step, (uint32_t)off, (uint32_t)m->vocab, m->cur, m->err, m->st);
       m->enqueue_body(0);
       m->enqueue_head(head, m->lp, m->am);
       launch_end_step(m->step, m->st);
@@ -659,7 +720,7 @@ int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float
   int8_t* q = m->alloc<int8_t>(cols);
   float* s = m->alloc<float>(cols / 32);
   launch_quantize(x_dev, cols, q, s, m->st);
-  launch_gemv(M->v, q, s, x_dev, y_dev, m->sms, m->st);
+  (m->exact ? launch_gemv_exact : launch_gemv)(M->v, q, s, x_dev, y_dev, m->sms, m->st);
   m->check_launch();
   m->sync();
   m->owned.pop_back();
@@ -679,8 +740,7 @@ static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_
   int8_t* q = m->alloc<int8_t>((size_t)batch * m->d);
   float* s = m->alloc<float>((size_t)batch * m->d / 32);
   launch_quantize(h_dev, batch * m->d, q, s, m->st);
-  if (which == 0) launch_head_full(m->head_args(q, s, h_dev, targets_dev, lp_dev, am_dev), batch, m->sms, m->st);
-  else launch_head_twolevel(m->tl_args(q, s, h_dev, targets_dev, lp_dev, am_dev), batch, m->sms, m->st);
+  m->run_head(which, q, s, h_dev, targets_dev, batch, lp_dev, am_dev);
   m->check_launch();
   m->sync();
   m->owned.pop_back();

@@ -16,7 +16,8 @@ import numpy as np
 
 PKG = Path(__file__).resolve().parents[1]          # prefix-head_b200/
 LIB = PKG / "_build" / "libgem_b200.so"
-SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "common.cuh", "kernels.cuh", "host.cpp", "host.hpp", "runtime.cpp")]
+SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "common.cuh", "kernels.cuh", "host.cpp",
+                                      "host.hpp", "runtime.cpp")]
 
 GEM_OK = 0
 STATUS = {-1: "GEM_E_ARG", -2: "GEM_E_IO", -3: "GEM_E_FORMAT", -4: "GEM_E_CUDA", -5: "GEM_E_NOMEM",
@@ -64,6 +65,7 @@ def lib():
     L.gem_get_info.argtypes = [vp, C.POINTER(Info)]
     L.gem_reset.argtypes = [vp, C.c_int]
     L.gem_sync.argtypes = [vp]
+    L.gem_set_numerics.argtypes = [vp, C.c_int, C.c_int]
     L.gem_forward.argtypes = [vp, C.c_uint32, C.c_uint32, _f32p]
     L.gem_full_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
     L.gem_twolevel_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
@@ -86,6 +88,7 @@ def _p(a: np.ndarray, t):
 
 
 FULL, TWO_LEVEL = 0, 1
+EXACT, FAST = 0, 1
 
 
 class Gemma:
@@ -129,6 +132,11 @@ class Gemma:
         info = Info()
         _check(lib().gem_get_info(self._h, C.byref(info)))
         self.info = {n: int(getattr(info, n)) for n, _ in Info._fields_}
+
+    def set_numerics(self, mode: int = EXACT, ref_threads: int = 8):
+        """EXACT: bit-identical to the reference's AVX-512 path with a pool of ref_threads threads.
+        FAST: tree reductions (within the reference's own cross-ISA spread)."""
+        _check(lib().gem_set_numerics(self._h, mode, ref_threads))
 
     def reset(self, seq: int = 0):
         _check(lib().gem_reset(self._h, seq))

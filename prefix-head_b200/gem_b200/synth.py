@@ -143,7 +143,8 @@ def tokens(n: int, vocab: int, seed: int = 11) -> np.ndarray:
 
 
 def cache_dir() -> Path:
-    d = Path(os.environ.get("GEM_CACHE", Path(__file__).resolve().parents[2] / "_cache"))
+    """Where generated models live: $GEM_CACHE, else ~/.cache/gem-b200 (outside the repository)."""
+    d = Path(os.environ.get("GEM_CACHE", Path.home() / ".cache" / "gem-b200"))
     d.mkdir(parents=True, exist_ok=True)
     return d
 

@@ -1,16 +1,21 @@
 """Parity of the sm_100a path (through the C ABI) with the oracle on identical seeded inputs.
 
-Bars: identical argmax token ids, per-token log-probs within 1e-3 absolute,
-dequantized weights bit-exact. Kernel-level GEMV outputs agree to fp32 summation-order noise."""
+Exact numerics (the default): hidden states and logits bit-identical to the oracle's AVX-512 path
+with the same pool size; log-probs within 1e-3 (they differ only in log-sum-exp summation order, so in
+practice ~1e-6); argmax token ids identical; dequantized weights bit-exact.
+
+Fast numerics: tree reductions make int8 quantization flips diverge from the oracle the same way the
+reference's own AVX2 and AVX-512 paths diverge from each other, so the bar is that spread."""
 import numpy as np
 import pytest
 
-from gem_b200 import FULL, TWO_LEVEL, Gemma, synth
+from gem_b200 import EXACT, FAST, FULL, TWO_LEVEL, Gemma, synth
 from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
 
-LP_TOL = 1e-3
+LP_TOL = 1e-3      # north-star per-token log-prob tolerance (absolute, nats)
+REF_THREADS = 8    # gem bench's default pool size (crates/gem/src/main.rs:197)
 
 
 @pytest.fixture(scope="module")
@@ -19,6 +24,14 @@ def torch():
     if not t.cuda.is_available():
         pytest.skip("no CUDA device")
     return t
+
+
+@pytest.fixture(scope="module")
+def isa():
+    i = orc.detect_isa()
+    if i != "avx512":
+        pytest.skip("exact numerics reproduce the AVX-512 path; this host has none")
+    return i
 
 
 def _gguf_mat(path, name):
@@ -34,59 +47,68 @@ NAMES = ["attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn
 
 
 @pytest.mark.parametrize("which", range(7))
-def test_matvec_matches_oracle(torch, small, which):
+def test_matvec_bit_exact(torch, isa, small, which):
     g = Gemma(small.gguf, ctx=64)
     m = _gguf_mat(small.gguf, f"blk.1.{NAMES[which]}.weight")
-    rng = np.random.default_rng(20 + which)
-    x = rng.standard_normal(m.cols).astype(np.float32)
+    x = np.random.default_rng(20 + which).standard_normal(m.cols).astype(np.float32)
     xd = torch.tensor(x, device="cuda")
     yd = torch.empty(m.rows, device="cuda")
     g.matvec_dev(1, which, xd.data_ptr(), yd.data_ptr())
-    want = m.matvec(x, "avx2", threads=1)
-    np.testing.assert_allclose(yd.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
+    want = m.matvec(x, "avx512", threads=1)
+    assert np.array_equal(yd.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
-def test_head_matvec_matches_oracle(torch, small):
+@pytest.mark.parametrize("which", [0, 6])
+def test_matvec_fast_close(torch, small, which):
+    g = Gemma(small.gguf, ctx=64)
+    g.set_numerics(FAST)
+    m = _gguf_mat(small.gguf, f"blk.2.{NAMES[which]}.weight")
+    x = np.random.default_rng(50 + which).standard_normal(m.cols).astype(np.float32)
+    xd = torch.tensor(x, device="cuda")
+    yd = torch.empty(m.rows, device="cuda")
+    g.matvec_dev(2, which, xd.data_ptr(), yd.data_ptr())
+    np.testing.assert_allclose(yd.cpu().numpy(), m.matvec(x, "avx2", threads=1), rtol=1e-5, atol=1e-6)
+
+
+def test_head_matvec_bit_exact(torch, isa, small):
     g = Gemma(small.gguf, ctx=64)
     m = _gguf_mat(small.gguf, "token_embd.weight")
     x = np.random.default_rng(30).standard_normal(m.cols).astype(np.float32)
     xd = torch.tensor(x, device="cuda")
     yd = torch.empty(m.rows, device="cuda")
     g.matvec_dev(-1, 0, xd.data_ptr(), yd.data_ptr())
-    np.testing.assert_allclose(yd.cpu().numpy(), m.matvec(x, "avx2", threads=4), rtol=1e-5, atol=1e-6)
+    assert np.array_equal(yd.cpu().numpy().view(np.uint32), m.matvec(x, "avx512", threads=4).view(np.uint32))
 
 
-def test_forward_hidden_state_tracks_oracle(torch, small, threads):
+def test_forward_hidden_state_bit_exact(torch, isa, small):
     g = Gemma(small.gguf, ctx=128)
-    o = orc.Model(small.gguf, ctx=128, threads=threads)
+    o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa="avx512")
     toks = synth.tokens(40, g.vocab, seed=3)
-    worst = 0.0
-    for i, t in enumerate(toks):
+    for i, t in enumerate(toks):  # 40 positions: past the 16-token window, through the global layer
         hg = g.forward(int(t), i)
         ho = o.forward(int(t), i)
-        worst = max(worst, float(np.abs(hg - ho).max()))
-        assert np.abs(hg - ho).mean() < 1e-3, (i, np.abs(hg - ho).mean())
-    assert worst < 5e-2
+        assert np.array_equal(hg.view(np.uint32), ho.view(np.uint32)), (i, np.abs(hg - ho).max())
 
 
 @pytest.mark.parametrize("head", [FULL, TWO_LEVEL])
-def test_score_matches_oracle(torch, small, threads, head):
+def test_score_exact(torch, isa, small, head):
     g = Gemma(small.gguf, ctx=128)
     g.load_twolevel(small.twolevel)
-    o = orc.Model(small.gguf, ctx=128, threads=threads)
+    o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa="avx512")
     o.load_twolevel(small.twolevel)
     toks = synth.tokens(49, g.vocab, seed=5)
     lp, am = g.score(toks, head)
     lpo, amo, _, _ = o.score(toks, head)
-    assert np.abs(lp - lpo).max() < LP_TOL, np.abs(lp - lpo).max()
+    assert np.abs(lp - lpo).max() < LP_TOL
+    assert np.abs(lp - lpo).max() < 2e-5  # only the log-sum-exp order differs
     assert np.array_equal(am, amo)
 
 
 @pytest.mark.parametrize("batch", [1, 64])
-def test_head_batch_matches_oracle(torch, small, threads, batch):
+def test_head_batch_exact(torch, isa, small, threads, batch):
     g = Gemma(small.gguf, ctx=64)
     g.load_twolevel(small.twolevel)
-    o = orc.Model(small.gguf, ctx=64, threads=threads)
+    o = orc.Model(small.gguf, ctx=64, threads=threads, isa="avx512")
     o.load_twolevel(small.twolevel)
     rng = np.random.default_rng(40 + batch)
     H = rng.standard_normal((batch, g.d)).astype(np.float32)
@@ -99,5 +121,26 @@ def test_head_batch_matches_oracle(torch, small, threads, batch):
         lp, am = lp.cpu().numpy(), am.cpu().numpy().astype(np.uint32)
         for b in range(batch):
             want = o.full(H[b], int(T[b])) if which == FULL else o.twolevel(H[b], int(T[b]))
-            assert abs(lp[b] - want[0]) < LP_TOL, (which, b, lp[b], want[0])
+            assert abs(lp[b] - want[0]) < 2e-5, (which, b, lp[b], want[0])
             assert am[b] == want[1], (which, b)
+
+
+@pytest.mark.parametrize("head", [FULL, TWO_LEVEL])
+def test_score_fast_within_reference_isa_spread(torch, isa, small, head):
+    g = Gemma(small.gguf, ctx=128)
+    g.set_numerics(FAST)
+    g.load_twolevel(small.twolevel)
+    toks = synth.tokens(49, g.vocab, seed=6)
+    lp, am = g.score(toks, head)
+    ref = {}
+    for i in ("avx512", "avx2"):
+        o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa=i)
+        o.load_twolevel(small.twolevel)
+        ref[i] = o.score(toks, head)[:2]
+    spread = np.abs(ref["avx512"][0] - ref["avx2"][0])
+    ours = np.abs(lp - ref["avx512"][0])
+    # The reference's own AVX-512 / AVX2 / scalar paths differ by up to ~0.045 nats per token on the
+    # 270M geometry (mean ~0.01): fast numerics must stay in that band.
+    assert ours.max() <= 0.05
+    assert ours.mean() <= 3 * max(spread.mean(), 1e-3)
+    assert (am == ref["avx512"][1]).mean() >= 0.9
