@@ -1,0 +1,377 @@
+#!/usr/bin/env python
+"""Benchmark of the per-token scoring path: tokens/s scored by the Gemma-3-270M-geometry Q8_0 model
+with the two-level head (2048 classes x 128 tokens), batch 1, 512 sequential random tokens per step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--numerics exact|fast]
+
+One step scores one 512-token sequence (gem bench's loop, crates/gem/src/main.rs:270-289) through the
+library's device-buffer entry point; `e2e` runs the same steps through the host-buffer entry point
+(token ids copied in, log-probs and argmax copied out, every step). Under torchrun each rank scores
+its own sequence on its own GPU (weak scaling, no collective on the data path); the timed region is
+bracketed by barriers and the time is the max over ranks. `--impl reference` times the oracle (the CPU
+restatement of gem's scoring path; the reference is Rust and no Rust toolchain exists here) on the
+host cores. Prints one JSON line from rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "prefix-head_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "tokens/s scored (270M Q8_0, 2-level head) b1+batched; head GEMV HBM GB/s"
+SEQ_TOKENS = 512
+CTX = 2048  # gem bench's context (main.rs:204)
+CLASSES = 2048
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--numerics", default="exact", choices=["exact", "fast"])
+    p.add_argument("--no-extras", action="store_true", help="skip the full-head / head-microbench / CPU legs")
+    p.add_argument("--cpu-threads", type=int, default=0, help="oracle threads for the CPU legs (0 = all cores)")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
+def hbm_peak():
+    p = peaks()
+    if "hbm_gbs" in p:
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def model_files():
+    from gem_b200 import synth
+    return synth.ensure("gemma3-270m", classes=CLASSES)
+
+
+def bytes_per_token(info, n_pos_per_layer, extra_blocks):
+    """Algorithmic HBM bytes of one scored token: every projection once (canonical GGUF sizes), the
+    class table and bias, the target class's block (plus the top class's block when it differs), the
+    KV rows attention reads and writes, and the small fp32 vectors (norm weights, RoPE rows)."""
+    d, nl, hd, nkv, nh = info["d"], info["layers"], info["head_dim"], info["n_kv_heads"], info["n_heads"]
+    k, per = info["classes"], info["per"]
+    row_bytes = d + d // 32 * 2  # one Q8_0 head row with f16 scales
+    kv_read = sum(n_pos_per_layer) * nkv * hd * 4 * 2
+    kv_write = nl * nkv * hd * 4 * 2
+    vectors = nl * (4 * d + 2 * hd + hd) * 4 + d * 4  # norm weights, q/k-norm weights, one RoPE sin/cos row
+    return info["body_bytes"] + k * d * 4 + k * 4 + (1 + extra_blocks) * per * row_bytes + kv_read + kv_write + vectors
+
+
+def n_pos_schedule(info, n_tokens):
+    """Average number of KV positions attention reads per layer over the sequence."""
+    w, nl = info["window"], info["layers"]
+    tot = np.zeros(nl)
+    for pos in range(n_tokens):
+        for l in range(nl):
+            swa = l % 6 < 5
+            tot[l] += min(pos + 1, w) if swa and w > 0 else pos + 1
+    return tot / n_tokens
+
+
+def run_reference(args):
+    """Times the oracle (the CPU restatement of the reference's scoring path) on all host cores."""
+    from gem_b200 import synth
+    from oracle import oracle as orc
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    mf = model_files()
+    threads = args.cpu_threads or os.cpu_count() or 1
+    m = orc.Model(mf.gguf, ctx=CTX, threads=threads)
+    m.load_twolevel(mf.twolevel)
+    toks = synth.tokens(SEQ_TOKENS + 1, m.vocab, seed=1000)
+    for _ in range(args.warmup):
+        m.score(toks, 1)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        m.score(toks, 1)
+        times.append(time.perf_counter() - t0)
+    per_step = sum(times) / len(times)
+    value = SEQ_TOKENS / per_step
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
+        "config": {"workload": "gemma3-270m Q8_0, two-level head 2048x128, batch 1, 512 random tokens per step",
+                   "model": "gemma3-270m geometry, random init N(0,0.02)", "global_batch": 1, "seq_len": SEQ_TOKENS,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "isa": m.isa, "sample": f"{args.steps} x {SEQ_TOKENS}-token sequences"},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import torch.distributed as dist
+    from gem_b200 import EXACT, FAST, FULL, TWO_LEVEL, Gemma, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    def barrier():
+        if world > 1:
+            dist.barrier()
+    if rank == 0:
+        mf = model_files()
+    barrier()
+    if rank != 0:
+        mf = model_files()
+
+    g = Gemma(mf.gguf, ctx=CTX, device=local)
+    g.load_twolevel(mf.twolevel)
+    g.set_numerics(EXACT if args.numerics == "exact" else FAST)
+    info = g.refresh_info()
+    stream = torch.cuda.ExternalStream(g.stream, device=local)
+    toks_h = synth.tokens(SEQ_TOKENS + 1, g.vocab, seed=1000 + rank)
+    toks_d = torch.tensor(toks_h.astype(np.int32), device="cuda")
+    lp_d = torch.empty(SEQ_TOKENS, device="cuda")
+    am_d = torch.empty(SEQ_TOKENS, dtype=torch.int32, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def step(head=TWO_LEVEL):
+        g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, head, lp_d.data_ptr(), am_d.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    g.sync()
+
+    # ---- timed region: K steps, device time with events on the model's stream, L2 flushed between ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        for a, b in evs:
+            flush.zero_()
+            torch.cuda.synchronize()
+            a.record(stream)
+            step()
+            b.record(stream)
+        torch.cuda.synchronize()
+        g.sync()
+    barrier()
+    ms = sum(a.elapsed_time(b) for a, b in evs)
+    t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    tokens = SEQ_TOKENS * args.steps * world
+    value = tokens / (ms_max / 1e3)
+    info = g.refresh_info()
+    kpt = info["kernels_per_token_twolevel"]
+
+    # roofline of the token step (a CUDA graph per token): algorithmic bytes per token / time per token
+    am_h = am_d.cpu().numpy().astype(np.uint32)
+    order = np.fromfile(str(mf.twolevel) + ".order", dtype="<u4")
+    per = info["per"]
+    cls_of = np.empty(g.vocab, np.int64)
+    cls_of[order] = np.arange(len(order)) // per
+    extra = float(np.mean(cls_of[am_h] != cls_of[toks_h[1:]]))
+    npos = n_pos_schedule(info, SEQ_TOKENS)
+    bpt = bytes_per_token(info, npos, extra)
+    per_token_s = (ms_max / 1e3) / (SEQ_TOKENS * args.steps)
+    peak, peak_kind = hbm_peak()
+    achieved = bpt / per_token_s / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "dram_bytes_per_token.txt"
+    if tf.exists():
+        for ln in tf.read_text().splitlines():
+            if ln.startswith(f"{args.numerics} two-level:"):
+                traffic = float(ln.split(":")[1].split()[0])
+
+    # ---- e2e: the host-buffer entry point (H2D token ids, D2H log-probs + argmax every step) ----
+    barrier()
+    torch.cuda.synchronize()
+    wall = []
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        g.score(toks_h, TWO_LEVEL)
+        wall.append(time.perf_counter() - t0)
+    barrier()
+    tw = torch.tensor([sum(wall)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tw, op=dist.ReduceOp.MAX)
+    e2e_value = tokens / float(tw.item())
+
+    extras = {}
+    if not args.no_extras and world == 1:
+        extras = run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf)
+
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
+            "numerics": args.numerics,
+            "config": {"workload": "gemma3-270m Q8_0, two-level head 2048x128, batch 1, 512 random tokens per step",
+                       "model": "gemma3-270m geometry (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "
+                                "random init N(0,0.02) quantized to Q8_0",
+                       "global_batch": world, "seq_len": SEQ_TOKENS, "parallelism": f"dp{world} (one sequence per GPU)",
+                       "l2": "flushed (256 MiB write) before every step; the 512 tokens of a step re-read the same weights"},
+            "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "kernel": f"token step (CUDA graph of {kpt} kernels)",
+                         "algorithmic_bytes_per_token": int(bpt)},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": (SEQ_TOKENS + 1) * 4,
+                    "d2h_bytes_per_step": SEQ_TOKENS * 8},
+            "gpu_launches": int(kpt * SEQ_TOKENS * args.steps) if kpt > 0 else None,
+            "clocks": clocks,
+        }
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    g.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def time_dev(torch, stream, fn, iters, flush):
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in evs:
+        flush.zero_()
+        torch.cuda.synchronize()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / iters
+
+
+def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
+    """Secondary figures: the full head end to end, the head microbenchmark (full 262144x640 GEMV with
+    fused log-sum-exp vs the two-level head, batch 1 and 64) and the CPU baseline."""
+    from gem_b200 import FULL, TWO_LEVEL, synth
+    from oracle import oracle as orc
+    out = {}
+    # full head, same sequence
+    g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr())
+    ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr()),
+                  2, flush)
+    out["full_head"] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3)}
+    # head microbenchmark: h ~ N(0, 1)
+    peak, _ = hbm_peak()
+    head_bytes = g.info["head_bytes"]
+    rng = np.random.default_rng(9)
+    hm = {}
+    for batch in (1, 64):
+        H = torch.tensor(rng.standard_normal((batch, g.d)).astype(np.float32), device="cuda")
+        T = torch.tensor(rng.integers(0, g.vocab, batch).astype(np.int32), device="cuda")
+        lp = torch.empty(batch, device="cuda")
+        am = torch.empty(batch, dtype=torch.int32, device="cuda")
+        for name, fn in (("full", g.head_full_dev), ("two_level", g.head_twolevel_dev)):
+            call = lambda: fn(H.data_ptr(), T.data_ptr(), batch, lp.data_ptr(), am.data_ptr())
+            call()
+            us = time_dev(torch, stream, call, 5, flush) * 1e3
+            e = {"us": round(us, 2)}
+            if name == "full":
+                gbs = head_bytes / (us * 1e-6) / 1e9
+                e.update({"GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4), "bytes": head_bytes})
+            hm[f"{name}_b{batch}"] = e
+    out["head_microbench"] = hm
+    # CPU baseline: the oracle on the host cores, one 512-token sequence, two-level head
+    threads = args.cpu_threads or os.cpu_count() or 1
+    m = orc.Model(mf.gguf, ctx=CTX, threads=threads)
+    m.load_twolevel(mf.twolevel)
+    toks = synth.tokens(SEQ_TOKENS + 1, m.vocab, seed=1000)
+    t0 = time.perf_counter()
+    m.score(toks, 1)
+    dt = time.perf_counter() - t0
+    out["cpu_baseline"] = {"value": round(SEQ_TOKENS / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+                           "isa": m.isa, "sample": f"one {SEQ_TOKENS}-token sequence, two-level head, same workload"}
+    m.close()
+    return out
+
+
+if __name__ == "__main__":
+    main()

@@ -49,6 +49,8 @@ typedef struct gem_info {
   int64_t body_bytes;       /* canonical (GGUF block size) bytes of the 7 projections x layers */
   int64_t head_bytes;       /* canonical bytes of the output matrix */
   int64_t device;
+  int64_t kernels_per_token_full;      /* kernels one scoring step launches (-1 until first used) */
+  int64_t kernels_per_token_twolevel;
 } gem_info;
 
 const char* gem_last_error(void);
@@ -79,6 +81,9 @@ int gem_set_numerics(gem_model* m, int mode, int ref_threads);
 /* Clears a sequence's KV cache (the reference rebuilds its cache per run; bench reuses it). */
 int gem_reset(gem_model* m, int seq);
 int gem_sync(gem_model* m);
+/* The CUDA stream (cudaStream_t) every call of this model is enqueued on, so callers can order
+ * their own work and time with events on it. */
+int gem_get_stream(const gem_model* m, void** stream);
 
 /* Gemma::forward(tok, pos) (model.rs:286-430) on sequence 0: runs one token, appends to the KV
  * cache, keeps the final-norm hidden state on the device for the head calls below and copies it to

@@ -115,7 +115,9 @@ struct gem_model {
   uint32_t* top_of = nullptr;
   // graphs
   cudaGraphExec_t score_graph[2] = {nullptr, nullptr};
+  int64_t graph_kernels[2] = {-1, -1};
   void drop_graphs() {
+    graph_kernels[0] = graph_kernels[1] = -1;
     for (auto& g : score_graph)
       if (g) {
         cudaGraphExecDestroy(g);
@@ -557,6 +559,8 @@ int gem_get_info(const gem_model* m, gem_info* o) {
   o->head_dim = m->hd, o->ffn = m->ff, o->ctx = m->ctx, o->window = m->window, o->bos = m->bos;
   o->body_bits = m->body_bits, o->head_bits = m->head_bits, o->classes = m->two ? m->k : 0, o->per = m->two ? m->per : 0;
   o->max_seqs = m->max_seqs, o->body_bytes = (int64_t)m->body_bytes, o->head_bytes = (int64_t)m->head.bytes, o->device = m->device;
+  o->kernels_per_token_full = m->graph_kernels[0];
+  o->kernels_per_token_twolevel = m->graph_kernels[1];
   API_END
 }
 
@@ -582,6 +586,13 @@ int gem_set_numerics(gem_model* m, int mode, int ref_threads) {
   m->exact = mode == GEM_NUMERICS_EXACT;
   m->ref_threads = ref_threads;
   m->drop_graphs();
+  API_END
+}
+
+int gem_get_stream(const gem_model* m, void** stream) {
+  API_BEGIN
+  if (!m || !stream) throw Error(GEM_E_ARG, "null argument");
+  *stream = (void*)m->st;
   API_END
 }
 
@@ -663,6 +674,17 @@ static void run_score(gem_model* m, size_t n, int head) {
       throw;
     }
     ck(cudaStreamEndCapture(m->st, &g), "end capture");
+    size_t nn = 0;
+    ck(cudaGraphGetNodes(g, nullptr, &nn), "graph nodes");
+    std::vector<cudaGraphNode_t> nodes(nn);
+    ck(cudaGraphGetNodes(g, nodes.data(), &nn), "graph nodes");
+    int64_t kernels = 0;
+    for (auto nd : nodes) {
+      cudaGraphNodeType t;
+      ck(cudaGraphNodeGetType(nd, &t), "node type");
+      kernels += t == cudaGraphNodeTypeKernel;
+    }
+    m->graph_kernels[head] = kernels;
     cudaGraphExec_t ge;
     cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);

@@ -16,8 +16,8 @@ import numpy as np
 
 PKG = Path(__file__).resolve().parents[1]          # prefix-head_b200/
 LIB = PKG / "_build" / "libgem_b200.so"
-SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "common.cuh", "kernels.cuh", "host.cpp",
-                                      "host.hpp", "runtime.cpp")]
+SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "common.cuh", "kernels.cuh",
+                                      "host.cpp", "host.hpp", "runtime.cpp")]
 
 GEM_OK = 0
 STATUS = {-1: "GEM_E_ARG", -2: "GEM_E_IO", -3: "GEM_E_FORMAT", -4: "GEM_E_CUDA", -5: "GEM_E_NOMEM",
@@ -33,7 +33,8 @@ class GemError(RuntimeError):
 class Info(C.Structure):
     _fields_ = [(n, C.c_int64) for n in ("d", "vocab", "layers", "n_heads", "n_kv_heads", "head_dim", "ffn", "ctx",
                                          "window", "bos", "body_bits", "head_bits", "classes", "per", "max_seqs",
-                                         "body_bytes", "head_bytes", "device")]
+                                         "body_bytes", "head_bytes", "device", "kernels_per_token_full",
+                                         "kernels_per_token_twolevel")]
 
 
 def build(force: bool = False) -> Path:
@@ -65,6 +66,7 @@ def lib():
     L.gem_get_info.argtypes = [vp, C.POINTER(Info)]
     L.gem_reset.argtypes = [vp, C.c_int]
     L.gem_sync.argtypes = [vp]
+    L.gem_get_stream.argtypes = [vp, C.POINTER(vp)]
     L.gem_set_numerics.argtypes = [vp, C.c_int, C.c_int]
     L.gem_forward.argtypes = [vp, C.c_uint32, C.c_uint32, _f32p]
     L.gem_full_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
@@ -172,6 +174,19 @@ class Gemma:
         """Same loop on device buffers (ints: device addresses); asynchronous on the model's stream."""
         _check(lib().gem_score_dev(self._h, toks_ptr, n, head, lp_ptr, am_ptr))
 
+    def refresh_info(self):
+        info = Info()
+        _check(lib().gem_get_info(self._h, C.byref(info)))
+        self.info = {n: int(getattr(info, n)) for n, _ in Info._fields_}
+        return self.info
+
+    @property
+    def stream(self) -> int:
+        """The model's cudaStream_t as an integer (for torch.cuda.ExternalStream)."""
+        s = C.c_void_p()
+        _check(lib().gem_get_stream(self._h, C.byref(s)))
+        return int(s.value or 0)
+
     def sync(self):
         _check(lib().gem_sync(self._h))
 
@@ -183,3 +198,4 @@ class Gemma:
 
     def head_twolevel_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
         _check(lib().gem_head_twolevel_dev(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
+
