@@ -119,6 +119,17 @@ int gem_head_full_dev(gem_model* m, const float* h_dev, const uint32_t* targets_
 /* Two-level head for `batch` hidden states. */
 int gem_head_twolevel_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
                           float* logprob_dev, uint32_t* argmax_dev);
+/* gem_head_full_dev for callers that cannot allocate device memory when they call it (a process whose
+ * memory belongs to another allocator or is planned up front, a loop that must not block in the
+ * allocator). No counterpart in the reference, which runs on the CPU and allocates freely. Same
+ * arguments and results as gem_head_full_dev; allocates nothing and does not synchronise (results
+ * and range errors are visible after gem_sync). Its scratch is one static 1 MiB device array per GPU,
+ * held until the process exits, so batch is limited (about 190 hidden states at d = 640; larger
+ * batches return GEM_E_ARG). The first call on a device resolves that array's address: make it
+ * before any stream capture. All calls on a device share the array: calls that overlap on the GPU
+ * race. */
+int gem_head_full_noalloc(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
+                          float* logprob_dev, uint32_t* argmax_dev);
 
 #ifdef __cplusplus
 }

@@ -13,6 +13,7 @@
 
 #include "../../include/gem.h"
 #include "host.hpp"
+#include "internal.hpp"
 #include "kernels.cuh"
 
 using namespace gem;
@@ -274,6 +275,25 @@ struct gem_model {
     }
   }
 };
+
+namespace {
+
+}  // namespace
+
+namespace gem {
+bool model_head_view(const gem_model* m, ModelHeadView* out) {
+  if (!m || !out) return false;
+  out->w = m->head.v;
+  out->exact = m->exact;
+  out->st = m->st;
+  out->sms = m->sms;
+  out->device = m->device;
+  out->d = m->d;
+  out->err = m->err;
+  return true;
+}
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace gem
 
 namespace {
 

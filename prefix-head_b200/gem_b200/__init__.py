@@ -16,8 +16,8 @@ import numpy as np
 
 PKG = Path(__file__).resolve().parents[1]          # prefix-head_b200/
 LIB = PKG / "_build" / "libgem_b200.so"
-SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "common.cuh", "kernels.cuh",
-                                      "host.cpp", "host.hpp", "runtime.cpp")]
+SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "noalloc.cu", "common.cuh", "kernels.cuh",
+                                      "internal.hpp", "host.cpp", "host.hpp", "runtime.cpp")]
 
 GEM_OK = 0
 STATUS = {-1: "GEM_E_ARG", -2: "GEM_E_IO", -3: "GEM_E_FORMAT", -4: "GEM_E_CUDA", -5: "GEM_E_NOMEM",
@@ -76,6 +76,7 @@ def lib():
     L.gem_matvec_dev.argtypes = [vp, C.c_int, C.c_int, vp, vp]
     L.gem_head_full_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
     L.gem_head_twolevel_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
+    L.gem_head_full_noalloc.argtypes = [vp, vp, vp, C.c_int, vp, vp]
     _lib = L
     return L
 
@@ -199,3 +200,6 @@ class Gemma:
     def head_twolevel_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
         _check(lib().gem_head_twolevel_dev(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
 
+    def head_full_noalloc(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
+        """gem_head_full_dev without any device allocation (static scratch; asynchronous)."""
+        _check(lib().gem_head_full_noalloc(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
