@@ -247,6 +247,7 @@ def main():
     tokens = SEQ_TOKENS * args.steps * world
     value = tokens / (ms_max / 1e3)
     info = g.refresh_info()
+    pipelined, G, GH, why = g.schedule(TWO_LEVEL)
     kpt = info["kernels_per_token_twolevel"]
 
     # roofline of the token step (a CUDA graph per token): algorithmic bytes per token / time per token
@@ -300,13 +301,16 @@ def main():
                                 "random init N(0,0.02) quantized to Q8_0",
                        "global_batch": world, "seq_len": SEQ_TOKENS, "parallelism": f"dp{world} (one sequence per GPU)",
                        "l2": "flushed (256 MiB write) before every step; the 512 tokens of a step re-read the same weights"},
+            "schedule": ({"kind": "layer-pipelined persistent kernel", "ctas_per_layer": G, "head_ctas": GH}
+                         if pipelined else {"kind": "CUDA graph per token", "why": why}),
             "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(achieved, 1), "peak": peak,
-                         "peak_kind": peak_kind, "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "kernel": f"token step (CUDA graph of {kpt} kernels)",
+                         "peak_kind": peak_kind, "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": ("k_pipe_score (one launch per 512-token step)" if pipelined
+                                    else f"token step (CUDA graph of {kpt} kernels)"),
                          "algorithmic_bytes_per_token": int(bpt)},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": (SEQ_TOKENS + 1) * 4,
                     "d2h_bytes_per_step": SEQ_TOKENS * 8},
-            "gpu_launches": int(kpt * SEQ_TOKENS * args.steps) if kpt > 0 else None,
+            "gpu_launches": (2 * args.steps if pipelined else int(kpt * SEQ_TOKENS * args.steps) if kpt > 0 else None),
             "clocks": clocks,
         }
         line.update(extras)
@@ -331,9 +335,17 @@ def time_dev(torch, stream, fn, iters, flush):
 def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     """Secondary figures: the full head end to end, the head microbenchmark (full 262144x640 GEMV with
     fused log-sum-exp vs the two-level head, batch 1 and 64) and the CPU baseline."""
-    from gem_b200 import FULL, TWO_LEVEL, synth
+    from gem_b200 import AUTO, FULL, SEQUENTIAL, TWO_LEVEL, synth
     from oracle import oracle as orc
     out = {}
+    # the same workload with each token finishing before the next starts (a CUDA graph per token)
+    g.set_schedule(SEQUENTIAL)
+    g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(), am_d.data_ptr())
+    ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(), am_d.data_ptr()),
+                  2, flush)
+    out["sequential"] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+                         "schedule": "one CUDA graph per token"}
+    g.set_schedule(AUTO)
     # full head, same sequence
     g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr())
     ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr()),

@@ -78,6 +78,21 @@ int gem_get_info(const gem_model* m, gem_info* out);
  *   quantization flips, within the spread between the reference's own AVX2 and AVX-512 paths. */
 enum { GEM_NUMERICS_EXACT = 0, GEM_NUMERICS_FAST = 1 };
 int gem_set_numerics(gem_model* m, int mode, int ref_threads);
+/* How gem_score / gem_score_dev run the two-level loop. GEM_SCHEDULE_AUTO (default): with exact
+ * numerics and a loaded two-level head, as one layer-pipelined kernel - each decoder layer and the
+ * head own a group of SMs and consecutive tokens flow through them as a wavefront; every token's
+ * arithmetic and weight reads are those of the per-token forward, so results are identical.
+ * GEM_SCHEDULE_SEQUENTIAL: one CUDA graph per token, each token finishing before the next starts. */
+enum { GEM_SCHEDULE_AUTO = 0, GEM_SCHEDULE_SEQUENTIAL = 1 };
+int gem_set_schedule(gem_model* m, int schedule);
+/* Whether scoring with `head` (0 full, 1 two-level) runs pipelined; stages_ctas (nullable, 2 ints)
+ * receives CTAs per layer stage and for the head stage. gem_last_error() then holds the reason. */
+int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas);
+/* Failure-detection test hook for the pipelined schedule: layer stage `stage` (-1: none) computes but
+ * never hands its residual on, so the next stage's wait, bounded by wait_ms, expires; the scoring call
+ * then returns GEM_E_TIMEOUT and the model stays usable. wait_ms also bounds every device-side wait
+ * afterwards (default 2000). */
+int gem_test_withhold_stage(gem_model* m, int stage, int wait_ms);
 /* Clears a sequence's KV cache (the reference rebuilds its cache per run; bench reuses it). */
 int gem_reset(gem_model* m, int seq);
 int gem_sync(gem_model* m);

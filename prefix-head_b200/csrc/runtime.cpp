@@ -15,6 +15,7 @@
 #include "host.hpp"
 #include "internal.hpp"
 #include "kernels.cuh"
+#include "pipeline.cuh"
 
 using namespace gem;
 
@@ -114,6 +115,14 @@ struct gem_model {
   int ref_threads = 8;
   float *qn = nullptr, *scores = nullptr, *top_inner = nullptr;
   uint32_t* top_of = nullptr;
+  // layer-pipelined scoring (pipeline.cu)
+  int schedule = GEM_SCHEDULE_AUTO;
+  bool pipe_ready = false;
+  PipeArgs pipe{};
+  size_t pipe_smem = 0;
+  std::string pipe_why;  // why the pipeline is not used, for gem_get_schedule
+  unsigned long long wait_ns = 2000000000ull;  // bound of every device-side wait
+  int withhold_stage = -1;                     // failure-detection test hook
   // graphs
   cudaGraphExec_t score_graph[2] = {nullptr, nullptr};
   int64_t graph_kernels[2] = {-1, -1};
@@ -262,6 +271,90 @@ struct gem_model {
     launch_tl_argmax(T, batch, top_of, top_inner, st);
   }
   void enqueue_head(int which, float* lpo, uint32_t* amo) { run_head(which, haq, has, h, nullptr, 1, lpo, amo); }
+
+  // Can the two-level scoring loop run as one layer-pipelined kernel on this model and GPU?
+  bool pipeline_supported() {
+    pipe_why.clear();
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+    if (!exact) pipe_why = "fast numerics";
+    else if (!two) pipe_why = "no two-level head";
+    else if (untied) pipe_why = "separate output matrix";
+    else if (!coop) pipe_why = "no cooperative launch";
+    else if (nh > 16 || nh + nkv > 15 || hd > 256) pipe_why = "head counts";
+    else if (nl + 1 > sms) pipe_why = "more layers than SMs";
+    return pipe_why.empty();
+  }
+
+  void setup_pipeline() {
+    if (pipe_ready) return;
+    PipeArgs& P = pipe;
+    P = PipeArgs{};
+    P.nl = nl, P.d = d, P.nh = nh, P.nkv = nkv, P.hd = hd, P.ff = ff, P.ctx = ctx, P.vocab = vocab;
+    bool any_global = false;
+    for (auto& L : layers) any_global |= !L.swa;
+    P.max_npos = (any_global || window <= 0) ? ctx : std::min(window, ctx);
+    P.eps = eps, P.qscale = 1.0f / std::sqrt((float)hd), P.embed_scale = embed_scale, P.silu = silu ? 1 : 0;
+    P.layers_bits = layers[0].qkv.v.bits, P.layers_scale_f32 = layers[0].qkv.v.scale_f32;
+    P.emb = head.v;
+    P.blocks = blocks.v;
+    P.A = A, P.b = b, P.out_norm = out_norm, P.cls_of = cls_of, P.pos_of = pos_of, P.order = order;
+    P.k = k, P.per = per;
+    P.ref_threads = ref_threads;
+    // CTAs per stage in proportion to the bytes each stage reads per token
+    double layer_bytes = (double)body_bytes / nl + (double)P.max_npos / 2 * nkv * hd * 8;
+    double head_bytes = (double)k * d * 4 + 2.0 * per * (blocks.bytes / std::max(1, blocks.v.rows));
+    int G = std::max(1, (int)std::floor(sms / (nl + head_bytes / layer_bytes)));
+    while (G > 1 && nl * G + 1 > sms) --G;
+    P.G = G;
+    P.GH = std::max(1, std::min(sms - nl * G, 32));
+    std::vector<PipeLayer> pl(nl);
+    size_t layer_elems = (size_t)ctx * nkv * hd;
+    for (int l = 0; l < nl; ++l) {
+      const Layer& L = layers[l];
+      PipeLayer& q = pl[l];
+      q.qkv = L.qkv.v, q.o = L.o.v, q.gu = L.gu.v, q.down = L.down.v;
+      q.attn_norm = L.attn_norm, q.q_norm = L.q_norm, q.k_norm = L.k_norm, q.post_attn = L.post_attn;
+      q.ffn_norm = L.ffn_norm, q.post_ffw = L.post_ffw, q.bqkv = L.bqkv;
+      q.rope_sin = rope_sin[L.swa ? 0 : 1], q.rope_cos = rope_cos[L.swa ? 0 : 1];
+      q.kcache = kc + (size_t)l * layer_elems;
+      q.vcache = vc + (size_t)l * layer_elems;
+      q.window = L.swa ? window : 0;
+    }
+    P.layers = upload(pl);
+    P.ring = alloc<float>((size_t)(nl + 1) * PIPE_RING * d);
+    P.ready = alloc<unsigned>((size_t)(nl + 1) * PIPE_RING);
+    P.consumed = alloc<unsigned>((size_t)(nl + 1));
+    P.bar = alloc<unsigned>((size_t)(nl + 1) * 32);
+    P.scratch_stride = pipe_scratch_floats(nh, nkv, hd, d, ff, P.max_npos, ref_threads);
+    P.scratch = alloc<float>(P.scratch_stride * nl);
+    P.head_scratch = alloc<float>((size_t)k + 2 * per);
+    P.err = err;
+    pipe_smem = std::max(pipe_smem_bytes(P), (size_t)120 * 1024);  // > half an SM: one CTA per SM
+    pipe_ready = true;
+  }
+
+  // The scoring loop as one pipelined kernel on device buffers (toks: n + 1 ids).
+  bool try_pipeline(const uint32_t* toks_d, size_t n, uint32_t base_pos, float* lp_d, uint32_t* am_d) {
+    if (schedule == GEM_SCHEDULE_SEQUENTIAL || !pipeline_supported()) return false;
+    setup_pipeline();
+    PipeArgs P = pipe;
+    P.ref_threads = ref_threads;
+    P.toks = toks_d, P.n = (int)n, P.base_pos = (int)base_pos, P.lp_out = lp_d, P.am_out = am_d, P.h_last = h;
+    P.wait_ns = wait_ns;
+    P.withhold_stage = withhold_stage;
+    ck(cudaMemsetAsync(P.ready, 0, (size_t)(nl + 1) * PIPE_RING * sizeof(unsigned), st), "memset");
+    ck(cudaMemsetAsync(P.consumed, 0, (size_t)(nl + 1) * sizeof(unsigned), st), "memset");
+    ck(cudaMemsetAsync(P.bar, 0, (size_t)(nl + 1) * 32 * sizeof(unsigned), st), "memset");
+    int rc = launch_pipe_score(P, pipe_smem, st);
+    if (rc == -1) {
+      pipe_why = "weight formats without a pipelined instantiation";
+      return false;
+    }
+    if (rc != 0) throw Error(GEM_E_CUDA, std::string("pipelined launch: ") + cudaGetErrorString((cudaError_t)rc));
+    launch_quantize(h, d, haq, has, st);  // the last token's hidden state, for later head calls
+    return true;
+  }
 
   void check_launch() { ck(cudaGetLastError(), "kernel launch"); }
   void sync() {
@@ -559,6 +652,7 @@ int gem_open_twolevel(gem_model* m, const char* prefix) {
   m->k = (int)k;
   m->per = (int)per;
   m->two = true;
+  m->pipe_ready = false;
   m->hbatch = 0;
   m->ensure_head_batch(1);
   m->drop_graphs();
@@ -604,8 +698,42 @@ int gem_set_numerics(gem_model* m, int mode, int ref_threads) {
   ck(cudaSetDevice(m->device), "cudaSetDevice");
   m->sync();
   m->exact = mode == GEM_NUMERICS_EXACT;
+  if (m->ref_threads != ref_threads) m->pipe_ready = false;  // scratch is sized by the pool size
   m->ref_threads = ref_threads;
   m->drop_graphs();
+  API_END
+}
+
+int gem_set_schedule(gem_model* m, int schedule) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  if (schedule != GEM_SCHEDULE_AUTO && schedule != GEM_SCHEDULE_SEQUENTIAL) throw Error(GEM_E_ARG, "unknown schedule");
+  m->schedule = schedule;
+  API_END
+}
+
+int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  bool ok = head == 1 && m->schedule == GEM_SCHEDULE_AUTO && m->pipeline_supported();
+  if (ok) m->setup_pipeline();
+  if (pipelined) *pipelined = ok ? 1 : 0;
+  if (stages_ctas) {
+    stages_ctas[0] = ok ? m->pipe.G : 0;
+    stages_ctas[1] = ok ? m->pipe.GH : 0;
+  }
+  if (!ok && m->pipe_why.empty()) m->pipe_why = head == 1 ? "sequential schedule requested" : "full head";
+  g_last_error = ok ? std::string("pipelined") : m->pipe_why;
+  API_END
+}
+
+int gem_test_withhold_stage(gem_model* m, int stage, int wait_ms) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  if (stage < -1 || stage >= m->nl) throw Error(GEM_E_RANGE, "stage out of range");
+  if (wait_ms < 1 || wait_ms > 60000) throw Error(GEM_E_ARG, "wait_ms must be in 1..60000");
+  m->withhold_stage = stage;
+  m->wait_ns = (unsigned long long)wait_ms * 1000000ull;
   API_END
 }
 
@@ -679,6 +807,10 @@ static void run_score(gem_model* m, size_t n, int head) {
     *m->cur_host = StepCur{(uint32_t)m->bos, 0, 0, 0};
     ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
     m->enqueue_body(0);
+  }
+  if (head == 1 && m->try_pipeline(m->toks, n, (uint32_t)off, m->lp, m->am)) {
+    m->have_h = true;
+    return;
   }
   ck(cudaMemsetAsync(m->step, 0, 4, m->st), "step");
   if (!m->score_graph[head]) {

@@ -16,7 +16,7 @@ import numpy as np
 
 PKG = Path(__file__).resolve().parents[1]          # prefix-head_b200/
 LIB = PKG / "_build" / "libgem_b200.so"
-SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "noalloc.cu", "common.cuh", "kernels.cuh",
+SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "pipeline.cu", "noalloc.cu", "exact.cuh", "pipeline.cuh", "common.cuh", "kernels.cuh",
                                       "internal.hpp", "host.cpp", "host.hpp", "runtime.cpp")]
 
 GEM_OK = 0
@@ -67,6 +67,9 @@ def lib():
     L.gem_reset.argtypes = [vp, C.c_int]
     L.gem_sync.argtypes = [vp]
     L.gem_get_stream.argtypes = [vp, C.POINTER(vp)]
+    L.gem_set_schedule.argtypes = [vp, C.c_int]
+    L.gem_test_withhold_stage.argtypes = [vp, C.c_int, C.c_int]
+    L.gem_get_schedule.argtypes = [vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.gem_set_numerics.argtypes = [vp, C.c_int, C.c_int]
     L.gem_forward.argtypes = [vp, C.c_uint32, C.c_uint32, _f32p]
     L.gem_full_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
@@ -92,6 +95,7 @@ def _p(a: np.ndarray, t):
 
 FULL, TWO_LEVEL = 0, 1
 EXACT, FAST = 0, 1
+AUTO, SEQUENTIAL = 0, 1
 
 
 class Gemma:
@@ -140,6 +144,21 @@ class Gemma:
         """EXACT: bit-identical to the reference's AVX-512 path with a pool of ref_threads threads.
         FAST: tree reductions (within the reference's own cross-ISA spread)."""
         _check(lib().gem_set_numerics(self._h, mode, ref_threads))
+
+    def set_schedule(self, schedule: int = AUTO):
+        """AUTO: two-level scoring as one layer-pipelined kernel when supported; SEQUENTIAL: a graph per token."""
+        _check(lib().gem_set_schedule(self._h, schedule))
+
+    def schedule(self, head: int = TWO_LEVEL):
+        """(pipelined, ctas per layer stage, head ctas, reason)."""
+        p = C.c_int()
+        sc = (C.c_int * 2)()
+        _check(lib().gem_get_schedule(self._h, head, C.byref(p), sc))
+        return bool(p.value), sc[0], sc[1], lib().gem_last_error().decode()
+
+    def test_withhold_stage(self, stage: int, wait_ms: int = 2000):
+        """Failure-detection hook: layer stage `stage` withholds its output (-1 restores normal runs)."""
+        _check(lib().gem_test_withhold_stage(self._h, stage, wait_ms))
 
     def reset(self, seq: int = 0):
         _check(lib().gem_reset(self._h, seq))

@@ -144,3 +144,63 @@ def test_score_fast_within_reference_isa_spread(torch, isa, small, head):
     assert ours.max() <= 0.05
     assert ours.mean() <= 3 * max(spread.mean(), 1e-3)
     assert (am == ref["avx512"][1]).mean() >= 0.9
+
+
+def test_pipelined_and_sequential_schedules_agree(torch, isa, small):
+    from gem_b200 import AUTO, SEQUENTIAL
+    g = Gemma(small.gguf, ctx=128)
+    g.load_twolevel(small.twolevel)
+    pipelined, G, GH, why = g.schedule(TWO_LEVEL)
+    assert pipelined, why
+    toks = synth.tokens(60, g.vocab, seed=12)
+    lp_p, am_p = g.score(toks, TWO_LEVEL)
+    g.set_schedule(SEQUENTIAL)
+    assert not g.schedule(TWO_LEVEL)[0]
+    lp_s, am_s = g.score(toks, TWO_LEVEL)
+    assert np.abs(lp_p - lp_s).max() < 2e-5 and np.array_equal(am_p, am_s)
+    o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa="avx512")
+    o.load_twolevel(small.twolevel)
+    lpo, amo, _, _ = o.score(toks, TWO_LEVEL)
+    assert np.abs(lp_p - lpo).max() < 2e-5 and np.array_equal(am_p, amo)
+    # the pipelined kernel also leaves the last hidden state for single-token head calls
+    g.set_schedule(AUTO)
+    g.score(toks, TWO_LEVEL)
+    lp1, am1 = g.twolevel_logprob(int(toks[-1]))
+    assert abs(lp1 - lp_p[-1]) < 2e-5 and am1 == am_p[-1]
+
+
+def test_pipeline_bounded_wait_reports_timeout(torch, small):
+    from gem_b200 import GemError
+    g = Gemma(small.gguf, ctx=64)
+    g.load_twolevel(small.twolevel)
+    toks = synth.tokens(20, g.vocab, seed=13)
+    want, _ = g.score(toks, TWO_LEVEL)
+    g.test_withhold_stage(2, wait_ms=200)
+    with pytest.raises(GemError) as e:
+        g.score(toks, TWO_LEVEL)
+    assert e.value.code == -9  # GEM_E_TIMEOUT
+    g.test_withhold_stage(-1, wait_ms=2000)
+    g.reset(0)
+    again, _ = g.score(toks, TWO_LEVEL)  # the context is still usable
+    assert np.abs(again - want).max() < 2e-5
+
+
+@pytest.fixture(scope="module")
+def m270():
+    return synth.ensure("gemma3-270m", classes=2048)  # shared cache with bench.py
+
+
+def test_270m_pipelined_scoring_is_exact(torch, isa, m270):
+    g = Gemma(m270.gguf, ctx=2048)
+    g.load_twolevel(m270.twolevel)
+    assert g.schedule(TWO_LEVEL)[0]
+    o = orc.Model(m270.gguf, ctx=2048, threads=REF_THREADS, isa="avx512")
+    o.load_twolevel(m270.twolevel)
+    toks = synth.tokens(97, g.vocab, seed=21)
+    lp, am = g.score(toks, TWO_LEVEL)
+    lpo, amo, _, _ = o.score(toks, TWO_LEVEL)
+    assert np.abs(lp - lpo).max() < 2e-5, np.abs(lp - lpo).max()
+    assert np.array_equal(am, amo)
+    lpf, amf = g.score(toks, FULL)
+    lpfo, amfo, _, _ = o.score(toks, FULL)
+    assert np.abs(lpf - lpfo).max() < 1e-4 and np.array_equal(amf, amfo)
