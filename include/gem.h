@@ -88,6 +88,14 @@ int gem_set_schedule(gem_model* m, int schedule);
 /* Whether scoring with `head` (0 full, 1 two-level) runs pipelined; stages_ctas (nullable, 2 ints)
  * receives CTAs per layer stage and for the head stage. gem_last_error() then holds the reason. */
 int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas);
+/* Phase profile of pipelined scoring, gem's GEM_PROFILE (main.rs:312-317) on the device: while on,
+ * CTA 0 of every stage timestamps its phases; gem_get_phase_profile returns mean microseconds per
+ * token per phase, averaged over layer stages (16 phases: input wait, attn norm, q/k/v, barrier,
+ * qk-norm + scores, barrier, softmax + P.V, barrier, combine + o, barrier, norms, gate/up, barrier,
+ * down, barrier, hand-off) and for the head stage (6: input wait, norm, classes + target block,
+ * barrier, top block, barrier). Turning it on clears the sums. */
+int gem_set_profiling(gem_model* m, int on);
+int gem_get_phase_profile(gem_model* m, double* layer_us, int n_layer, double* head_us, int n_head);
 /* Failure-detection test hook for the pipelined schedule: layer stage `stage` (-1: none) computes but
  * never hands its residual on, so the next stage's wait, bounded by wait_ms, expires; the scoring call
  * then returns GEM_E_TIMEOUT and the model stays usable. wait_ms also bounds every device-side wait

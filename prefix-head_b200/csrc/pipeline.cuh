@@ -7,7 +7,8 @@
 
 namespace gem {
 
-constexpr int PIPE_RING = 4;  // residual slots between consecutive stages
+constexpr int PIPE_RING = 4;     // residual slots between consecutive stages
+constexpr int PIPE_PHASES = 24;  // profiled phases per stage
 
 struct PipeLayer {
   MatView qkv, o, gu, down;
@@ -47,7 +48,11 @@ struct PipeArgs {
   size_t scratch_stride;
   float* head_scratch;  // k + 2 * per
   int* err;
+  int ring_slots, slot_bytes, slot_scale_off;  // weight ring geometry (layer stages)
+  int checks;                                   // self-checks on (see check_ok)
   unsigned long long wait_ns;  // bound of every wait
+  unsigned long long* prof;    // nullable: [nl + 1][PIPE_PHASES] summed phase times (ns), tokens >= prof_from
+  int prof_from;
   int withhold_stage;          // test hook: this layer stage never hands its residual on (-1: none)
 };
 

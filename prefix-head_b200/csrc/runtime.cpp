@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -123,6 +124,7 @@ struct gem_model {
   std::string pipe_why;  // why the pipeline is not used, for gem_get_schedule
   unsigned long long wait_ns = 2000000000ull;  // bound of every device-side wait
   int withhold_stage = -1;                     // failure-detection test hook
+  unsigned long long* prof = nullptr;          // per-stage phase times of pipelined runs (nullable)
   // graphs
   cudaGraphExec_t score_graph[2] = {nullptr, nullptr};
   int64_t graph_kernels[2] = {-1, -1};
@@ -283,6 +285,7 @@ struct gem_model {
     else if (!coop) pipe_why = "no cooperative launch";
     else if (nh > 16 || nh + nkv > 15 || hd > 256) pipe_why = "head counts";
     else if (nl + 1 > sms) pipe_why = "more layers than SMs";
+    else if (((nh + 2 * nkv) * hd) % 16 || d % 16 || ff % 32) pipe_why = "projection rows not in 16-row groups";
     return pipe_why.empty();
   }
 
@@ -330,6 +333,30 @@ struct gem_model {
     P.scratch = alloc<float>(P.scratch_stride * nl);
     P.head_scratch = alloc<float>((size_t)k + 2 * per);
     P.err = err;
+    P.checks = std::getenv("GEM_PIPELINE_CHECKS") ? 1 : 0;  // index self-checks (debugging aid)
+    // weight ring: a slot holds one 16-row group of the widest projection (plus its scales)
+    int max_stride = 0, max_sbytes = 0;
+    for (const MatView* w : {&layers[0].qkv.v, &layers[0].o.v, &layers[0].gu.v, &layers[0].down.v}) {
+      int rb = w->cols * w->bits / 8;
+      max_stride = std::max(max_stride, rb + 32);
+      max_sbytes = std::max(max_sbytes, w->bits == 16 ? 0 : (w->cols / 32) * (w->scale_f32 ? 4 : 2));
+    }
+    P.slot_scale_off = 16 * max_stride;
+    P.slot_bytes = (16 * max_stride + 16 * max_sbytes + 127) / 128 * 128;
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    P.ring_slots = 0;
+    for (int ns = 8; ns >= 2; --ns) {
+      P.ring_slots = ns;
+      if (pipe_smem_bytes(P) <= (size_t)optin) break;
+      P.ring_slots = 0;
+    }
+    // The shared-memory weight ring measured slower than direct loads on the 270M workload (7.2k vs
+    // 10.6k tokens/s): its refills arrive in bursts that slow the latency-bound phases around them.
+    // It stays available for tuning (GEM_PIPE_RING_SLOTS=n) and is off by default.
+    int want = 0;
+    if (const char* e = std::getenv("GEM_PIPE_RING_SLOTS")) want = std::max(0, std::atoi(e));
+    P.ring_slots = std::min(P.ring_slots, want);
     pipe_smem = std::max(pipe_smem_bytes(P), (size_t)120 * 1024);  // > half an SM: one CTA per SM
     pipe_ready = true;
   }
@@ -343,6 +370,8 @@ struct gem_model {
     P.toks = toks_d, P.n = (int)n, P.base_pos = (int)base_pos, P.lp_out = lp_d, P.am_out = am_d, P.h_last = h;
     P.wait_ns = wait_ns;
     P.withhold_stage = withhold_stage;
+    P.prof = prof;
+    P.prof_from = 16;
     ck(cudaMemsetAsync(P.ready, 0, (size_t)(nl + 1) * PIPE_RING * sizeof(unsigned), st), "memset");
     ck(cudaMemsetAsync(P.consumed, 0, (size_t)(nl + 1) * sizeof(unsigned), st), "memset");
     ck(cudaMemsetAsync(P.bar, 0, (size_t)(nl + 1) * 32 * sizeof(unsigned), st), "memset");
@@ -724,6 +753,37 @@ int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas) {
   }
   if (!ok && m->pipe_why.empty()) m->pipe_why = head == 1 ? "sequential schedule requested" : "full head";
   g_last_error = ok ? std::string("pipelined") : m->pipe_why;
+  API_END
+}
+
+int gem_set_profiling(gem_model* m, int on) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  if (on && !m->prof) m->prof = m->alloc<unsigned long long>((size_t)(m->nl + 1) * PIPE_PHASES);
+  if (on) ck(cudaMemsetAsync(m->prof, 0, (size_t)(m->nl + 1) * PIPE_PHASES * 8, m->st), "memset");
+  if (!on) m->prof = nullptr;  // the buffer stays owned by the model
+  m->sync();
+  API_END
+}
+
+int gem_get_phase_profile(gem_model* m, double* layer_us, int n_layer, double* head_us, int n_head) {
+  API_BEGIN
+  if (!m || !m->prof) throw Error(GEM_E_STATE, "profiling is off");
+  m->sync();
+  std::vector<unsigned long long> h((size_t)(m->nl + 1) * PIPE_PHASES);
+  ck(cudaMemcpy(h.data(), m->prof, h.size() * 8, cudaMemcpyDeviceToHost), "profile");
+  for (int i = 0; i < n_layer && i < PIPE_PHASES - 1; ++i) {
+    double sum = 0, cnt = 0;
+    for (int l = 0; l < m->nl; ++l) {
+      sum += (double)h[(size_t)l * PIPE_PHASES + i];
+      cnt += (double)h[(size_t)l * PIPE_PHASES + PIPE_PHASES - 1];
+    }
+    layer_us[i] = cnt > 0 ? sum / cnt / 1000.0 : 0.0;
+  }
+  const unsigned long long* hh = &h[(size_t)m->nl * PIPE_PHASES];
+  for (int i = 0; i < n_head && i < PIPE_PHASES - 1; ++i)
+    head_us[i] = hh[PIPE_PHASES - 1] ? (double)hh[i] / (double)hh[PIPE_PHASES - 1] / 1000.0 : 0.0;
   API_END
 }
 

@@ -69,6 +69,8 @@ def lib():
     L.gem_get_stream.argtypes = [vp, C.POINTER(vp)]
     L.gem_set_schedule.argtypes = [vp, C.c_int]
     L.gem_test_withhold_stage.argtypes = [vp, C.c_int, C.c_int]
+    L.gem_set_profiling.argtypes = [vp, C.c_int]
+    L.gem_get_phase_profile.argtypes = [vp, C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_double), C.c_int]
     L.gem_get_schedule.argtypes = [vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.gem_set_numerics.argtypes = [vp, C.c_int, C.c_int]
     L.gem_forward.argtypes = [vp, C.c_uint32, C.c_uint32, _f32p]
@@ -159,6 +161,20 @@ class Gemma:
     def test_withhold_stage(self, stage: int, wait_ms: int = 2000):
         """Failure-detection hook: layer stage `stage` withholds its output (-1 restores normal runs)."""
         _check(lib().gem_test_withhold_stage(self._h, stage, wait_ms))
+
+    LAYER_PHASES = ["wait", "attn_norm", "qkv", "bar1", "qknorm+scores", "bar2", "softmax+pv", "bar3", "combine+o",
+                    "bar4", "norms", "gate_up", "bar5", "down", "bar6", "handoff"]
+    HEAD_PHASES = ["wait", "norm", "classes+block", "bar1", "top_block", "bar2"]
+
+    def set_profiling(self, on: bool = True):
+        _check(lib().gem_set_profiling(self._h, 1 if on else 0))
+
+    def phase_profile(self):
+        """Mean us per token per phase of pipelined scoring: (layer stages, head stage)."""
+        la = (C.c_double * 16)()
+        ha = (C.c_double * 6)()
+        _check(lib().gem_get_phase_profile(self._h, la, 16, ha, 6))
+        return dict(zip(self.LAYER_PHASES, [round(v, 3) for v in la])), dict(zip(self.HEAD_PHASES, [round(v, 3) for v in ha]))
 
     def reset(self, seq: int = 0):
         _check(lib().gem_reset(self._h, seq))
