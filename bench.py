@@ -188,7 +188,7 @@ def main():
         return run_reference(args)
     import torch
     import torch.distributed as dist
-    from gem_b200 import EXACT, FAST, FULL, TWO_LEVEL, Gemma, synth
+    from gem_b200 import EXACT, FAST, FULL, PARALLEL, TWO_LEVEL, Gemma, synth
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -247,28 +247,14 @@ def main():
     tokens = SEQ_TOKENS * args.steps * world
     value = tokens / (ms_max / 1e3)
     info = g.refresh_info()
-    pipelined, G, GH, why = g.schedule(TWO_LEVEL)
-    kpt = info["kernels_per_token_twolevel"]
-
-    # roofline of the token step (a CUDA graph per token): algorithmic bytes per token / time per token
+    kind, kind_why = g.schedule_kind(TWO_LEVEL)
+    launches_per_step = g.last_launches()
     am_h = am_d.cpu().numpy().astype(np.uint32)
-    order = np.fromfile(str(mf.twolevel) + ".order", dtype="<u4")
-    per = info["per"]
-    cls_of = np.empty(g.vocab, np.int64)
-    cls_of[order] = np.arange(len(order)) // per
-    extra = float(np.mean(cls_of[am_h] != cls_of[toks_h[1:]]))
-    npos = n_pos_schedule(info, SEQ_TOKENS)
-    bpt = bytes_per_token(info, npos, extra)
-    per_token_s = (ms_max / 1e3) / (SEQ_TOKENS * args.steps)
-    peak, peak_kind = hbm_peak()
-    achieved = bpt / per_token_s / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "dram_bytes_per_token.txt"
-    if tf.exists():
-        for ln in tf.read_text().splitlines():
-            if ln.startswith(f"{args.numerics} two-level:"):
-                traffic = float(ln.split(":")[1].split()[0])
-
+    clocks = clk.summary()
+    if kind == PARALLEL:
+        roofline, sched = parallel_roofline(g, torch, step, info, ms_max / args.steps, clocks, args)
+    else:
+        roofline, sched = token_roofline(g, info, mf, am_h, toks_h, ms_max / args.steps, args, kind)
     # ---- e2e: the host-buffer entry point (H2D token ids, D2H log-probs + argmax every step) ----
     barrier()
     torch.cuda.synchronize()
@@ -290,7 +276,6 @@ def main():
         extras = run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf)
 
     if rank == 0:
-        clocks = clk.summary()
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
@@ -300,17 +285,12 @@ def main():
                        "model": "gemma3-270m geometry (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "
                                 "random init N(0,0.02) quantized to Q8_0",
                        "global_batch": world, "seq_len": SEQ_TOKENS, "parallelism": f"dp{world} (one sequence per GPU)",
-                       "l2": "flushed (256 MiB write) before every step; the 512 tokens of a step re-read the same weights"},
-            "schedule": ({"kind": "layer-pipelined persistent kernel", "ctas_per_layer": G, "head_ctas": GH}
-                         if pipelined else {"kind": "CUDA graph per token", "why": why}),
-            "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": round(achieved, 1), "peak": peak,
-                         "peak_kind": peak_kind, "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": ("k_pipe_score (one launch per 512-token step)" if pipelined
-                                    else f"token step (CUDA graph of {kpt} kernels)"),
-                         "algorithmic_bytes_per_token": int(bpt)},
+                       "l2": "flushed (256 MiB write) before every step"},
+            "schedule": sched,
+            "roofline": roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": (SEQ_TOKENS + 1) * 4,
                     "d2h_bytes_per_step": SEQ_TOKENS * 8},
-            "gpu_launches": (2 * args.steps if pipelined else int(kpt * SEQ_TOKENS * args.steps) if kpt > 0 else None),
+            "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks,
         }
         line.update(extras)
@@ -318,6 +298,78 @@ def main():
     g.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def body_weights(info):
+    d, nl, nh, nkv, hd, ff = (info[k] for k in ("d", "layers", "n_heads", "n_kv_heads", "head_dim", "ffn"))
+    return nl * ((nh + 2 * nkv) * hd * d + d * nh * hd + 2 * ff * d + d * ff)
+
+
+def gemm_traffic():
+    """DRAM bytes per step of the exact matrix products from the committed ncu summary, if present."""
+    tf = ROOT / "profiles" / "dram_bytes_per_token.txt"
+    if tf.exists():
+        for ln in tf.read_text().splitlines():
+            if ln.startswith("k_seq_gemm per step:"):
+                return float(ln.split(":")[1].split()[0])
+    return None
+
+
+def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
+    """Roofline of the dominant kernel of parallel scoring, the exact int8 matrix product (k_seq_gemm).
+
+    It is bound by CUDA-core issue, not by HBM or tensor cores: the reference's rounding (one fp32 FMA
+    per 32-block per lane, q8.rs:248-292) leaves at least three instructions per int8 weight pair and
+    position (the pair dot, its exact conversion to fp32, the FMA). The peak is that floor at the SM
+    clock: SMs x 128 lanes x clock / 3 pairs per second, 2 multiply-adds per pair, 2 ops each."""
+    g.set_profiling(True)
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    prof = g.parallel_profile()
+    g.set_profiling(False)
+    gemm_us = prof["qkv"] + prof["o"] + prof["gate_up"] + prof["down"]
+    ops = 2.0 * body_weights(info) * SEQ_TOKENS
+    achieved = ops / (gemm_us * 1e-6) / 1e12
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    peak = sms * 128 * mhz * 1e6 / 3 * 4 / 1e12
+    hbm, hbm_kind = hbm_peak()
+    alg_bytes = info["body_bytes"] + info["classes"] * info["d"] * 4
+    roof = {"bound": "alu", "unit": "TOP/s", "achieved": round(achieved, 2), "peak": round(peak, 2),
+            "peak_kind": f"derived: {sms} SMs x 128 lanes x {mhz:.0f} MHz / 3 instructions per int8 pair x 4 ops",
+            "frac": round(achieved / peak, 4), "traffic": gemm_traffic(),
+            "kernel": "k_seq_gemm (4 launches per layer, 72 per step)", "ops_per_step": ops,
+            "kernel_ms_per_step": round(gemm_us / 1e3, 3), "share_of_step": round(gemm_us / 1e3 / ms_step, 3),
+            "hbm_view": {"algorithmic_bytes_per_step": alg_bytes, "achieved_GB_s": round(alg_bytes / (ms_step * 1e-3) / 1e9, 1),
+                         "peak": hbm, "peak_kind": hbm_kind},
+            "tensor_view": {"bf16_peak_tflops": peaks().get("bf16_tflops"),
+                            "note": "the reference's per-block fp32 FMA order cannot be reproduced by tensor-core accumulation"}}
+    sched = {"kind": "sequence-parallel (every position of the sequence through each layer together)",
+             "groups_us_per_step": prof}
+    return roof, sched
+
+
+def token_roofline(g, info, mf, am_h, toks_h, ms_step, args, kind):
+    """HBM roofline of per-token scoring: algorithmic bytes per token / time per token."""
+    from gem_b200 import TWO_LEVEL
+    order = np.fromfile(str(mf.twolevel) + ".order", dtype="<u4")
+    per = info["per"]
+    cls_of = np.empty(g.vocab, np.int64)
+    cls_of[order] = np.arange(len(order)) // per
+    extra = float(np.mean(cls_of[am_h] != cls_of[toks_h[1:]]))
+    bpt = bytes_per_token(info, n_pos_schedule(info, SEQ_TOKENS), extra)
+    per_token_s = ms_step / 1e3 / SEQ_TOKENS
+    peak, peak_kind = hbm_peak()
+    achieved = bpt / per_token_s / 1e9
+    pipelined, G, GH, why = g.schedule(TWO_LEVEL)
+    roof = {"bound": "hbm", "unit": "GB/s", "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+            "frac": round(achieved / peak, 4), "traffic": None,
+            "kernel": "k_pipe_score (one launch per step)" if pipelined else "token step (a CUDA graph per token)",
+            "algorithmic_bytes_per_token": int(bpt)}
+    sched = ({"kind": "layer-pipelined persistent kernel", "ctas_per_layer": G, "head_ctas": GH} if pipelined
+             else {"kind": "CUDA graph per token", "why": why})
+    return roof, sched
 
 
 def time_dev(torch, stream, fn, iters, flush):
@@ -335,16 +387,22 @@ def time_dev(torch, stream, fn, iters, flush):
 def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     """Secondary figures: the full head end to end, the head microbenchmark (full 262144x640 GEMV with
     fused log-sum-exp vs the two-level head, batch 1 and 64) and the CPU baseline."""
-    from gem_b200 import AUTO, FULL, SEQUENTIAL, TWO_LEVEL, synth
+    from gem_b200 import AUTO, FULL, PIPELINED, SEQUENTIAL, TWO_LEVEL, synth
     from oracle import oracle as orc
     out = {}
-    # the same workload with each token finishing before the next starts (a CUDA graph per token)
-    g.set_schedule(SEQUENTIAL)
-    g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(), am_d.data_ptr())
-    ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(), am_d.data_ptr()),
-                  2, flush)
-    out["sequential"] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
-                         "schedule": "one CUDA graph per token"}
+    mf_info = g.refresh_info()
+    # the same workload scored token after token: as a layer-pipelined wavefront (one kernel) and with
+    # each token finishing before the next starts (a CUDA graph per token)
+    for name, sch, iters in (("pipelined", PIPELINED, 3), ("sequential", SEQUENTIAL, 1)):
+        g.set_schedule(sch)
+        g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(), am_d.data_ptr())
+        ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(),
+                                                         am_d.data_ptr()), iters, flush)
+        am_h = am_d.cpu().numpy().astype(np.uint32)
+        toks_h = toks_d.cpu().numpy().astype(np.uint32)
+        roof, sched = token_roofline(g, mf_info, mf, am_h, toks_h, ms, args, sch)
+        out[name] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+                     "schedule": sched, "roofline": roof}
     g.set_schedule(AUTO)
     # full head, same sequence
     g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr())

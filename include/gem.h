@@ -78,24 +78,39 @@ int gem_get_info(const gem_model* m, gem_info* out);
  *   quantization flips, within the spread between the reference's own AVX2 and AVX-512 paths. */
 enum { GEM_NUMERICS_EXACT = 0, GEM_NUMERICS_FAST = 1 };
 int gem_set_numerics(gem_model* m, int mode, int ref_threads);
-/* How gem_score / gem_score_dev run the two-level loop. GEM_SCHEDULE_AUTO (default): with exact
- * numerics and a loaded two-level head, as one layer-pipelined kernel - each decoder layer and the
- * head own a group of SMs and consecutive tokens flow through them as a wavefront; every token's
- * arithmetic and weight reads are those of the per-token forward, so results are identical.
- * GEM_SCHEDULE_SEQUENTIAL: one CUDA graph per token, each token finishing before the next starts. */
-enum { GEM_SCHEDULE_AUTO = 0, GEM_SCHEDULE_SEQUENTIAL = 1 };
+/* How gem_score / gem_score_dev run the scoring loop. With exact numerics every schedule gives the
+ * same results (each position's arithmetic is that of the per-token forward); they differ in how
+ * positions overlap. PARALLEL always computes with exact numerics.
+ * GEM_SCHEDULE_SEQUENTIAL: one CUDA graph per token, each token finishing before the next starts.
+ * GEM_SCHEDULE_PIPELINED (two-level head, exact numerics): one layer-pipelined kernel - each decoder
+ *   layer and the head own a group of SMs and consecutive tokens flow through them as a wavefront.
+ * GEM_SCHEDULE_PARALLEL: the tokens are known in advance, so all positions of a chunk (up to 1024)
+ *   go through each layer together; the K/V rows of a chunk are written before its attention reads
+ *   them. The projections become exact int8 matrix products that read each weight once per chunk.
+ * GEM_SCHEDULE_AUTO (default): PARALLEL where the model supports it, else PIPELINED for the
+ *   two-level head, else SEQUENTIAL. */
+enum { GEM_SCHEDULE_AUTO = 0, GEM_SCHEDULE_SEQUENTIAL = 1, GEM_SCHEDULE_PIPELINED = 2, GEM_SCHEDULE_PARALLEL = 3 };
 int gem_set_schedule(gem_model* m, int schedule);
 /* Whether scoring with `head` (0 full, 1 two-level) runs pipelined; stages_ctas (nullable, 2 ints)
  * receives CTAs per layer stage and for the head stage. gem_last_error() then holds the reason. */
 int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas);
+/* The schedule (SEQUENTIAL, PIPELINED or PARALLEL) that scoring with `head` runs under the current
+ * setting; gem_last_error() then names it, or why a faster one is not used. */
+int gem_get_schedule_kind(gem_model* m, int head, int* kind);
 /* Phase profile of pipelined scoring, gem's GEM_PROFILE (main.rs:312-317) on the device: while on,
  * CTA 0 of every stage timestamps its phases; gem_get_phase_profile returns mean microseconds per
  * token per phase, averaged over layer stages (16 phases: input wait, attn norm, q/k/v, barrier,
  * qk-norm + scores, barrier, softmax + P.V, barrier, combine + o, barrier, norms, gate/up, barrier,
- * down, barrier, hand-off) and for the head stage (6: input wait, norm, classes + target block,
- * barrier, top block, barrier). Turning it on clears the sums. */
+ * down, barrier, hand-off) and for the head stage (6: input wait, final norm + class logits + target
+ * block, barrier, class selection + top block, barrier, argmax). Turning it on clears the sums. */
 int gem_set_profiling(gem_model* m, int on);
 int gem_get_phase_profile(gem_model* m, double* layer_us, int n_layer, double* head_us, int n_head);
+/* Profile of parallel scoring (while profiling is on): mean device microseconds per scoring call in
+ * each of 9 launch groups, timed with events between them - embedding, norms, q/k/v product,
+ * attention, o product, gate/up product, gate, down product, head. No counterpart in the reference. */
+int gem_get_parallel_profile(gem_model* m, double* us, int n);
+/* Kernels launched by the last scoring call (gem_score / gem_score_dev). */
+int gem_get_last_launches(gem_model* m, int64_t* n);
 /* Failure-detection test hook for the pipelined schedule: layer stage `stage` (-1: none) computes but
  * never hands its residual on, so the next stage's wait, bounded by wait_ms, expires; the scoring call
  * then returns GEM_E_TIMEOUT and the model stays usable. wait_ms also bounds every device-side wait

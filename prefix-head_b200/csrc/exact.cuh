@@ -141,5 +141,60 @@ __device__ __forceinline__ void quant_block_warp_x(float v, int lane, int8_t* q,
   if (lane == 0) *s = d;
 }
 
+// QK-norm, RoPE, q scale, KV append for one token and kv group `g` (the body of the per-token
+// kernel below and of the sequence-parallel one): raw projections `qkv`, position `pos`, normalised
+// queries to `qn` ([nh][hd] of this token). `smp` holds (G + 2) * hd floats, `s_r` G + 1.
+__device__ inline void attn_prep_token(const AttnArgs& A, const float* qkv, uint32_t pos, int g, float* qn, float* smp,
+                                float* s_r) {
+  const int hd = A.hd, G = A.nh / A.nkv;
+  float* sq = smp;           // G*hd
+  float* sk = sq + G * hd;   // hd
+  float* sv = sk + hd;       // hd
+  const int rw = A.nkv * hd;
+  const float* bq = A.bqkv;
+  for (int j = threadIdx.x; j < G * hd; j += blockDim.x) {
+    size_t i = (size_t)g * G * hd + j;
+    sq[j] = bq ? add(qkv[i], bq[i]) : qkv[i];
+  }
+  for (int j = threadIdx.x; j < hd; j += blockDim.x) {
+    size_t ik = (size_t)A.nh * hd + g * hd + j, iv = (size_t)A.nh * hd + rw + g * hd + j;
+    sk[j] = bq ? add(qkv[ik], bq[ik]) : qkv[ik];
+    sv[j] = bq ? add(qkv[iv], bq[iv]) : qkv[iv];
+  }
+  __syncthreads();
+  // per-head sequential sums of squares, one thread per head (+1 for k)
+  if ((int)threadIdx.x <= G) {
+    const float* v = threadIdx.x < (unsigned)G ? sq + threadIdx.x * hd : sk;
+    const float* nw = threadIdx.x < (unsigned)G ? A.q_norm : A.k_norm;
+    s_r[threadIdx.x] = nw ? rms_r_exact(seq_sumsq(v, hd), hd, A.eps) : 1.0f;
+  }
+  __syncthreads();
+  const float* sn = A.rope_sin + (size_t)pos * (hd / 2);
+  const float* cs = A.rope_cos + (size_t)pos * (hd / 2);
+  const int half = hd / 2;
+  for (int t = threadIdx.x; t < (G + 1) * half; t += blockDim.x) {
+    int h = t / half, i = t % half;
+    float* v = h < G ? sq + h * hd : sk;
+    const float* nw = h < G ? A.q_norm : A.k_norm;
+    float r = s_r[h];
+    float a = v[i], b = v[i + half];
+    if (nw) {  // rmsnorm_inplace: v *= r * w
+      a = mul(a, mul(r, nw[i]));
+      b = mul(b, mul(r, nw[i + half]));
+    }
+    float na = sub(mul(a, cs[i]), mul(b, sn[i]));  // rope (model.rs:97-104)
+    float nb = add(mul(a, sn[i]), mul(b, cs[i]));
+    if (h < G) {  // q * 1/sqrt(hd) (model.rs:317-324)
+      na = mul(na, A.qscale);
+      nb = mul(nb, A.qscale);
+      qn[(size_t)(g * G + h) * hd + i] = na;
+      qn[(size_t)(g * G + h) * hd + i + half] = nb;
+    } else {
+      A.kcache[(size_t)pos * rw + g * hd + i] = na;  // KV append (model.rs:333-335)
+      A.kcache[(size_t)pos * rw + g * hd + i + half] = nb;
+    }
+  }
+  for (int j = threadIdx.x; j < hd; j += blockDim.x) A.vcache[(size_t)pos * rw + g * hd + j] = sv[j];
+}
 
 }  // namespace gem

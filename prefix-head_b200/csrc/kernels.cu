@@ -14,22 +14,6 @@ namespace gem {
 // in the (possibly class-permuted) output matrix.
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
-__device__ __forceinline__ float weight_at(const MatView& w, size_t r, int j) {  // q8.rs:112-126
-  if constexpr (BITS == 16) {
-    return __half2float(((const __half*)w.q)[r * w.cols + j]);
-  } else if constexpr (BITS == 8) {
-    float s = ld_scale((const ST*)w.s, (r * w.cols + j) / 32);
-    return mul((float)((const int8_t*)w.q)[r * w.cols + j], s);
-  } else {
-    float s = ld_scale((const ST*)w.s, (r * w.cols + j) / 32);
-    int blk = j / 32, k = j % 32;
-    uint8_t byte = ((const uint8_t*)w.q)[r * w.cols / 2 + blk * 16 + (k % 16)];
-    int nib = k < 16 ? (byte & 15) : (byte >> 4);
-    return mul((float)(nib - 8), s);
-  }
-}
-
-template <int BITS, typename ST>
 __global__ void k_embed(MatView head, const uint32_t* row_of, const StepCur* cur, float scale, float* x) {
   uint32_t tok = cur->tok;
   size_t row = row_of ? row_of[tok] : tok;

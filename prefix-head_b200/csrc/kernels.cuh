@@ -23,6 +23,26 @@ struct MatView {
   int rows = 0, cols = 0, bits = 8, scale_f32 = 0;
 };
 
+#ifdef __CUDACC__
+// Mat::weight (q8.rs:112-126): the dequantized weight at row r, column j -- the bit-exact dequant
+// definition (q * s in one fp32 rounding; nibble - 8 for Q4_0; the f16 value for F16).
+template <int BITS, typename ST>
+__device__ __forceinline__ float weight_at(const MatView& w, size_t r, int j) {  // q8.rs:112-126
+  if constexpr (BITS == 16) {
+    return __half2float(((const __half*)w.q)[r * w.cols + j]);
+  } else if constexpr (BITS == 8) {
+    float s = ld_scale((const ST*)w.s, (r * w.cols + j) / 32);
+    return mul((float)((const int8_t*)w.q)[r * w.cols + j], s);
+  } else {
+    float s = ld_scale((const ST*)w.s, (r * w.cols + j) / 32);
+    int blk = j / 32, k = j % 32;
+    uint8_t byte = ((const uint8_t*)w.q)[r * w.cols / 2 + blk * 16 + (k % 16)];
+    int nib = k < 16 ? (byte & 15) : (byte >> 4);
+    return mul((float)(nib - 8), s);
+  }
+}
+#endif
+
 // Token, position, target and output slot of the step being run; written by k_begin_step (scoring
 // loop) or by a host copy (single-token calls).
 struct StepCur {
@@ -109,5 +129,21 @@ void launch_attn_exact(const AttnArgs& A, float* qn, float* scores, int sstride,
 void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t st);
 void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, int block_ctas, cudaStream_t st);
 void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_of, float* top_inner, cudaStream_t st);
+
+// Sequence-parallel scoring (seq.cu): every position of a chunk through one layer at a time, with the
+// exact per-position arithmetic above. Activations are [T][n] row-major, scales [T][n/32].
+void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, float scale, float* x, int* err,
+                      cudaStream_t st);
+void launch_seq_norm(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d, int T,
+                     int8_t* aq, float* as, float* xn_out, cudaStream_t st);
+bool seq_gemm_supported(const MatView& w);
+void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, cudaStream_t st);
+void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uint32_t pos0, float* qn, float* scores,
+                     int sstride, int threads, int8_t* aq, float* as, cudaStream_t st);
+void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st);
+void launch_seq_class_logits(const float* A, const float* b, int k, const float* h, int d, int T, float* cl,
+                             cudaStream_t st);
+void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, float* lp, uint32_t* am, int* err,
+                             cudaStream_t st);
 
 }  // namespace gem

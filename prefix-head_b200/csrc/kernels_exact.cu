@@ -90,60 +90,11 @@ __global__ void k_residual_norm_quant_exact(float* x, const float* delta, const 
 // ------------------------------------------------------------------------------------------------
 // Attention, exact (model.rs:316-383).
 // ------------------------------------------------------------------------------------------------
-// QK-norm, RoPE, q scale, KV append. One CTA per kv group; writes normalised q to qn.
+// One CTA per kv group; writes normalised q to qn.
 __global__ void k_attn_prep_exact(AttnArgs A, float* qn) {
   extern __shared__ __align__(16) float smp[];
-  const int hd = A.hd, G = A.nh / A.nkv, g = blockIdx.x;
-  float* sq = smp;           // G*hd
-  float* sk = sq + G * hd;   // hd
-  float* sv = sk + hd;       // hd
-  __shared__ float s_r[9];
-  const uint32_t pos = A.cur->pos;
-  const int rw = A.nkv * hd;
-  const float* bq = A.bqkv;
-  for (int j = threadIdx.x; j < G * hd; j += blockDim.x) {
-    size_t i = (size_t)g * G * hd + j;
-    sq[j] = bq ? add(A.qkv[i], bq[i]) : A.qkv[i];
-  }
-  for (int j = threadIdx.x; j < hd; j += blockDim.x) {
-    size_t ik = (size_t)A.nh * hd + g * hd + j, iv = (size_t)A.nh * hd + rw + g * hd + j;
-    sk[j] = bq ? add(A.qkv[ik], bq[ik]) : A.qkv[ik];
-    sv[j] = bq ? add(A.qkv[iv], bq[iv]) : A.qkv[iv];
-  }
-  __syncthreads();
-  // per-head sequential sums of squares, one thread per head (+1 for k)
-  if ((int)threadIdx.x <= G) {
-    const float* v = threadIdx.x < (unsigned)G ? sq + threadIdx.x * hd : sk;
-    const float* nw = threadIdx.x < (unsigned)G ? A.q_norm : A.k_norm;
-    s_r[threadIdx.x] = nw ? rms_r_exact(seq_sumsq(v, hd), hd, A.eps) : 1.0f;
-  }
-  __syncthreads();
-  const float* sn = A.rope_sin + (size_t)pos * (hd / 2);
-  const float* cs = A.rope_cos + (size_t)pos * (hd / 2);
-  const int half = hd / 2;
-  for (int t = threadIdx.x; t < (G + 1) * half; t += blockDim.x) {
-    int h = t / half, i = t % half;
-    float* v = h < G ? sq + h * hd : sk;
-    const float* nw = h < G ? A.q_norm : A.k_norm;
-    float r = s_r[h];
-    float a = v[i], b = v[i + half];
-    if (nw) {  // rmsnorm_inplace: v *= r * w
-      a = mul(a, mul(r, nw[i]));
-      b = mul(b, mul(r, nw[i + half]));
-    }
-    float na = sub(mul(a, cs[i]), mul(b, sn[i]));  // rope (model.rs:97-104)
-    float nb = add(mul(a, sn[i]), mul(b, cs[i]));
-    if (h < G) {  // q * 1/sqrt(hd) (model.rs:317-324)
-      na = mul(na, A.qscale);
-      nb = mul(nb, A.qscale);
-      qn[(size_t)(g * G + h) * hd + i] = na;
-      qn[(size_t)(g * G + h) * hd + i + half] = nb;
-    } else {
-      A.kcache[(size_t)pos * rw + g * hd + i] = na;  // KV append (model.rs:333-335)
-      A.kcache[(size_t)pos * rw + g * hd + i + half] = nb;
-    }
-  }
-  for (int j = threadIdx.x; j < hd; j += blockDim.x) A.vcache[(size_t)pos * rw + g * hd + j] = sv[j];
+  __shared__ float s_r[17];
+  attn_prep_token(A, A.qkv, A.cur->pos, blockIdx.x, qn, smp, s_r);
 }
 
 // scores[h][i] = dot512(q_h, k_(lo+i)) for every head and position (model.rs:344-353).

@@ -125,6 +125,23 @@ struct gem_model {
   unsigned long long wait_ns = 2000000000ull;  // bound of every device-side wait
   int withhold_stage = -1;                     // failure-detection test hook
   unsigned long long* prof = nullptr;          // per-stage phase times of pipelined runs (nullable)
+  // sequence-parallel scoring (seq.cu): buffers for up to seq_cap positions
+  static constexpr int kSeqChunk = 1024;  // positions per chunk
+  static constexpr int kHeadChunk = 256;  // positions per full-head logits pass
+  int seq_cap = 0, seq_sstride = 0, logits_cap = 0;
+  float *s_x = nullptr, *s_y = nullptr, *s_gu = nullptr, *s_dn = nullptr, *s_h = nullptr, *s_qn = nullptr,
+        *s_scores = nullptr, *s_logits = nullptr;
+  int8_t *s_aq = nullptr, *s_haq = nullptr;
+  float *s_as = nullptr, *s_has = nullptr;
+  std::string seq_why;  // why the sequence-parallel schedule is not used
+  // per-category device time of parallel scoring (gem_set_profiling): events between launch groups
+  enum { PAR_EMBED, PAR_NORM, PAR_QKV, PAR_ATTN, PAR_O, PAR_GU, PAR_GLU, PAR_DOWN, PAR_HEAD, PAR_CATS };
+  bool par_prof = false;
+  std::vector<cudaEvent_t> pev;
+  std::vector<int> pcat;
+  double par_us[PAR_CATS] = {};
+  int64_t par_calls = 0;
+  int64_t last_launches = 0;  // kernels the last scoring call launched
   // graphs
   cudaGraphExec_t score_graph[2] = {nullptr, nullptr};
   int64_t graph_kernels[2] = {-1, -1};
@@ -140,6 +157,7 @@ struct gem_model {
 
   ~gem_model() {
     if (st) cudaStreamSynchronize(st);
+    for (cudaEvent_t e : pev) cudaEventDestroy(e);
     for (auto& g : score_graph)
       if (g) cudaGraphExecDestroy(g);
     for (void* p : owned) cudaFree(p);
@@ -274,6 +292,150 @@ struct gem_model {
   }
   void enqueue_head(int which, float* lpo, uint32_t* amo) { run_head(which, haq, has, h, nullptr, 1, lpo, amo); }
 
+  // Can a whole sequence go through each layer at once (seq.cu)?
+  bool seq_supported() {
+    seq_why.clear();
+    const int G = nkv > 0 ? nh / nkv : 0;
+    if (G != 1 && G != 2 && G != 4 && G != 8) seq_why = "query heads per kv head not 1, 2, 4 or 8";
+    else if (hd % 16 || hd > 1024 || d % 32 || ff % 32 || (nh * hd) % 32) seq_why = "dimensions not in 32-blocks";
+    for (const Layer& L : layers)
+      for (const DevMat* w : {&L.qkv, &L.o, &L.gu, &L.down})
+        if (seq_why.empty() && !seq_gemm_supported(w->v)) seq_why = "body weights not Q8_0/Q4_0 with even block counts";
+    return seq_why.empty();
+  }
+  bool use_parallel() {
+    if (schedule != GEM_SCHEDULE_AUTO && schedule != GEM_SCHEDULE_PARALLEL) return false;
+    if (seq_supported()) return true;
+    if (schedule == GEM_SCHEDULE_PARALLEL) throw Error(GEM_E_STATE, "sequence-parallel schedule unavailable: " + seq_why);
+    return false;
+  }
+
+  void ensure_seq(int T) {
+    if (T <= seq_cap) return;
+    const size_t qkv_rows = (size_t)(nh + 2 * nkv) * hd;
+    const size_t wide = std::max({(size_t)d, (size_t)nh * hd, (size_t)ff});
+    s_x = alloc<float>((size_t)T * d);
+    s_y = alloc<float>((size_t)T * std::max(qkv_rows, (size_t)d));
+    s_gu = alloc<float>((size_t)T * 2 * ff);
+    s_dn = alloc<float>((size_t)T * d);
+    s_h = alloc<float>((size_t)T * d);
+    s_qn = alloc<float>((size_t)T * nh * hd);
+    seq_sstride = ctx;
+    s_scores = alloc<float>((size_t)T * nh * seq_sstride);
+    s_aq = alloc<int8_t>((size_t)T * wide);
+    s_as = alloc<float>((size_t)T * wide / 32);
+    s_haq = alloc<int8_t>((size_t)T * d);
+    s_has = alloc<float>((size_t)T * d / 32);
+    seq_cap = T;
+  }
+
+  // Head over T final hidden states (s_h, s_haq, s_has) with targets[0..T); returns the kernels launched.
+  int seq_head(int which, const uint32_t* targets, int T, float* lpo, uint32_t* amo) {
+    if (which == 1) {
+      ensure_head_batch(T);
+      launch_seq_class_logits(A, b, k, s_h, d, T, cl, st);
+      TwoLevelArgs TL = tl_args(s_haq, s_has, s_h, targets, lpo, amo);
+      TL.class_ctas = 0;
+      const int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
+      launch_tl_stage1_exact(TL, T, 0, block_ctas, st);
+      launch_tl_select(TL, T, top_of, st);
+      launch_tl_top_exact(TL, T, top_of, top_inner, st);
+      launch_tl_argmax(TL, T, top_of, top_inner, st);
+      return 5;
+    }
+    if (!seq_gemm_supported(head.v)) {  // F16 output matrix: the per-position exact head kernels
+      run_head(0, s_haq, s_has, s_h, targets, T, lpo, amo);
+      return 2;
+    }
+    const int hc = std::min(T, kHeadChunk);
+    if (hc > logits_cap) {
+      s_logits = alloc<float>((size_t)hc * vocab);
+      logits_cap = hc;
+    }
+    int launches = 0;
+    for (int h0 = 0; h0 < T; h0 += hc) {
+      const int n = std::min(hc, T - h0);
+      launch_seq_gemm(head.v, s_haq + (size_t)h0 * d, s_has + (size_t)h0 * d / 32, n, s_logits, vocab, st);
+      launch_seq_logit_reduce(s_logits, vocab, n, targets + h0, lpo + h0, amo ? amo + h0 : nullptr, err, st);
+      launches += 2;
+    }
+    return launches;
+  }
+
+  // Scoring with every position of a chunk going through each layer together: tokens toks_d[0..n]
+  // at positions base_pos.., log-probs of toks_d[i + 1] to lp_d[i].
+  // Records an event after the launches of category `cat` when profiling is on.
+  void par_mark(int cat) {
+    if (!par_prof) return;
+    const size_t i = pcat.size();
+    if (i >= pev.size()) {
+      cudaEvent_t e;
+      ck(cudaEventCreate(&e), "event");
+      pev.push_back(e);
+    }
+    ck(cudaEventRecord(pev[i], st), "event record");
+    pcat.push_back(cat);
+  }
+  void par_collect() {
+    if (!par_prof || pcat.empty()) return;
+    ck(cudaStreamSynchronize(st), "stream sync");
+    for (size_t i = 1; i < pcat.size(); ++i) {
+      float ms = 0;
+      ck(cudaEventElapsedTime(&ms, pev[i - 1], pev[i]), "event time");
+      par_us[pcat[i]] += ms * 1e3;
+    }
+    pcat.clear();
+    ++par_calls;
+  }
+
+  void score_parallel(const uint32_t* toks_d, size_t n, int which, uint32_t base_pos, float* lp_d, uint32_t* am_d) {
+    const int cap = (int)std::min<size_t>(n, kSeqChunk);
+    ensure_seq(cap);
+    const DevMat& E = untied ? emb : head;
+    const int qkv_rows = (nh + 2 * nkv) * hd;
+    int T = 0;
+    int64_t nk = 0;
+    pcat.clear();
+    par_mark(-1);
+    for (size_t c0 = 0; c0 < n; c0 += cap) {
+      T = (int)std::min<size_t>(cap, n - c0);
+      const uint32_t pos0 = base_pos + (uint32_t)c0;
+      launch_seq_embed(E.v, toks_d + c0, T, vocab, embed_scale, s_x, err, st);
+      par_mark(PAR_EMBED);
+      for (int l = 0; l < nl; ++l) {
+        const Layer& L = layers[l];
+        const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
+        launch_seq_norm(s_x, P ? s_dn : nullptr, P ? P->post_ffw : nullptr, L.attn_norm, eps, d, T, s_aq, s_as, nullptr, st);
+        par_mark(PAR_NORM);
+        launch_seq_gemm(L.qkv.v, s_aq, s_as, T, s_y, qkv_rows, st);
+        par_mark(PAR_QKV);
+        launch_seq_attn(attn_args(l, 0), s_y, qkv_rows, T, pos0, s_qn, s_scores, seq_sstride, ref_threads, s_aq, s_as, st);
+        par_mark(PAR_ATTN);
+        launch_seq_gemm(L.o.v, s_aq, s_as, T, s_y, d, st);
+        par_mark(PAR_O);
+        launch_seq_norm(s_x, s_y, L.post_attn, L.ffn_norm, eps, d, T, s_aq, s_as, nullptr, st);
+        par_mark(PAR_NORM);
+        launch_seq_gemm(L.gu.v, s_aq, s_as, T, s_gu, 2 * ff, st);
+        par_mark(PAR_GU);
+        launch_seq_glu_quant(s_gu, ff, T, silu ? 1 : 0, s_aq, s_as, sms, st);
+        par_mark(PAR_GLU);
+        launch_seq_gemm(L.down.v, s_aq, s_as, T, s_dn, d, st);
+        par_mark(PAR_DOWN);
+        nk += 11;  // 2 norms, 4 matrix products, 4 attention kernels, the gate
+      }
+      launch_seq_norm(s_x, s_dn, layers[nl - 1].post_ffw, out_norm, eps, d, T, s_haq, s_has, s_h, st);
+      par_mark(PAR_NORM);
+      nk += 2 + seq_head(which, toks_d + c0 + 1, T, lp_d + c0, am_d ? am_d + c0 : nullptr);
+      par_mark(PAR_HEAD);
+    }
+    last_launches = nk;
+    par_collect();
+    // the last position's final hidden state, for later single-token head calls
+    ck(cudaMemcpyAsync(h, s_h + (size_t)(T - 1) * d, (size_t)d * 4, cudaMemcpyDeviceToDevice, st), "h");
+    ck(cudaMemcpyAsync(haq, s_haq + (size_t)(T - 1) * d, (size_t)d, cudaMemcpyDeviceToDevice, st), "haq");
+    ck(cudaMemcpyAsync(has, s_has + (size_t)(T - 1) * (d / 32), (size_t)d / 32 * 4, cudaMemcpyDeviceToDevice, st), "has");
+  }
+
   // Can the two-level scoring loop run as one layer-pipelined kernel on this model and GPU?
   bool pipeline_supported() {
     pipe_why.clear();
@@ -363,7 +525,7 @@ struct gem_model {
 
   // The scoring loop as one pipelined kernel on device buffers (toks: n + 1 ids).
   bool try_pipeline(const uint32_t* toks_d, size_t n, uint32_t base_pos, float* lp_d, uint32_t* am_d) {
-    if (schedule == GEM_SCHEDULE_SEQUENTIAL || !pipeline_supported()) return false;
+    if (schedule == GEM_SCHEDULE_SEQUENTIAL || schedule == GEM_SCHEDULE_PARALLEL || !pipeline_supported()) return false;
     setup_pipeline();
     PipeArgs P = pipe;
     P.ref_threads = ref_threads;
@@ -736,7 +898,7 @@ int gem_set_numerics(gem_model* m, int mode, int ref_threads) {
 int gem_set_schedule(gem_model* m, int schedule) {
   API_BEGIN
   if (!m) throw Error(GEM_E_ARG, "null argument");
-  if (schedule != GEM_SCHEDULE_AUTO && schedule != GEM_SCHEDULE_SEQUENTIAL) throw Error(GEM_E_ARG, "unknown schedule");
+  if (schedule < GEM_SCHEDULE_AUTO || schedule > GEM_SCHEDULE_PARALLEL) throw Error(GEM_E_ARG, "unknown schedule");
   m->schedule = schedule;
   API_END
 }
@@ -744,8 +906,11 @@ int gem_set_schedule(gem_model* m, int schedule) {
 int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas) {
   API_BEGIN
   if (!m) throw Error(GEM_E_ARG, "null argument");
-  bool ok = head == 1 && m->schedule == GEM_SCHEDULE_AUTO && m->pipeline_supported();
+  const bool parallel = (m->schedule == GEM_SCHEDULE_AUTO || m->schedule == GEM_SCHEDULE_PARALLEL) && m->seq_supported();
+  bool ok = head == 1 && !parallel && (m->schedule == GEM_SCHEDULE_AUTO || m->schedule == GEM_SCHEDULE_PIPELINED) &&
+            m->pipeline_supported();
   if (ok) m->setup_pipeline();
+  if (parallel) m->pipe_why = "sequence-parallel schedule";
   if (pipelined) *pipelined = ok ? 1 : 0;
   if (stages_ctas) {
     stages_ctas[0] = ok ? m->pipe.G : 0;
@@ -756,6 +921,24 @@ int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas) {
   API_END
 }
 
+int gem_get_schedule_kind(gem_model* m, int head, int* kind) {
+  API_BEGIN
+  if (!m || !kind) throw Error(GEM_E_ARG, "null argument");
+  if (head != 0 && head != 1) throw Error(GEM_E_ARG, "head must be 0 (full) or 1 (two-level)");
+  if ((m->schedule == GEM_SCHEDULE_AUTO || m->schedule == GEM_SCHEDULE_PARALLEL) && m->seq_supported()) {
+    *kind = GEM_SCHEDULE_PARALLEL;
+    g_last_error = "sequence-parallel";
+  } else if (head == 1 && (m->schedule == GEM_SCHEDULE_AUTO || m->schedule == GEM_SCHEDULE_PIPELINED) &&
+             m->pipeline_supported()) {
+    *kind = GEM_SCHEDULE_PIPELINED;
+    g_last_error = "pipelined";
+  } else {
+    *kind = GEM_SCHEDULE_SEQUENTIAL;
+    g_last_error = !m->seq_why.empty() ? m->seq_why : m->pipe_why;
+  }
+  API_END
+}
+
 int gem_set_profiling(gem_model* m, int on) {
   API_BEGIN
   if (!m) throw Error(GEM_E_ARG, "null argument");
@@ -763,7 +946,25 @@ int gem_set_profiling(gem_model* m, int on) {
   if (on && !m->prof) m->prof = m->alloc<unsigned long long>((size_t)(m->nl + 1) * PIPE_PHASES);
   if (on) ck(cudaMemsetAsync(m->prof, 0, (size_t)(m->nl + 1) * PIPE_PHASES * 8, m->st), "memset");
   if (!on) m->prof = nullptr;  // the buffer stays owned by the model
+  m->par_prof = on != 0;
+  for (double& v : m->par_us) v = 0;
+  m->par_calls = 0;
   m->sync();
+  API_END
+}
+
+int gem_get_parallel_profile(gem_model* m, double* us, int n) {
+  API_BEGIN
+  if (!m || !us) throw Error(GEM_E_ARG, "null argument");
+  if (!m->par_prof) throw Error(GEM_E_STATE, "profiling is off");
+  for (int i = 0; i < n && i < gem_model::PAR_CATS; ++i) us[i] = m->par_calls ? m->par_us[i] / (double)m->par_calls : 0.0;
+  API_END
+}
+
+int gem_get_last_launches(gem_model* m, int64_t* n) {
+  API_BEGIN
+  if (!m || !n) throw Error(GEM_E_ARG, "null argument");
+  *n = m->last_launches;
   API_END
 }
 
@@ -868,7 +1069,13 @@ static void run_score(gem_model* m, size_t n, int head) {
     ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
     m->enqueue_body(0);
   }
+  if (m->use_parallel()) {
+    m->score_parallel(m->toks, n, head, (uint32_t)off, m->lp, m->am);
+    m->have_h = true;
+    return;
+  }
   if (head == 1 && m->try_pipeline(m->toks, n, (uint32_t)off, m->lp, m->am)) {
+    m->last_launches = 2;  // the pipelined kernel and the last hidden state's quantization
     m->have_h = true;
     return;
   }
@@ -904,6 +1111,7 @@ static void run_score(gem_model* m, size_t n, int head) {
     m->score_graph[head] = ge;
   }
   for (size_t i = 0; i < n; ++i) ck(cudaGraphLaunch(m->score_graph[head], m->st), "graph launch");
+  m->last_launches = m->graph_kernels[head] * (int64_t)n;
   m->have_h = true;
 }
 

@@ -72,6 +72,9 @@ def lib():
     L.gem_set_profiling.argtypes = [vp, C.c_int]
     L.gem_get_phase_profile.argtypes = [vp, C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_double), C.c_int]
     L.gem_get_schedule.argtypes = [vp, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]
+    L.gem_get_schedule_kind.argtypes = [vp, C.c_int, C.POINTER(C.c_int)]
+    L.gem_get_parallel_profile.argtypes = [vp, C.POINTER(C.c_double), C.c_int]
+    L.gem_get_last_launches.argtypes = [vp, C.POINTER(C.c_int64)]
     L.gem_set_numerics.argtypes = [vp, C.c_int, C.c_int]
     L.gem_forward.argtypes = [vp, C.c_uint32, C.c_uint32, _f32p]
     L.gem_full_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
@@ -97,7 +100,8 @@ def _p(a: np.ndarray, t):
 
 FULL, TWO_LEVEL = 0, 1
 EXACT, FAST = 0, 1
-AUTO, SEQUENTIAL = 0, 1
+AUTO, SEQUENTIAL, PIPELINED, PARALLEL = 0, 1, 2, 3
+SCHEDULE_NAMES = {SEQUENTIAL: "sequential", PIPELINED: "pipelined", PARALLEL: "parallel"}
 
 
 class Gemma:
@@ -148,8 +152,15 @@ class Gemma:
         _check(lib().gem_set_numerics(self._h, mode, ref_threads))
 
     def set_schedule(self, schedule: int = AUTO):
-        """AUTO: two-level scoring as one layer-pipelined kernel when supported; SEQUENTIAL: a graph per token."""
+        """SEQUENTIAL: a CUDA graph per token. PIPELINED: two-level scoring as one layer-pipelined kernel.
+        PARALLEL: every position of a chunk through each layer together. AUTO: the fastest supported."""
         _check(lib().gem_set_schedule(self._h, schedule))
+
+    def schedule_kind(self, head: int = TWO_LEVEL):
+        """(schedule that scoring with `head` runs, its name or why a faster one is not used)."""
+        k = C.c_int()
+        _check(lib().gem_get_schedule_kind(self._h, head, C.byref(k)))
+        return k.value, lib().gem_last_error().decode()
 
     def schedule(self, head: int = TWO_LEVEL):
         """(pipelined, ctas per layer stage, head ctas, reason)."""
@@ -164,7 +175,7 @@ class Gemma:
 
     LAYER_PHASES = ["wait", "attn_norm", "qkv", "bar1", "qknorm+scores", "bar2", "softmax+pv", "bar3", "combine+o",
                     "bar4", "norms", "gate_up", "bar5", "down", "bar6", "handoff"]
-    HEAD_PHASES = ["wait", "norm", "classes+block", "bar1", "top_block", "bar2"]
+    HEAD_PHASES = ["wait", "norm+classes+block", "bar1", "select+top_block", "bar2", "argmax"]
 
     def set_profiling(self, on: bool = True):
         _check(lib().gem_set_profiling(self._h, 1 if on else 0))
@@ -175,6 +186,20 @@ class Gemma:
         ha = (C.c_double * 6)()
         _check(lib().gem_get_phase_profile(self._h, la, 16, ha, 6))
         return dict(zip(self.LAYER_PHASES, [round(v, 3) for v in la])), dict(zip(self.HEAD_PHASES, [round(v, 3) for v in ha]))
+
+    PARALLEL_GROUPS = ["embed", "norm", "qkv", "attention", "o", "gate_up", "gate", "down", "head"]
+
+    def parallel_profile(self):
+        """Mean device us per scoring call in each launch group of parallel scoring (profiling on)."""
+        a = (C.c_double * 9)()
+        _check(lib().gem_get_parallel_profile(self._h, a, 9))
+        return dict(zip(self.PARALLEL_GROUPS, [round(v, 2) for v in a]))
+
+    def last_launches(self) -> int:
+        """Kernels launched by the last scoring call."""
+        n = C.c_int64()
+        _check(lib().gem_get_last_launches(self._h, C.byref(n)))
+        return n.value
 
     def reset(self, seq: int = 0):
         _check(lib().gem_reset(self._h, seq))

@@ -90,10 +90,13 @@ def test_forward_hidden_state_bit_exact(torch, isa, small):
         assert np.array_equal(hg.view(np.uint32), ho.view(np.uint32)), (i, np.abs(hg - ho).max())
 
 
+@pytest.mark.parametrize("schedule", ["sequential", "pipelined", "parallel"])
 @pytest.mark.parametrize("head", [FULL, TWO_LEVEL])
-def test_score_exact(torch, isa, small, head):
+def test_score_exact(torch, isa, small, head, schedule):
+    from gem_b200 import PARALLEL, PIPELINED, SEQUENTIAL
     g = Gemma(small.gguf, ctx=128)
     g.load_twolevel(small.twolevel)
+    g.set_schedule({"sequential": SEQUENTIAL, "pipelined": PIPELINED, "parallel": PARALLEL}[schedule])
     o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa="avx512")
     o.load_twolevel(small.twolevel)
     toks = synth.tokens(49, g.vocab, seed=5)
@@ -127,8 +130,10 @@ def test_head_batch_exact(torch, isa, small, threads, batch):
 
 @pytest.mark.parametrize("head", [FULL, TWO_LEVEL])
 def test_score_fast_within_reference_isa_spread(torch, isa, small, head):
+    from gem_b200 import SEQUENTIAL
     g = Gemma(small.gguf, ctx=128)
     g.set_numerics(FAST)
+    g.set_schedule(SEQUENTIAL)  # the parallel schedule always computes exactly
     g.load_twolevel(small.twolevel)
     toks = synth.tokens(49, g.vocab, seed=6)
     lp, am = g.score(toks, head)
@@ -147,9 +152,10 @@ def test_score_fast_within_reference_isa_spread(torch, isa, small, head):
 
 
 def test_pipelined_and_sequential_schedules_agree(torch, isa, small):
-    from gem_b200 import AUTO, SEQUENTIAL
+    from gem_b200 import PIPELINED, SEQUENTIAL
     g = Gemma(small.gguf, ctx=128)
     g.load_twolevel(small.twolevel)
+    g.set_schedule(PIPELINED)
     pipelined, G, GH, why = g.schedule(TWO_LEVEL)
     assert pipelined, why
     toks = synth.tokens(60, g.vocab, seed=12)
@@ -163,16 +169,17 @@ def test_pipelined_and_sequential_schedules_agree(torch, isa, small):
     lpo, amo, _, _ = o.score(toks, TWO_LEVEL)
     assert np.abs(lp_p - lpo).max() < 2e-5 and np.array_equal(am_p, amo)
     # the pipelined kernel also leaves the last hidden state for single-token head calls
-    g.set_schedule(AUTO)
+    g.set_schedule(PIPELINED)
     g.score(toks, TWO_LEVEL)
     lp1, am1 = g.twolevel_logprob(int(toks[-1]))
     assert abs(lp1 - lp_p[-1]) < 2e-5 and am1 == am_p[-1]
 
 
 def test_pipeline_bounded_wait_reports_timeout(torch, small):
-    from gem_b200 import GemError
+    from gem_b200 import PIPELINED, GemError
     g = Gemma(small.gguf, ctx=64)
     g.load_twolevel(small.twolevel)
+    g.set_schedule(PIPELINED)
     toks = synth.tokens(20, g.vocab, seed=13)
     want, _ = g.score(toks, TWO_LEVEL)
     g.test_withhold_stage(2, wait_ms=200)
@@ -190,10 +197,13 @@ def m270():
     return synth.ensure("gemma3-270m", classes=2048)  # shared cache with bench.py
 
 
-def test_270m_pipelined_scoring_is_exact(torch, isa, m270):
+@pytest.mark.parametrize("schedule", ["pipelined", "parallel"])
+def test_270m_scoring_is_exact(torch, isa, m270, schedule):
+    from gem_b200 import PARALLEL, PIPELINED
     g = Gemma(m270.gguf, ctx=2048)
     g.load_twolevel(m270.twolevel)
-    assert g.schedule(TWO_LEVEL)[0]
+    g.set_schedule(PIPELINED if schedule == "pipelined" else PARALLEL)
+    assert g.schedule_kind(TWO_LEVEL)[0] == (PIPELINED if schedule == "pipelined" else PARALLEL)
     o = orc.Model(m270.gguf, ctx=2048, threads=REF_THREADS, isa="avx512")
     o.load_twolevel(m270.twolevel)
     toks = synth.tokens(97, g.vocab, seed=21)
@@ -204,3 +214,41 @@ def test_270m_pipelined_scoring_is_exact(torch, isa, m270):
     lpf, amf = g.score(toks, FULL)
     lpfo, amfo, _, _ = o.score(toks, FULL)
     assert np.abs(lpf - lpfo).max() < 1e-4 and np.array_equal(amf, amfo)
+
+
+def test_parallel_schedule_is_auto_default(torch, small):
+    from gem_b200 import PARALLEL
+    g = Gemma(small.gguf, ctx=64)
+    g.load_twolevel(small.twolevel)
+    assert g.schedule_kind(TWO_LEVEL)[0] == PARALLEL and g.schedule_kind(FULL)[0] == PARALLEL
+
+
+@pytest.mark.parametrize("n", [1, 33, 1100])
+def test_parallel_lengths_and_chunks(torch, isa, small, n):
+    """A single position, a ragged tile (33 = 32 + 1) and two chunks (1100 > 1024 positions per chunk,
+    the second chunk's attention reading K/V rows the first chunk wrote)."""
+    g = Gemma(small.gguf, ctx=1200)
+    g.load_twolevel(small.twolevel)
+    o = orc.Model(small.gguf, ctx=1200, threads=REF_THREADS, isa="avx512")
+    o.load_twolevel(small.twolevel)
+    toks = synth.tokens(n + 1, g.vocab, seed=70 + n)
+    lp, am = g.score(toks, TWO_LEVEL)
+    lpo, amo, _, _ = o.score(toks, TWO_LEVEL)
+    assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo)
+    # the last position's hidden state is left for single-token head calls
+    lp1, am1 = g.twolevel_logprob(int(toks[-1]))
+    assert abs(lp1 - lp[-1]) < 2e-5 and am1 == am[-1]
+
+
+@pytest.mark.parametrize("body_bits,head_bits", [(4, 0), (8, 4), (4, 8)])
+def test_parallel_requantized_formats(torch, isa, small, body_bits, head_bits):
+    """--body-bits / --head-bits (to_q4 / to_q8, q8.rs:129-165; f32 scales) through the exact GEMM."""
+    g = Gemma(small.gguf, ctx=128, body_bits=body_bits, head_bits=head_bits)
+    g.load_twolevel(small.twolevel)
+    o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa="avx512", body_bits=body_bits, head_bits=head_bits)
+    o.load_twolevel(small.twolevel)
+    toks = synth.tokens(41, g.vocab, seed=90 + body_bits + head_bits)
+    for head in (FULL, TWO_LEVEL):
+        lp, am = g.score(toks, head)
+        lpo, amo, _, _ = o.score(toks, head)
+        assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo), (head, np.abs(lp - lpo).max())
