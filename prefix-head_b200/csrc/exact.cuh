@@ -120,6 +120,7 @@ __device__ __forceinline__ float dot512_pair(const float* a, const float* b, int
 // Rust `iter().map(|v| v * v).sum::<f32>()`: one thread, in order.
 __device__ __forceinline__ float seq_sumsq(const float* v, int n) {
   float s = 0.0f;
+#pragma unroll 4
   for (int i = 0; i < n; i += 4) {
     float4 t = *(const float4*)(v + i);
     s = add(s, mul(t.x, t.x));
@@ -152,10 +153,12 @@ __device__ inline void attn_prep_token(const AttnArgs& A, const float* qkv, uint
   float* sv = sk + hd;       // hd
   const int rw = A.nkv * hd;
   const float* bq = A.bqkv;
+#pragma unroll 4
   for (int j = threadIdx.x; j < G * hd; j += blockDim.x) {
     size_t i = (size_t)g * G * hd + j;
     sq[j] = bq ? add(qkv[i], bq[i]) : qkv[i];
   }
+#pragma unroll 2
   for (int j = threadIdx.x; j < hd; j += blockDim.x) {
     size_t ik = (size_t)A.nh * hd + g * hd + j, iv = (size_t)A.nh * hd + rw + g * hd + j;
     sk[j] = bq ? add(qkv[ik], bq[ik]) : qkv[ik];

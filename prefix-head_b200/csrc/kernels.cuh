@@ -137,9 +137,10 @@ void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, 
 void launch_seq_norm(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d, int T,
                      int8_t* aq, float* as, float* xn_out, cudaStream_t st);
 bool seq_gemm_supported(const MatView& w);
-void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, cudaStream_t st);
+void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
+                     cudaStream_t st);
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uint32_t pos0, float* qn, float* scores,
-                     int sstride, int threads, int8_t* aq, float* as, cudaStream_t st);
+                     int sstride, int threads, float* part, int8_t* aq, float* as, cudaStream_t st);
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st);
 void launch_seq_class_logits(const float* A, const float* b, int k, const float* h, int d, int T, float* cl,
                              cudaStream_t st);

@@ -128,7 +128,8 @@ struct gem_model {
   // sequence-parallel scoring (seq.cu): buffers for up to seq_cap positions
   static constexpr int kSeqChunk = 1024;  // positions per chunk
   static constexpr int kHeadChunk = 256;  // positions per full-head logits pass
-  int seq_cap = 0, seq_sstride = 0, logits_cap = 0;
+  int seq_cap = 0, seq_sstride = 0, logits_cap = 0, part_cap = 0;
+  float* s_part = nullptr;  // P.V partials [T][nh][ref_threads][hd]
   float *s_x = nullptr, *s_y = nullptr, *s_gu = nullptr, *s_dn = nullptr, *s_h = nullptr, *s_qn = nullptr,
         *s_scores = nullptr, *s_logits = nullptr;
   int8_t *s_aq = nullptr, *s_haq = nullptr;
@@ -297,7 +298,8 @@ struct gem_model {
     seq_why.clear();
     const int G = nkv > 0 ? nh / nkv : 0;
     if (G != 1 && G != 2 && G != 4 && G != 8) seq_why = "query heads per kv head not 1, 2, 4 or 8";
-    else if (hd % 16 || hd > 1024 || d % 32 || ff % 32 || (nh * hd) % 32) seq_why = "dimensions not in 32-blocks";
+    else if (hd % 32 || hd > 256 || d % 32 || d > 1152 || ff % 32)
+      seq_why = "head_dim above 256, hidden size above 1152 or dimensions not in 32-blocks";
     for (const Layer& L : layers)
       for (const DevMat* w : {&L.qkv, &L.o, &L.gu, &L.down})
         if (seq_why.empty() && !seq_gemm_supported(w->v)) seq_why = "body weights not Q8_0/Q4_0 with even block counts";
@@ -355,7 +357,7 @@ struct gem_model {
     int launches = 0;
     for (int h0 = 0; h0 < T; h0 += hc) {
       const int n = std::min(hc, T - h0);
-      launch_seq_gemm(head.v, s_haq + (size_t)h0 * d, s_has + (size_t)h0 * d / 32, n, s_logits, vocab, st);
+      launch_seq_gemm(head.v, s_haq + (size_t)h0 * d, s_has + (size_t)h0 * d / 32, n, s_logits, vocab, sms, st);
       launch_seq_logit_reduce(s_logits, vocab, n, targets + h0, lpo + h0, amo ? amo + h0 : nullptr, err, st);
       launches += 2;
     }
@@ -391,6 +393,10 @@ struct gem_model {
   void score_parallel(const uint32_t* toks_d, size_t n, int which, uint32_t base_pos, float* lp_d, uint32_t* am_d) {
     const int cap = (int)std::min<size_t>(n, kSeqChunk);
     ensure_seq(cap);
+    if ((int64_t)cap * ref_threads > part_cap) {
+      s_part = alloc<float>((size_t)cap * ref_threads * nh * hd);
+      part_cap = cap * ref_threads;
+    }
     const DevMat& E = untied ? emb : head;
     const int qkv_rows = (nh + 2 * nkv) * hd;
     int T = 0;
@@ -407,21 +413,22 @@ struct gem_model {
         const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
         launch_seq_norm(s_x, P ? s_dn : nullptr, P ? P->post_ffw : nullptr, L.attn_norm, eps, d, T, s_aq, s_as, nullptr, st);
         par_mark(PAR_NORM);
-        launch_seq_gemm(L.qkv.v, s_aq, s_as, T, s_y, qkv_rows, st);
+        launch_seq_gemm(L.qkv.v, s_aq, s_as, T, s_y, qkv_rows, sms, st);
         par_mark(PAR_QKV);
-        launch_seq_attn(attn_args(l, 0), s_y, qkv_rows, T, pos0, s_qn, s_scores, seq_sstride, ref_threads, s_aq, s_as, st);
+        launch_seq_attn(attn_args(l, 0), s_y, qkv_rows, T, pos0, s_qn, s_scores, seq_sstride, ref_threads, s_part, s_aq,
+                        s_as, st);
         par_mark(PAR_ATTN);
-        launch_seq_gemm(L.o.v, s_aq, s_as, T, s_y, d, st);
+        launch_seq_gemm(L.o.v, s_aq, s_as, T, s_y, d, sms, st);
         par_mark(PAR_O);
         launch_seq_norm(s_x, s_y, L.post_attn, L.ffn_norm, eps, d, T, s_aq, s_as, nullptr, st);
         par_mark(PAR_NORM);
-        launch_seq_gemm(L.gu.v, s_aq, s_as, T, s_gu, 2 * ff, st);
+        launch_seq_gemm(L.gu.v, s_aq, s_as, T, s_gu, 2 * ff, sms, st);
         par_mark(PAR_GU);
         launch_seq_glu_quant(s_gu, ff, T, silu ? 1 : 0, s_aq, s_as, sms, st);
         par_mark(PAR_GLU);
-        launch_seq_gemm(L.down.v, s_aq, s_as, T, s_dn, d, st);
+        launch_seq_gemm(L.down.v, s_aq, s_as, T, s_dn, d, sms, st);
         par_mark(PAR_DOWN);
-        nk += 11;  // 2 norms, 4 matrix products, 4 attention kernels, the gate
+        nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
       }
       launch_seq_norm(s_x, s_dn, layers[nl - 1].post_ffw, out_norm, eps, d, T, s_haq, s_has, s_h, st);
       par_mark(PAR_NORM);

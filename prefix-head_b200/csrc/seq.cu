@@ -15,13 +15,15 @@
 //   k_seq_norm         residual + post-norm, pre-norm, Act::quantize; warp per position
 //   k_seq_gemm         Y[t][r] = row r . act[t] with the reference's 16-lane order (q8.rs:248-292)
 //   k_seq_attn_prep    QK-norm, RoPE, q scale, K/V append                           (model.rs:316-335)
-//   k_seq_scores       dot512(q[t][h], K[p]) for p in the window of t             (model.rs:344-353)
+//   k_seq_scores_tile  dot512(q[t][h], K[p]) for p in the window of t             (model.rs:344-353)
 //   k_seq_softmax      max, exp_fast, sequential sum, 1/sum                         (model.rs:354-361)
-//   k_seq_pv           P.V in the pool's position ranges, then Act::quantize        (model.rs:362-382)
+//   k_seq_pv_tile      P.V partial sums over the pool's position ranges             (model.rs:362-382)
+//   k_seq_pv_combine   partials added in range order, then Act::quantize
 //   k_seq_glu_quant    GELU-tanh (or SiLU) gate * up, Act::quantize                 (model.rs:408-416)
 //   k_seq_class_logits two-level class logits dot512(A[c], h[t]) + b[c]            (main.rs:82-93)
 //   k_seq_logit_reduce full-head log-sum-exp, argmax and target logit per position  (main.rs:30-37)
 #include <algorithm>
+#include <cstdlib>
 
 #include "kernels.cuh"
 #include "exact.cuh"
@@ -42,15 +44,8 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// One madd_epi16 lane as an exact float: the int32 pair sum p (|p| <= 2 * 128 * 127) is added to the
-// bit pattern of 1.5 * 2^23 by the dot instruction itself, which gives the float 1.5 * 2^23 + p
-// exactly; subtracting 1.5 * 2^23 leaves p. Two full-rate instructions instead of a conversion.
-constexpr int kMagicI = 0x4B400000;
-constexpr float kMagicF = 12582912.0f;
-__device__ __forceinline__ float madd_lo_f(int w, int a) { return sub(__int_as_float(__dp4a(w & 0x0000ffff, a, kMagicI)), kMagicF); }
-__device__ __forceinline__ float madd_hi_f(int w, int a) { return sub(__int_as_float(__dp4a(w & (int)0xffff0000, a, kMagicI)), kMagicF); }
 
-__device__ __forceinline__ uint32_t window_lo(uint32_t pos, int window) {
+__host__ __device__ __forceinline__ uint32_t window_lo(uint32_t pos, int window) {
   return (window > 0 && pos + 1 > (uint32_t)window) ? pos + 1 - window : 0;
 }
 
@@ -74,11 +69,12 @@ __global__ void k_seq_embed(MatView E, const uint32_t* toks, int vocab, float sc
 // Residual + post-norm, then pre-norm + quantize (k_residual_norm_quant_exact per position). One warp
 // per position: squares in parallel, lane 0 adds them in order (Rust's sequential f32 sum).
 // ------------------------------------------------------------------------------------------------
-constexpr int kNormWarps = 8;
+constexpr int kNormWarps = 4;
 
 __device__ __forceinline__ float warp_seq_sum(const float* sq, int n, int lane) {
   float s = 0.0f;
   if (lane == 0)
+#pragma unroll 8
     for (int j = 0; j < n; j += 4) {
       float4 v = *(const float4*)(sq + j);
       s = add(s, v.x);
@@ -89,48 +85,73 @@ __device__ __forceinline__ float warp_seq_sum(const float* sq, int n, int lane) 
   return __shfl_sync(0xffffffffu, s, 0);
 }
 
+constexpr int kNormMaxV = 9;  // float4 per lane: d <= 1152
+
 __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const float* delta, const float* w_post,
                                                               const float* w_pre, float eps, int d, int T, int8_t* aq,
                                                               float* as, float* xn_out) {
-  extern __shared__ __align__(16) float sn[];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  extern __shared__ __align__(16) float sn[];  // w_post [d], w_pre [d], then per warp xs [d], sq [d]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n4 = d / 4;
+  float* swpost = sn;
+  float* swpre = sn + d;
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    ((float4*)swpre)[i] = ((const float4*)w_pre)[i];
+    if (w_post) ((float4*)swpost)[i] = ((const float4*)w_post)[i];
+  }
+  __syncthreads();
   const int t = blockIdx.x * kNormWarps + warp;
   if (t >= T) return;
-  float* xs = sn + (size_t)warp * 2 * d;
+  float* xs = sn + 2 * d + (size_t)warp * 2 * d;
   float* sq = xs + d;
-  float* xt = x + (size_t)t * d;
+  float4* xt = (float4*)(x + (size_t)t * d);
+  float4 xv[kNormMaxV], dv[kNormMaxV];
+#pragma unroll
+  for (int k = 0; k < kNormMaxV; ++k) {  // every load of this position issued before any is used
+    const int i = lane + 32 * k;
+    if (i < n4) {
+      xv[k] = xt[i];
+      if (delta) dv[k] = ((const float4*)(delta + (size_t)t * d))[i];
+    }
+  }
+  auto sq4 = [](float4 v) { return make_float4(mul(v.x, v.x), mul(v.y, v.y), mul(v.z, v.z), mul(v.w, v.w)); };
   if (delta) {
-    const float* dt = delta + (size_t)t * d;
     float r = 1.0f;
     if (w_post) {
-      for (int j = lane; j < d; j += 32) {
-        float v = dt[j];
-        sq[j] = mul(v, v);
-      }
+#pragma unroll
+      for (int k = 0; k < kNormMaxV; ++k)
+        if (lane + 32 * k < n4) ((float4*)sq)[lane + 32 * k] = sq4(dv[k]);
       __syncwarp();
       r = rms_r_exact(warp_seq_sum(sq, d, lane), d, eps);
     }
-    for (int j = lane; j < d; j += 32) {
-      float v = dt[j];
-      if (w_post) v = mul(v, mul(r, w_post[j]));  // rmsnorm_inplace (model.rs:89-95)
-      float s = add(xt[j], v);
-      xs[j] = s;
-      xt[j] = s;
-      sq[j] = mul(s, s);
+#pragma unroll
+    for (int k = 0; k < kNormMaxV; ++k) {
+      const int i = lane + 32 * k;
+      if (i >= n4) continue;
+      float4 v = dv[k];
+      if (w_post) {  // rmsnorm_inplace (model.rs:89-95): v *= r * w
+        const float4 w = ((const float4*)swpost)[i];
+        v = make_float4(mul(v.x, mul(r, w.x)), mul(v.y, mul(r, w.y)), mul(v.z, mul(r, w.z)), mul(v.w, mul(r, w.w)));
+      }
+      const float4 o = xv[k];
+      xv[k] = make_float4(add(o.x, v.x), add(o.y, v.y), add(o.z, v.z), add(o.w, v.w));
+      xt[i] = xv[k];
     }
-  } else {
-    for (int j = lane; j < d; j += 32) {
-      float s = xt[j];
-      xs[j] = s;
-      sq[j] = mul(s, s);
+  }
+#pragma unroll
+  for (int k = 0; k < kNormMaxV; ++k) {
+    const int i = lane + 32 * k;
+    if (i < n4) {
+      ((float4*)xs)[i] = xv[k];
+      ((float4*)sq)[i] = sq4(xv[k]);
     }
   }
   __syncwarp();
   const float r = rms_r_exact(warp_seq_sum(sq, d, lane), d, eps);
   const int nb = d / 32;
+#pragma unroll 4
   for (int b = 0; b < nb; ++b) {
     const int j = b * 32 + lane;
-    float v = mul(mul(xs[j], r), w_pre[j]);  // rmsnorm (model.rs:81-87)
+    const float v = mul(mul(xs[j], r), swpre[j]);  // rmsnorm (model.rs:81-87)
     if (xn_out) xn_out[(size_t)t * d + j] = v;
     if (aq) quant_block_warp_x(v, lane, aq + (size_t)t * d + b * 32, as + (size_t)t * nb + b);
   }
@@ -139,29 +160,31 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const fl
 // ------------------------------------------------------------------------------------------------
 // Exact int8 matrix product: Y[t][r] = row_dot(W[r], act[t]) for Q8 / Q4 weights, with the lane
 // structure of dot_avx512 / dot4_avx512 (lane i = w[2i]a[2i] + w[2i+1]a[2i+1] per 32-block, one FMA
-// per block with scale ws*as, halving reduction). A thread pair holds the 16 lanes of one row for 8
-// positions (8 + 8 lanes, as in row_dot_exact). CTA tile: 32 rows x 32 positions, 8 warps
-// (warp w: rows 16*(w&1) .. +15, positions 8*(w>>1) .. +7), K staged through shared memory in
-// chunks of 8 blocks (256 columns) by cp.async, three stages deep.
+// per block with scale ws*as, halving reduction). A thread pair holds the 16 lanes of one row for RN
+// positions (8 + 8 lanes, as in row_dot_exact). CTA tile: 32 rows x 4*RN positions, 8 warps
+// (warp w: rows 16*(w&1) .. +15, positions RN*(w>>1) .. +RN-1), K staged through shared memory in
+// chunks of 8 blocks (256 columns) by cp.async, three stages deep. RN = 8 for large matrices, 4 where
+// the smaller tile fills the SMs more evenly (640-row projections at 512 positions).
 // ------------------------------------------------------------------------------------------------
-constexpr int kGemmBM = 32, kGemmBN = 32, kGemmKB = 8, kGemmStages = 3, kGemmThreads = 256;
+constexpr int kGemmBM = 32, kGemmKB = 8, kGemmStages = 3, kGemmThreads = 256;
 
-template <int BITS, typename ST>
+template <int BITS, typename ST, int RN>
 struct GemmTile {
+  static constexpr int BN = 4 * RN;                    // positions per CTA
   static constexpr int WB = BITS == 8 ? 32 : 16;       // weight bytes per 32-block of a row
   static constexpr int WROW = kGemmKB * WB + 16;       // padded row: 16-row reads hit distinct banks
   static constexpr int SB = (int)sizeof(ST);
   static constexpr int A_OFF = kGemmBM * WROW;                        // activations [BN][KB*32]
-  static constexpr int SW_OFF = A_OFF + kGemmBN * kGemmKB * 32;       // weight scales [BM][KB]
+  static constexpr int SW_OFF = A_OFF + BN * kGemmKB * 32;            // weight scales [BM][KB]
   static constexpr int SA_OFF = SW_OFF + kGemmBM * kGemmKB * SB;      // activation scales [KB][BN]
-  static constexpr int STAGE = (SA_OFF + kGemmKB * kGemmBN * 4 + 127) / 128 * 128;
+  static constexpr int STAGE = (SA_OFF + kGemmKB * BN * 4 + 127) / 128 * 128;
   static constexpr int SMEM = kGemmStages * STAGE;
 };
 
-template <int BITS, typename ST>
+template <int BITS, typename ST, int RN>
 __device__ __forceinline__ void gemm_issue(unsigned char* stage, const MatView& w, const int8_t* aq, const float* as,
                                            int T, int row0, int tok0, int b0, int kb) {
-  using G = GemmTile<BITS, ST>;
+  using G = GemmTile<BITS, ST, RN>;
   const int tid = threadIdx.x, nb = w.cols / 32;
   const size_t rowbytes = (size_t)nb * G::WB;
   constexpr int WP = kGemmKB * G::WB / 16;  // 16-byte pieces per weight row
@@ -172,7 +195,7 @@ __device__ __forceinline__ void gemm_issue(unsigned char* stage, const MatView& 
     cp16(stage + r * G::WROW + p * 16, src, ok);
   }
   constexpr int AP = kGemmKB * 2;
-  for (int i = tid; i < kGemmBN * AP; i += kGemmThreads) {
+  for (int i = tid; i < G::BN * AP; i += kGemmThreads) {
     const int t = i / AP, p = i % AP;
     const bool ok = p < 2 * kb && tok0 + t < T;
     const int8_t* src = aq + (ok ? (size_t)(tok0 + t) * w.cols + (size_t)b0 * 32 + p * 16 : 0);
@@ -185,35 +208,36 @@ __device__ __forceinline__ void gemm_issue(unsigned char* stage, const MatView& 
     const unsigned char* src = (const unsigned char*)w.s + (ok ? ((size_t)(row0 + r) * nb + b0) * G::SB + p * 4 : 0);
     cp4(stage + G::SW_OFF + r * kGemmKB * G::SB + p * 4, src, ok);
   }
-  for (int i = tid; i < kGemmKB * kGemmBN; i += kGemmThreads) {
-    const int b = i / kGemmBN, t = i % kGemmBN;
+  for (int i = tid; i < kGemmKB * G::BN; i += kGemmThreads) {
+    const int b = i / G::BN, t = i % G::BN;
     const bool ok = b < kb && tok0 + t < T;
     const float* src = as + (ok ? (size_t)(tok0 + t) * nb + b0 + b : 0);
-    cp4(stage + G::SA_OFF + (b * kGemmBN + t) * 4, src, ok);
+    cp4(stage + G::SA_OFF + (b * G::BN + t) * 4, src, ok);
   }
 }
 
-template <int BITS, typename ST>
-__global__ void __launch_bounds__(kGemmThreads, 2) k_seq_gemm(MatView w, const int8_t* aq, const float* as, int T,
-                                                               float* y, int ldy) {
-  using G = GemmTile<BITS, ST>;
+template <int BITS, typename ST, int RN>
+__global__ void __launch_bounds__(kGemmThreads, RN == 8 ? 2 : 3) k_seq_gemm(MatView w, const int8_t* aq,
+                                                                             const float* as, int T, float* y, int ldy) {
+  using G = GemmTile<BITS, ST, RN>;
   extern __shared__ __align__(128) unsigned char sg[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane & 1;
-  const int tok0 = blockIdx.x * kGemmBN, row0 = blockIdx.y * kGemmBM;
+  const int tok0 = blockIdx.x * G::BN, row0 = blockIdx.y * kGemmBM;
   const int rl = (warp & 1) * 16 + (lane >> 1);  // row inside the tile
-  const int tl = (warp >> 1) * 8;                // first of this thread's 8 positions
+  const int tl = (warp >> 1) * RN;               // first of this thread's RN positions
   const int nb = w.cols / 32;
   const int nchunks = (nb + kGemmKB - 1) / kGemmKB;
 
-  float acc[8][8];
+  float2 acc[RN][4];  // lanes (2q, 2q + 1) of this thread's half, per position
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < RN; ++i)
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[i][k] = 0.0f;
+    for (int k = 0; k < 4; ++k) acc[i][k] = make_float2(0.0f, 0.0f);
 
 #pragma unroll
   for (int s = 0; s < kGemmStages - 1; ++s) {
-    if (s < nchunks) gemm_issue<BITS, ST>(sg + s * G::STAGE, w, aq, as, T, row0, tok0, s * kGemmKB, min(kGemmKB, nb - s * kGemmKB));
+    if (s < nchunks)
+      gemm_issue<BITS, ST, RN>(sg + s * G::STAGE, w, aq, as, T, row0, tok0, s * kGemmKB, min(kGemmKB, nb - s * kGemmKB));
     cp_commit();
   }
   for (int c = 0; c < nchunks; ++c) {
@@ -222,8 +246,8 @@ __global__ void __launch_bounds__(kGemmThreads, 2) k_seq_gemm(MatView w, const i
     {
       const int cn = c + kGemmStages - 1;
       if (cn < nchunks)
-        gemm_issue<BITS, ST>(sg + (cn % kGemmStages) * G::STAGE, w, aq, as, T, row0, tok0, cn * kGemmKB,
-                             min(kGemmKB, nb - cn * kGemmKB));
+        gemm_issue<BITS, ST, RN>(sg + (cn % kGemmStages) * G::STAGE, w, aq, as, T, row0, tok0, cn * kGemmKB,
+                                 min(kGemmKB, nb - cn * kGemmKB));
       cp_commit();
     }
     const unsigned char* S = sg + (c % kGemmStages) * G::STAGE;
@@ -245,29 +269,36 @@ __global__ void __launch_bounds__(kGemmThreads, 2) k_seq_gemm(MatView w, const i
         wv.z = (int)__vsub4(((unsigned)raw.z >> sh) & m, e);
         wv.w = (int)__vsub4(((unsigned)raw.w >> sh) & m, e);
       }
+      // the low / high int16 pair of each weight word, masked once for all RN positions
+      const int wl[4] = {wv.x & 0x0000ffff, wv.y & 0x0000ffff, wv.z & 0x0000ffff, wv.w & 0x0000ffff};
+      const int wh[4] = {wv.x & (int)0xffff0000, wv.y & (int)0xffff0000, wv.z & (int)0xffff0000, wv.w & (int)0xffff0000};
       const float swb = ld_scale(wsc, b);
-      const float4 sa0 = *(const float4*)(asc + b * kGemmBN), sa1 = *(const float4*)(asc + b * kGemmBN + 4);
-      const float sa[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
+      float sa[RN];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < RN; k += 4) {
+        const float4 v = *(const float4*)(asc + b * G::BN + k);
+        sa[k] = v.x, sa[k + 1] = v.y, sa[k + 2] = v.z, sa[k + 3] = v.w;
+      }
+#pragma unroll
+      for (int k = 0; k < RN; ++k) {
         const int4 av = *(const int4*)(arow + k * (kGemmKB * 32) + b * 32);
         const float s = mul(swb, sa[k]);
-        acc[k][0] = fmaf(madd_lo_f(wv.x, av.x), s, acc[k][0]);
-        acc[k][1] = fmaf(madd_hi_f(wv.x, av.x), s, acc[k][1]);
-        acc[k][2] = fmaf(madd_lo_f(wv.y, av.y), s, acc[k][2]);
-        acc[k][3] = fmaf(madd_hi_f(wv.y, av.y), s, acc[k][3]);
-        acc[k][4] = fmaf(madd_lo_f(wv.z, av.z), s, acc[k][4]);
-        acc[k][5] = fmaf(madd_hi_f(wv.z, av.z), s, acc[k][5]);
-        acc[k][6] = fmaf(madd_lo_f(wv.w, av.w), s, acc[k][6]);
-        acc[k][7] = fmaf(madd_hi_f(wv.w, av.w), s, acc[k][7]);
+        const float2 s2 = make_float2(s, s);
+        const int a4[4] = {av.x, av.y, av.z, av.w};
+        // two madd_epi16 lanes per step: exact int32 pair sums converted to fp32 (exact: |p| < 2^24),
+        // then one packed FMA, which rounds each lane as fmaf does
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          acc[k][q] = __ffma2_rn(make_float2((float)__dp4a(wl[q], a4[q], 0), (float)__dp4a(wh[q], a4[q], 0)), s2, acc[k][q]);
       }
     }
   }
   cp_wait<0>();
   const int r = row0 + rl;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float v = reduce16_pair(acc[k]);
+  for (int k = 0; k < RN; ++k) {
+    const float a8[8] = {acc[k][0].x, acc[k][0].y, acc[k][1].x, acc[k][1].y, acc[k][2].x, acc[k][2].y, acc[k][3].x, acc[k][3].y};
+    const float v = reduce16_pair(a8);
     const int t = tok0 + tl + k;
     if (half == 0 && r < w.rows && t < T) y[(size_t)t * ldy + r] = v;
   }
@@ -284,46 +315,77 @@ __global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, uint32
   attn_prep_token(A, qkv + (size_t)t * qkv_ld, pos0 + t, blockIdx.y, qn + (size_t)t * A.nh * A.hd, smp, s_r);
 }
 
-// scores[t][h][i] = dot512(q[t][h], K[lo_t + i]) (model.rs:344-353). One CTA per position; a thread
-// pair takes one key position and the G query heads that share its kv group (dot512_pair lanes).
+// Tiled scores: a CTA takes kAttnTQ consecutive positions (rows: position x query head of kv group
+// blockIdx.z) against kAttnPC key positions starting at pbase + blockIdx.y * kAttnPC, with the queries
+// and the key rows staged in shared memory, so each key row is read once per tile instead of once
+// per position. A thread pair computes one row against 8 keys with dot512_pair's lanes. Only keys in
+// a row's window [lo, pos] are written.
+constexpr int kAttnTQ = 8, kAttnPC = 64;
+
 template <int G>
-__global__ void k_seq_scores(AttnArgs A, const float* qn, uint32_t pos0, float* scores, int sstride) {
-  extern __shared__ __align__(16) float sq[];  // this position's queries [nh][hd]
-  const int t = blockIdx.x, hd = A.hd;
-  const uint32_t pos = pos0 + t, lo = window_lo(pos, A.window);
-  const int n_pos = (int)(pos + 1 - lo);
-  const int rw = A.nkv * hd;
-  for (int j = threadIdx.x; j < A.nh * hd / 4; j += blockDim.x)
-    ((float4*)sq)[j] = ((const float4*)(qn + (size_t)t * A.nh * hd))[j];
+__global__ void __launch_bounds__(256) k_seq_scores_tile(AttnArgs A, const float* qn, int T, uint32_t pos0,
+                                                         uint32_t pbase, float* scores, int sstride) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int R = kAttnTQ * G;  // a multiple of 4 (kAttnTQ = 8)
+  const int hd = A.hd, g = blockIdx.z, qs = hd + 4;  // padded query rows: 16 rows hit distinct banks
+  const int t0 = blockIdx.x * kAttnTQ, tn = min(kAttnTQ, T - t0);
+  const uint32_t p0 = pbase + blockIdx.y * kAttnPC;
+  const uint32_t need_lo = window_lo(pos0 + t0, A.window), need_hi = pos0 + t0 + tn - 1;
+  if (p0 > need_hi || p0 + kAttnPC <= need_lo) return;
+  float* sq = sm;              // [R][hd + 4]
+  float* sk = sm + R * qs;     // [PC][hd]
+  const int rw = A.nkv * hd, h4 = hd / 4;
+  for (int i = threadIdx.x; i < R * h4; i += blockDim.x) {
+    const int row = i / h4, e = i % h4, tt = row / G, h = row % G;
+    const bool ok = tt < tn;
+    cp16(sq + row * qs + e * 4, qn + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * hd + e * 4 : 0), ok);
+  }
+  for (int i = threadIdx.x; i < kAttnPC * h4; i += blockDim.x) {
+    const int pr = i / h4, e = i % h4;
+    const uint32_t p = p0 + pr;
+    const bool ok = p <= need_hi;
+    cp16(sk + i * 4, A.kcache + (ok ? (size_t)p * rw + g * hd + e * 4 : 0), ok);
+  }
+  cp_commit();
+  cp_wait<0>();
   __syncthreads();
+  // A thread pair takes one row against 8 keys (dot512_pair's lanes); a warp's 16 pairs share the keys,
+  // so key reads are broadcasts and query rows (padded) hit distinct banks.
   const int half = threadIdx.x & 1, pairs = blockDim.x / 2;
-  const int tasks = n_pos * A.nkv;
-  for (int base = 0; base < tasks; base += pairs) {
+  constexpr int ntask = R * (kAttnPC / 8);
+  for (int base = 0; base < ntask; base += pairs) {
     const int task = base + (int)threadIdx.x / 2;
-    const bool ok = task < tasks;
-    const int i = ok ? task / A.nkv : 0, g = ok ? task % A.nkv : 0;
-    const float* k = A.kcache + (size_t)(lo + i) * rw + g * hd + half * 8;
-    float acc[G][8];
+    const bool ok = task < ntask;
+    const int tk = ok ? task : 0;
+    const int row = tk % R, pg = tk / R;
+    const float* q = sq + row * qs + half * 8;
+    const float* k = sk + (pg * 8) * hd + half * 8;
+    float2 acc[8][4];
 #pragma unroll
-    for (int h = 0; h < G; ++h)
+    for (int u = 0; u < 8; ++u)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[h][e] = 0.0f;
+      for (int e = 0; e < 4; ++e) acc[u][e] = make_float2(0.0f, 0.0f);
     for (int c = 0; c < hd / 16; ++c) {
-      const float4 k0 = __ldcg((const float4*)(k + c * 16)), k1 = __ldcg((const float4*)(k + c * 16 + 4));
+      const float4 q0 = *(const float4*)(q + c * 16), q1 = *(const float4*)(q + c * 16 + 4);
+      const float2 qv[4] = {make_float2(q0.x, q0.y), make_float2(q0.z, q0.w), make_float2(q1.x, q1.y), make_float2(q1.z, q1.w)};
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float* q = sq + (size_t)(g * G + h) * hd + c * 16 + half * 8;
-        const float4 q0 = *(const float4*)q, q1 = *(const float4*)(q + 4);
-        acc[h][0] = fmaf(q0.x, k0.x, acc[h][0]); acc[h][1] = fmaf(q0.y, k0.y, acc[h][1]);
-        acc[h][2] = fmaf(q0.z, k0.z, acc[h][2]); acc[h][3] = fmaf(q0.w, k0.w, acc[h][3]);
-        acc[h][4] = fmaf(q1.x, k1.x, acc[h][4]); acc[h][5] = fmaf(q1.y, k1.y, acc[h][5]);
-        acc[h][6] = fmaf(q1.z, k1.z, acc[h][6]); acc[h][7] = fmaf(q1.w, k1.w, acc[h][7]);
+      for (int u = 0; u < 8; ++u) {
+        const float4 k0 = *(const float4*)(k + u * hd + c * 16), k1 = *(const float4*)(k + u * hd + c * 16 + 4);
+        acc[u][0] = __ffma2_rn(qv[0], make_float2(k0.x, k0.y), acc[u][0]);
+        acc[u][1] = __ffma2_rn(qv[1], make_float2(k0.z, k0.w), acc[u][1]);
+        acc[u][2] = __ffma2_rn(qv[2], make_float2(k1.x, k1.y), acc[u][2]);
+        acc[u][3] = __ffma2_rn(qv[3], make_float2(k1.z, k1.w), acc[u][3]);
       }
     }
+    const int tt = row / G, h = row % G;
+    const uint32_t pos = pos0 + t0 + tt, lo = window_lo(pos, A.window);
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float s = reduce16_pair(acc[h]);
-      if (ok && half == 0) scores[((size_t)t * A.nh + g * G + h) * sstride + i] = s;
+    for (int u = 0; u < 8; ++u) {
+      const float a8[8] = {acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y, acc[u][2].x, acc[u][2].y, acc[u][3].x, acc[u][3].y};
+      const float sc = reduce16_pair(a8);
+      const uint32_t p = p0 + pg * 8 + u;
+      if (ok && half == 0 && tt < tn && p >= lo && p <= pos)
+        scores[((size_t)(t0 + tt) * A.nh + g * G + h) * sstride + (p - lo)] = sc;
     }
   }
 }
@@ -339,59 +401,127 @@ __global__ void k_seq_softmax(AttnArgs A, int T, uint32_t pos0, float* scores, i
   const uint32_t pos = pos0 + t, lo = window_lo(pos, A.window);
   const int n = (int)(pos + 1 - lo);
   float* s = scores + (size_t)task * sstride;
-  float* e = ss + (size_t)warp * sstride;
+  float* e = ss + (size_t)warp * ((sstride + 3) & ~3);  // 16-byte aligned rows
+  for (int i = lane; i < n; i += 32) cp4(e + i, s + i, true);
+  cp_commit();
+  cp_wait<0>();
+  __syncwarp();
   float m = -INFINITY;
-  for (int i = lane; i < n; i += 32) m = fmaxf(m, s[i]);
+  for (int i = lane; i < n; i += 32) m = fmaxf(m, e[i]);
   m = warp_max(m);
-  for (int i = lane; i < n; i += 32) e[i] = exp_fast(sub(s[i], m));
+  for (int i = lane; i < n; i += 32) e[i] = exp_fast(sub(e[i], m));
   __syncwarp();
   float sum = 0.0f;
-  if (lane == 0)
-    for (int i = 0; i < n; ++i) sum = add(sum, e[i]);
+  if (lane == 0) {
+    int i = 0;
+#pragma unroll 4
+    for (; i + 4 <= n; i += 4) {
+      const float4 v = *(const float4*)(e + i);
+      sum = add(sum, v.x);
+      sum = add(sum, v.y);
+      sum = add(sum, v.z);
+      sum = add(sum, v.w);
+    }
+    for (; i < n; ++i) sum = add(sum, e[i]);
+  }
   const float inv = div(1.0f, __shfl_sync(0xffffffffu, sum, 0));
   for (int i = lane; i < n; i += 32) s[i] = mul(e[i], inv);
 }
 
-// P.V with the pool's partition (model.rs:362-382): positions split into `threads` ranges of
-// per = ceil(n / threads); range r accumulates fma(p, v, acc) in order; att = partials summed in
-// range order. Then Act::quantize of att. One CTA per position, thread j = output element of every
-// head; ranges are processed 8 at a time so their FMA chains overlap.
-__global__ void k_seq_pv(AttnArgs A, uint32_t pos0, const float* scores, int sstride, int threads, int8_t* aq,
-                         float* as) {
-  const int t = blockIdx.x, hd = A.hd, G = A.nh / A.nkv, j = threadIdx.x;
-  const uint32_t pos = pos0 + t, lo = window_lo(pos, A.window);
-  const int n = (int)(pos + 1 - lo);
-  const int per = (n + threads - 1) / threads;
+// P.V by range: the pool's partition (model.rs:362-382) makes each of the `threads` position ranges
+// of a row an independent partial sum, so a CTA takes one range r of every row of a tile of
+// kAttnTQ positions (all heads), stages the V rows of the tile's ranges in chunks of kPvRows, and
+// writes the partials; k_seq_pv_combine adds them in range order. Thread j = output element.
+constexpr int kPvRows = 32;
+
+template <int G>
+__global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A, int T, uint32_t pos0, const float* scores,
+                                                     int sstride, int threads, float* part) {
+  constexpr int R = kAttnTQ * G;               // rows of the tile: position x head of the group
+  extern __shared__ __align__(16) float sv[];  // V [kPvRows][hd], then probabilities P [R][kPvRows]
+  __shared__ uint32_t s_lo[kAttnTQ], s_a[kAttnTQ], s_b[kAttnTQ];
+  const int hd = A.hd, h4 = hd / 4, t0 = blockIdx.x * kAttnTQ, tn = min(kAttnTQ, T - t0), r = blockIdx.y;
+  const int j2 = threadIdx.x * 2;  // this thread's two output columns
   const int rw = A.nkv * hd;
-  const int lane = j & 31;
-  const int nbh = A.nh * hd / 32;
-  for (int h = 0; h < A.nh; ++h) {
-    const float* p = scores + ((size_t)t * A.nh + h) * sstride;
-    const float* vc = A.vcache + (size_t)lo * rw + (h / G) * hd + j;
-    float a = 0.0f;
-    for (int r0 = 0; r0 < threads; r0 += 8) {
-      float acc[8];
-      int i0[8], i1[8];
+  float* sp = sv + kPvRows * hd;
+  if (threadIdx.x < kAttnTQ) {
+    const int tt = threadIdx.x;
+    uint32_t lo = 0, a = 0, b = 0;
+    if (tt < tn) {
+      const uint32_t pos = pos0 + t0 + tt;
+      lo = window_lo(pos, A.window);
+      const int n = (int)(pos + 1 - lo), per = (n + threads - 1) / threads;
+      a = lo + min(r * per, n);
+      b = lo + min((r + 1) * per, n);
+    }
+    s_lo[tt] = lo, s_a[tt] = a, s_b[tt] = b;
+  }
+  __syncthreads();
+  uint32_t ua = 0xffffffffu, ub = 0;
+  for (int tt = 0; tt < tn; ++tt)
+    if (s_a[tt] < s_b[tt]) ua = min(ua, s_a[tt]), ub = max(ub, s_b[tt]);
+  for (int g = 0; g < A.nkv; ++g) {
+    float2 acc[R];  // columns j2, j2 + 1
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        acc[u] = 0.0f;
-        i0[u] = min((r0 + u) * per, n);
-        i1[u] = r0 + u < threads ? min((r0 + u + 1) * per, n) : i0[u];
+    for (int i = 0; i < R; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    for (uint32_t c0 = ua; c0 < ub; c0 += kPvRows) {
+      const int rows = (int)min((uint32_t)kPvRows, ub - c0), rows4 = (rows + 3) & ~3;
+      __syncthreads();
+      for (int i = threadIdx.x; i < rows4 * h4; i += blockDim.x) {  // rows past `rows` are zero
+        const int pr = i / h4, e = i % h4;
+        const bool ok = pr < rows;
+        cp16(sv + pr * hd + e * 4, A.vcache + (ok ? (size_t)(c0 + pr) * rw + g * hd + e * 4 : 0), ok);
       }
-      for (int k = 0; k < per; ++k) {
+      // a row's probabilities are zero outside its range, which makes its FMAs there exact no-ops
+      // (a range's sum starts at +0 and never becomes -0, so adding 0 * v changes nothing)
+      for (int i = threadIdx.x; i < R * kPvRows; i += blockDim.x) {
+        const int row = i / kPvRows, pi = i % kPvRows, tt = row / G, h = row % G;
+        const uint32_t p = c0 + pi;
+        const bool ok = tt < tn && pi < rows && p >= s_a[tt] && p < s_b[tt];
+        cp4(sp + i, scores + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride + (p - s_lo[tt]) : 0), ok);
+      }
+      cp_commit();
+      cp_wait<0>();
+      __syncthreads();
+      for (int p4 = 0; p4 < rows4; p4 += 4) {
+        const float2 v0 = *(const float2*)(sv + (p4 + 0) * hd + j2), v1 = *(const float2*)(sv + (p4 + 1) * hd + j2);
+        const float2 v2 = *(const float2*)(sv + (p4 + 2) * hd + j2), v3 = *(const float2*)(sv + (p4 + 3) * hd + j2);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = i0[u] + k;
-          if (i < i1[u]) acc[u] = fmaf(p[i], vc[(size_t)i * rw], acc[u]);
+        for (int i = 0; i < R; ++i) {
+          const float4 pp = *(const float4*)(sp + i * kPvRows + p4);
+          acc[i] = __ffma2_rn(make_float2(pp.x, pp.x), v0, acc[i]);
+          acc[i] = __ffma2_rn(make_float2(pp.y, pp.y), v1, acc[i]);
+          acc[i] = __ffma2_rn(make_float2(pp.z, pp.z), v2, acc[i]);
+          acc[i] = __ffma2_rn(make_float2(pp.w, pp.w), v3, acc[i]);
         }
       }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (r0 + u < threads) a = add(a, acc[u]);
     }
-    const int b = (h * hd + j) / 32;
-    quant_block_warp_x(a, lane, aq + (size_t)t * A.nh * hd + b * 32, as + (size_t)t * nbh + b);
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const int tt = i / G, h = i % G;
+      if (tt < tn)
+        *(float2*)(part + (((size_t)(t0 + tt) * A.nh + g * G + h) * threads + r) * hd + j2) = acc[i];
+    }
   }
+}
+
+// att[t][h][j] = partials summed in range order (from 0), then Act::quantize. One CTA per
+// (position, head), all partial loads in flight before the ordered adds.
+__global__ void k_seq_pv_combine(AttnArgs A, const float* part, int threads, int8_t* aq, float* as) {
+  const int t = blockIdx.x, h = blockIdx.y, hd = A.hd, j = threadIdx.x, lane = j & 31;
+  const int nbh = A.nh * hd / 32;
+  const float* pp = part + ((size_t)t * A.nh + h) * threads * hd + j;
+  float a = 0.0f;
+  for (int r0 = 0; r0 < threads; r0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = r0 + u < threads ? pp[(size_t)(r0 + u) * hd] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (r0 + u < threads) a = add(a, v[u]);
+  }
+  const int b = (h * hd + j) / 32;
+  quant_block_warp_x(a, lane, aq + (size_t)t * A.nh * hd + b * 32, as + (size_t)t * nbh + b);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -432,32 +562,41 @@ __global__ void __launch_bounds__(256, 2) k_seq_class_logits(const float* A, con
   const int tok0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
   for (int i = threadIdx.x; i < 32 * d / 4; i += blockDim.x) {
     const int t = i / (d / 4), j = i % (d / 4);
-    ((float4*)sh)[i] = tok0 + t < T ? ((const float4*)(h + (size_t)(tok0 + t) * d))[j] : make_float4(0, 0, 0, 0);
+    const bool ok = tok0 + t < T;
+    cp16(sh + i * 4, h + (ok ? (size_t)(tok0 + t) * d + j * 4 : 0), ok);
   }
+  cp_commit();
+  cp_wait<0>();
   __syncthreads();
   const int c = c0 + (warp & 1) * 16 + (lane >> 1);
   const int tl = (warp >> 1) * 8;
   const float* arow = A + (size_t)min(c, k - 1) * d + half * 8;
-  float acc[8][8];
+  float2 acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[i][e] = 0.0f;
+    for (int e = 0; e < 4; ++e) acc[i][e] = make_float2(0.0f, 0.0f);
+  float4 a0 = __ldg((const float4*)arow), a1 = __ldg((const float4*)(arow + 4));
   for (int ch = 0; ch < d / 16; ++ch) {
-    const float4 a0 = __ldg((const float4*)(arow + ch * 16)), a1 = __ldg((const float4*)(arow + ch * 16 + 4));
+    const float2 av[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
+    if (ch + 1 < d / 16) {  // the next chunk's class row while this one computes
+      a0 = __ldg((const float4*)(arow + (ch + 1) * 16));
+      a1 = __ldg((const float4*)(arow + (ch + 1) * 16 + 4));
+    }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const float* hv = sh + (size_t)(tl + u) * d + ch * 16 + half * 8;
       const float4 b0 = *(const float4*)hv, b1 = *(const float4*)(hv + 4);
-      acc[u][0] = fmaf(a0.x, b0.x, acc[u][0]); acc[u][1] = fmaf(a0.y, b0.y, acc[u][1]);
-      acc[u][2] = fmaf(a0.z, b0.z, acc[u][2]); acc[u][3] = fmaf(a0.w, b0.w, acc[u][3]);
-      acc[u][4] = fmaf(a1.x, b1.x, acc[u][4]); acc[u][5] = fmaf(a1.y, b1.y, acc[u][5]);
-      acc[u][6] = fmaf(a1.z, b1.z, acc[u][6]); acc[u][7] = fmaf(a1.w, b1.w, acc[u][7]);
+      acc[u][0] = __ffma2_rn(av[0], make_float2(b0.x, b0.y), acc[u][0]);
+      acc[u][1] = __ffma2_rn(av[1], make_float2(b0.z, b0.w), acc[u][1]);
+      acc[u][2] = __ffma2_rn(av[2], make_float2(b1.x, b1.y), acc[u][2]);
+      acc[u][3] = __ffma2_rn(av[3], make_float2(b1.z, b1.w), acc[u][3]);
     }
   }
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
-    const float z = reduce16_pair(acc[u]);
+    const float a8[8] = {acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y, acc[u][2].x, acc[u][2].y, acc[u][3].x, acc[u][3].y};
+    const float z = reduce16_pair(a8);
     const int t = tok0 + tl + u;
     if (half == 0 && c < k && t < T) cl[(size_t)t * k + c] = add(z, bias[c]);
   }
@@ -523,7 +662,7 @@ void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, 
 
 void launch_seq_norm(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d, int T,
                      int8_t* aq, float* as, float* xn_out, cudaStream_t st) {
-  size_t sm = (size_t)kNormWarps * 2 * d * 4;
+  size_t sm = (size_t)(kNormWarps + 1) * 2 * d * 4;
   static bool init = false;
   if (!init) {
     cudaFuncSetAttribute(k_seq_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -540,32 +679,71 @@ bool seq_gemm_supported(const MatView& w) {
   return true;
 }
 
-void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, cudaStream_t st) {
-  dim3 grid((T + kGemmBN - 1) / kGemmBN, (w.rows + kGemmBM - 1) / kGemmBM);
-#define F(B, S)                                                                                              \
-  do {                                                                                                       \
-    static bool init = false;                                                                                \
-    if (!init) {                                                                                             \
-      cudaFuncSetAttribute(k_seq_gemm<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmTile<B, S>::SMEM); \
-      init = true;                                                                                           \
-    }                                                                                                        \
-    k_seq_gemm<B, S><<<grid, kGemmThreads, GemmTile<B, S>::SMEM, st>>>(w, aq, as, T, y, ldy);                \
+// Tile choice: estimated time = waves x time of one wave, with 2 resident CTAs per SM for 8 positions
+// per thread and 3 for 4 (register-bound occupancy); a wave of 4-position tiles (48 positions per SM)
+// takes about 0.78 of a wave of 8-position tiles (64 per SM), as measured on B200.
+static int gemm_rn(int rows, int T, int sms) {
+  static const int forced = [] {  // tuning override: GEM_GEMM_RN=4 or 8
+    const char* e = std::getenv("GEM_GEMM_RN");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced == 4 || forced == 8) return forced;
+  const long long c8 = (long long)((T + 31) / 32) * ((rows + kGemmBM - 1) / kGemmBM);
+  const long long c4 = (long long)((T + 15) / 16) * ((rows + kGemmBM - 1) / kGemmBM);
+  const double t8 = (double)((c8 + 2LL * sms - 1) / (2LL * sms));
+  const double t4 = 0.78 * (double)((c4 + 3LL * sms - 1) / (3LL * sms));
+  return t4 < t8 ? 4 : 8;
+}
+
+void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
+                     cudaStream_t st) {
+  const int rn = gemm_rn(w.rows, T, sms);
+#define F2(B, S, RNV)                                                                                            \
+  do {                                                                                                          \
+    using GT = GemmTile<B, S, RNV>;                                                                             \
+    static bool init = false;                                                                                   \
+    if (!init) {                                                                                                \
+      cudaFuncSetAttribute(k_seq_gemm<B, S, RNV>, cudaFuncAttributeMaxDynamicSharedMemorySize, GT::SMEM);       \
+      init = true;                                                                                              \
+    }                                                                                                           \
+    dim3 grid((T + GT::BN - 1) / GT::BN, (w.rows + kGemmBM - 1) / kGemmBM);                                    \
+    k_seq_gemm<B, S, RNV><<<grid, kGemmThreads, GT::SMEM, st>>>(w, aq, as, T, y, ldy);                          \
+  } while (0)
+#define F(B, S)             \
+  do {                      \
+    if (rn == 8) F2(B, S, 8); \
+    else F2(B, S, 4);        \
   } while (0)
   GEM_DISPATCH_Q(w.bits, w.scale_f32, F);
 #undef F
+#undef F2
 }
 
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uint32_t pos0, float* qn, float* scores,
-                     int sstride, int threads, int8_t* aq, float* as, cudaStream_t st) {
+                     int sstride, int threads, float* part, int8_t* aq, float* as, cudaStream_t st) {
   const int G = A.nh / A.nkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return;  // rejected by the caller before any launch
   k_seq_attn_prep<<<dim3(T, A.nkv), 256, (size_t)(G + 2) * A.hd * 4, st>>>(A, qkv, qkv_ld, pos0, qn);
-  const size_t qsm = (size_t)A.nh * A.hd * 4;
-#define F(GG) k_seq_scores<GG><<<T, 256, qsm, st>>>(A, qn, pos0, scores, sstride)
+  const uint32_t pbase = window_lo(pos0, A.window);
+  const int nchunk = (int)((pos0 + T - pbase + kAttnPC - 1) / kAttnPC);
+  const dim3 sgrid((T + kAttnTQ - 1) / kAttnTQ, nchunk, A.nkv), pgrid((T + kAttnTQ - 1) / kAttnTQ, threads);
+  const size_t ssm = ((size_t)kAttnTQ * G * (A.hd + 4) + (size_t)kAttnPC * A.hd) * 4;
+  const size_t psm = ((size_t)kPvRows * A.hd + (size_t)kAttnTQ * G * kPvRows) * 4;
+  const int pth = A.hd / 2;
+#define F(GG)                                                                                                        \
+  do {                                                                                                               \
+    static bool init = false;                                                                                        \
+    if (!init) {                                                                                                     \
+      cudaFuncSetAttribute(k_seq_scores_tile<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);         \
+      cudaFuncSetAttribute(k_seq_pv_tile<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);             \
+      init = true;                                                                                                   \
+    }                                                                                                                \
+    k_seq_scores_tile<GG><<<sgrid, 256, ssm, st>>>(A, qn, T, pos0, pbase, scores, sstride);                          \
+  } while (0)
   if (G == 1) F(1);
   else if (G == 2) F(2);
   else if (G == 4) F(4);
-  else if (G == 8) F(8);
-  else return;  // other group sizes are rejected by the caller before any launch
+  else F(8);
 #undef F
   {
     static bool init = false;
@@ -573,15 +751,20 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uin
       cudaFuncSetAttribute(k_seq_softmax, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       init = true;
     }
-    const int nw = (int)std::max<size_t>(1, std::min<size_t>(8, (size_t)(200 * 1024) / ((size_t)sstride * 4)));
-    k_seq_softmax<<<(T * A.nh + nw - 1) / nw, nw * 32, (size_t)nw * sstride * 4, st>>>(A, T, pos0, scores, sstride);
+    const size_t es = ((size_t)sstride + 3) & ~(size_t)3;
+    const int nw = (int)std::max<size_t>(1, std::min<size_t>(8, (size_t)(200 * 1024) / (es * 4)));
+    k_seq_softmax<<<(T * A.nh + nw - 1) / nw, nw * 32, (size_t)nw * es * 4, st>>>(A, T, pos0, scores, sstride);
   }
-  k_seq_pv<<<T, A.hd, 0, st>>>(A, pos0, scores, sstride, threads, aq, as);
+  if (G == 1) k_seq_pv_tile<1><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
+  else if (G == 2) k_seq_pv_tile<2><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
+  else if (G == 4) k_seq_pv_tile<4><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
+  else k_seq_pv_tile<8><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
+  k_seq_pv_combine<<<dim3(T, A.nh), A.hd, 0, st>>>(A, part, threads, aq, as);
 }
 
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st) {
   const long long tasks = (long long)T * (ff / 32);
-  const int blocks = (int)std::min<long long>((tasks + 7) / 8, (long long)sms * 16);
+  const int blocks = (int)std::min<long long>((tasks + 7) / 8, 1LL << 30);
   k_seq_glu_quant<<<blocks, 256, 0, st>>>(gu, ff, T, silu, aq, as);
 }
 
