@@ -387,7 +387,7 @@ def time_dev(torch, stream, fn, iters, flush):
 def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     """Secondary figures: the full head end to end, the head microbenchmark (full 262144x640 GEMV with
     fused log-sum-exp vs the two-level head, batch 1 and 64) and the CPU baseline."""
-    from gem_b200 import AUTO, FULL, PIPELINED, SEQUENTIAL, TWO_LEVEL, synth
+    from gem_b200 import AUTO, FULL, PIPELINED, SEQUENTIAL, TWO_LEVEL, Gemma, synth
     from oracle import oracle as orc
     out = {}
     mf_info = g.refresh_info()
@@ -409,6 +409,22 @@ def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr()),
                   2, flush)
     out["full_head"] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3)}
+    # batched scoring: 256 independent sequences x 512 positions (8 KV slots, groups of 8 sequences)
+    gb = Gemma(mf.gguf, ctx=CTX, device=torch.cuda.current_device(), max_seqs=8)
+    gb.load_twolevel(mf.twolevel)
+    bstream = torch.cuda.ExternalStream(gb.stream)
+    nseq = 256
+    btoks = np.stack([synth.tokens(SEQ_TOKENS + 1, gb.vocab, seed=2000 + s) for s in range(nseq)])
+    btd = torch.tensor(btoks.astype(np.int32), device="cuda")
+    blp = torch.empty((nseq, SEQ_TOKENS), device="cuda")
+    bam = torch.empty((nseq, SEQ_TOKENS), dtype=torch.int32, device="cuda")
+    bcall = lambda: gb.score_batch_dev(btd.data_ptr(), nseq, SEQ_TOKENS, TWO_LEVEL, blp.data_ptr(), bam.data_ptr())
+    bcall()
+    ms = time_dev(torch, bstream, bcall, 2, flush)
+    out["batched"] = {"value": round(nseq * SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+                      "workload": f"{nseq} sequences x {SEQ_TOKENS} positions, two-level head, one step = the whole batch",
+                      "gpu_launches_per_step": gb.last_launches()}
+    gb.close()
     # head microbenchmark: h ~ N(0, 1)
     peak, _ = hbm_peak()
     head_bytes = g.info["head_bytes"]

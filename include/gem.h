@@ -137,12 +137,21 @@ int gem_twolevel_logprob(gem_model* m, uint32_t target, float* logprob, uint32_t
 /* gem bench / gem check's scoring loop (main.rs:270-289) on sequence 0: BOS forward when the model
  * has one, then for i < n: forward(toks[i], i + off), head logprob of toks[i + 1]. toks has n + 1
  * entries; logprob_out / argmax_out have n (argmax_out may be NULL). head: 0 full, 1 two-level.
- * Host buffers; the whole loop runs on the device as one CUDA graph per token. */
+ * Host buffers; the loop runs on the device under the schedule gem_set_schedule selects. */
 int gem_score(gem_model* m, const uint32_t* toks, size_t n, int head, float* logprob_out,
               uint32_t* argmax_out);
 /* Same loop on device buffers (toks_dev n + 1, outputs n), enqueued on the model's stream. */
 int gem_score_dev(gem_model* m, const uint32_t* toks_dev, size_t n, int head, float* logprob_dev,
                   uint32_t* argmax_dev);
+/* Batched scoring of nseq independent sequences (the bench loop run once per sequence): toks holds
+ * nseq rows of len + 1 ids, logprob_out / argmax_out nseq rows of len. Each sequence starts at
+ * position 0 (after the BOS forward) with its own KV slot; the parallel schedule scores up to
+ * max_seqs (gem_open) sequences at once. No counterpart in the reference, which scores one text. */
+int gem_score_batch(gem_model* m, const uint32_t* toks, size_t nseq, size_t len, int head, float* logprob_out,
+                    uint32_t* argmax_out);
+/* Same on device buffers, enqueued on the model's stream. */
+int gem_score_batch_dev(gem_model* m, const uint32_t* toks_dev, size_t nseq, size_t len, int head,
+                        float* logprob_dev, uint32_t* argmax_dev);
 
 /* Kernel-level entry points on caller-provided DEVICE buffers, enqueued on the model's stream.
  * They stand in for q8::matvec (q8.rs:439-461) with Act::quantize (q8.rs:187-246) fused in front,

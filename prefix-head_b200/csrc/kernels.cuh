@@ -139,8 +139,11 @@ void launch_seq_norm(float* x, const float* delta, const float* w_post, const fl
 bool seq_gemm_supported(const MatView& w);
 void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
                      cudaStream_t st);
-void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uint32_t pos0, float* qn, float* scores,
-                     int sstride, int threads, float* part, int8_t* aq, float* as, cudaStream_t st);
+void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
+                     float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
+                     cudaStream_t st);
+void launch_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin, uint32_t* tgt,
+                              cudaStream_t st);
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st);
 void launch_seq_class_logits(const float* A, const float* b, int k, const float* h, int d, int T, float* cl,
                              cudaStream_t st);

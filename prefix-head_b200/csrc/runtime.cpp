@@ -126,10 +126,13 @@ struct gem_model {
   int withhold_stage = -1;                     // failure-detection test hook
   unsigned long long* prof = nullptr;          // per-stage phase times of pipelined runs (nullable)
   // sequence-parallel scoring (seq.cu): buffers for up to seq_cap positions
-  static constexpr int kSeqChunk = 1024;  // positions per chunk
-  static constexpr int kHeadChunk = 256;  // positions per full-head logits pass
+  static constexpr int kSeqChunk = 1024;   // positions of one sequence per chunk
+  static constexpr int kBatchRows = 4096;  // positions of all sequences per chunk (batched scoring)
+  static constexpr int kHeadChunk = 256;   // positions per full-head logits pass
   int seq_cap = 0, seq_sstride = 0, logits_cap = 0, part_cap = 0;
   float* s_part = nullptr;  // P.V partials [T][nh][ref_threads][hd]
+  uint32_t *s_tin = nullptr, *s_tgt = nullptr, *s_am = nullptr;  // chunk token ids, targets, argmax
+  float* s_lp = nullptr;                                           // chunk log-probs
   float *s_x = nullptr, *s_y = nullptr, *s_gu = nullptr, *s_dn = nullptr, *s_h = nullptr, *s_qn = nullptr,
         *s_scores = nullptr, *s_logits = nullptr;
   int8_t *s_aq = nullptr, *s_haq = nullptr;
@@ -155,6 +158,21 @@ struct gem_model {
       }
   }
   bool have_h = false;
+  // host-buffer batched scoring: device copies of the ids and outputs
+  uint32_t *btoks = nullptr, *bam = nullptr;
+  float* blp = nullptr;
+  size_t btoks_cap = 0, bout_cap = 0;
+  void ensure_batch_io(size_t ntoks, size_t nout) {
+    if (ntoks > btoks_cap) {
+      btoks = alloc<uint32_t>(ntoks);
+      btoks_cap = ntoks;
+    }
+    if (nout > bout_cap) {
+      blp = alloc<float>(nout);
+      bam = alloc<uint32_t>(nout);
+      bout_cap = nout;
+    }
+  }
 
   ~gem_model() {
     if (st) cudaStreamSynchronize(st);
@@ -328,6 +346,10 @@ struct gem_model {
     s_as = alloc<float>((size_t)T * wide / 32);
     s_haq = alloc<int8_t>((size_t)T * d);
     s_has = alloc<float>((size_t)T * d / 32);
+    s_tin = alloc<uint32_t>(T);
+    s_tgt = alloc<uint32_t>(T);
+    s_am = alloc<uint32_t>(T);
+    s_lp = alloc<float>(T);
     seq_cap = T;
   }
 
@@ -390,8 +412,15 @@ struct gem_model {
     ++par_calls;
   }
 
-  void score_parallel(const uint32_t* toks_d, size_t n, int which, uint32_t base_pos, float* lp_d, uint32_t* am_d) {
-    const int cap = (int)std::min<size_t>(n, kSeqChunk);
+  // Scoring with every position of a chunk going through each layer together. toks_d holds nseq
+  // sequences of len + 1 ids, `stride` ids apart; sequence s's log-probs of ids 1..len go to
+  // lp_d[s * len ..] (argmax likewise). A chunk holds up to kBatchRows positions of whole sequences
+  // (each in its own KV slot) or kSeqChunk positions of one long sequence.
+  void score_parallel(const uint32_t* toks_d, size_t stride, int nseq, size_t len, int which, uint32_t base_pos,
+                      float* lp_d, uint32_t* am_d) {
+    const int L = (int)std::min<size_t>(len, kSeqChunk);
+    const int SC = std::max(1, std::min({nseq, max_seqs, kBatchRows / L}));
+    const int cap = L * SC;
     ensure_seq(cap);
     if ((int64_t)cap * ref_threads > part_cap) {
       s_part = alloc<float>((size_t)cap * ref_threads * nh * hd);
@@ -399,41 +428,57 @@ struct gem_model {
     }
     const DevMat& E = untied ? emb : head;
     const int qkv_rows = (nh + 2 * nkv) * hd;
+    const size_t kv_stride = (size_t)nl * ctx * nkv * hd;  // between the KV slots of two sequences
     int T = 0;
     int64_t nk = 0;
     pcat.clear();
     par_mark(-1);
-    for (size_t c0 = 0; c0 < n; c0 += cap) {
-      T = (int)std::min<size_t>(cap, n - c0);
-      const uint32_t pos0 = base_pos + (uint32_t)c0;
-      launch_seq_embed(E.v, toks_d + c0, T, vocab, embed_scale, s_x, err, st);
-      par_mark(PAR_EMBED);
-      for (int l = 0; l < nl; ++l) {
-        const Layer& L = layers[l];
-        const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
-        launch_seq_norm(s_x, P ? s_dn : nullptr, P ? P->post_ffw : nullptr, L.attn_norm, eps, d, T, s_aq, s_as, nullptr, st);
+    // positions start after a BOS forward in slot 0: the other slots get its K/V rows (position 0 is
+    // never rewritten, so one copy serves every group of sequences)
+    if (base_pos > 0)
+      for (int s = 1; s < SC; ++s) copy_bos_kv(s);
+    for (int s0 = 0; s0 < nseq; s0 += SC) {
+      const int ns = std::min(SC, nseq - s0);
+      for (size_t c0 = 0; c0 < len; c0 += L) {
+        const int Lc = (int)std::min<size_t>(L, len - c0);
+        T = Lc * ns;
+        const uint32_t pos0 = base_pos + (uint32_t)c0;
+        launch_seq_gather_tokens(toks_d + (size_t)s0 * stride, stride, Lc, (int)c0, T, s_tin, s_tgt, st);
+        launch_seq_embed(E.v, s_tin, T, vocab, embed_scale, s_x, err, st);
+        par_mark(PAR_EMBED);
+        for (int l = 0; l < nl; ++l) {
+          const Layer& Ly = layers[l];
+          const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
+          launch_seq_norm(s_x, P ? s_dn : nullptr, P ? P->post_ffw : nullptr, Ly.attn_norm, eps, d, T, s_aq, s_as, nullptr, st);
+          par_mark(PAR_NORM);
+          launch_seq_gemm(Ly.qkv.v, s_aq, s_as, T, s_y, qkv_rows, sms, st);
+          par_mark(PAR_QKV);
+          launch_seq_attn(attn_args(l, 0), s_y, qkv_rows, Lc, ns, pos0, kv_stride, s_qn, s_scores, seq_sstride, ref_threads,
+                          s_part, s_aq, s_as, st);
+          par_mark(PAR_ATTN);
+          launch_seq_gemm(Ly.o.v, s_aq, s_as, T, s_y, d, sms, st);
+          par_mark(PAR_O);
+          launch_seq_norm(s_x, s_y, Ly.post_attn, Ly.ffn_norm, eps, d, T, s_aq, s_as, nullptr, st);
+          par_mark(PAR_NORM);
+          launch_seq_gemm(Ly.gu.v, s_aq, s_as, T, s_gu, 2 * ff, sms, st);
+          par_mark(PAR_GU);
+          launch_seq_glu_quant(s_gu, ff, T, silu ? 1 : 0, s_aq, s_as, sms, st);
+          par_mark(PAR_GLU);
+          launch_seq_gemm(Ly.down.v, s_aq, s_as, T, s_dn, d, sms, st);
+          par_mark(PAR_DOWN);
+          nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
+        }
+        launch_seq_norm(s_x, s_dn, layers[nl - 1].post_ffw, out_norm, eps, d, T, s_haq, s_has, s_h, st);
         par_mark(PAR_NORM);
-        launch_seq_gemm(L.qkv.v, s_aq, s_as, T, s_y, qkv_rows, sms, st);
-        par_mark(PAR_QKV);
-        launch_seq_attn(attn_args(l, 0), s_y, qkv_rows, T, pos0, s_qn, s_scores, seq_sstride, ref_threads, s_part, s_aq,
-                        s_as, st);
-        par_mark(PAR_ATTN);
-        launch_seq_gemm(L.o.v, s_aq, s_as, T, s_y, d, sms, st);
-        par_mark(PAR_O);
-        launch_seq_norm(s_x, s_y, L.post_attn, L.ffn_norm, eps, d, T, s_aq, s_as, nullptr, st);
-        par_mark(PAR_NORM);
-        launch_seq_gemm(L.gu.v, s_aq, s_as, T, s_gu, 2 * ff, sms, st);
-        par_mark(PAR_GU);
-        launch_seq_glu_quant(s_gu, ff, T, silu ? 1 : 0, s_aq, s_as, sms, st);
-        par_mark(PAR_GLU);
-        launch_seq_gemm(L.down.v, s_aq, s_as, T, s_dn, d, sms, st);
-        par_mark(PAR_DOWN);
-        nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
+        nk += 4 + seq_head(which, s_tgt, T, s_lp, s_am);
+        par_mark(PAR_HEAD);
+        // rows [seq][Lc] of the chunk into [seq][len] of the caller's outputs
+        ck(cudaMemcpy2DAsync(lp_d + (size_t)s0 * len + c0, len * 4, s_lp, (size_t)Lc * 4, (size_t)Lc * 4, ns,
+                             cudaMemcpyDeviceToDevice, st), "lp");
+        if (am_d)
+          ck(cudaMemcpy2DAsync(am_d + (size_t)s0 * len + c0, len * 4, s_am, (size_t)Lc * 4, (size_t)Lc * 4, ns,
+                               cudaMemcpyDeviceToDevice, st), "am");
       }
-      launch_seq_norm(s_x, s_dn, layers[nl - 1].post_ffw, out_norm, eps, d, T, s_haq, s_has, s_h, st);
-      par_mark(PAR_NORM);
-      nk += 2 + seq_head(which, toks_d + c0 + 1, T, lp_d + c0, am_d ? am_d + c0 : nullptr);
-      par_mark(PAR_HEAD);
     }
     last_launches = nk;
     par_collect();
@@ -441,6 +486,15 @@ struct gem_model {
     ck(cudaMemcpyAsync(h, s_h + (size_t)(T - 1) * d, (size_t)d * 4, cudaMemcpyDeviceToDevice, st), "h");
     ck(cudaMemcpyAsync(haq, s_haq + (size_t)(T - 1) * d, (size_t)d, cudaMemcpyDeviceToDevice, st), "haq");
     ck(cudaMemcpyAsync(has, s_has + (size_t)(T - 1) * (d / 32), (size_t)d / 32 * 4, cudaMemcpyDeviceToDevice, st), "has");
+  }
+
+  // The BOS position's K/V rows (position 0 of every layer) from KV slot 0 into slot `s`: every
+  // sequence starts with the same BOS forward (main.rs:270-272).
+  void copy_bos_kv(int s) {
+    const size_t le = (size_t)ctx * nkv * hd, rw = (size_t)nkv * hd;
+    for (float* c : {kc, vc})
+      ck(cudaMemcpy2DAsync(c + (size_t)s * nl * le, le * 4, c, le * 4, rw * 4, nl, cudaMemcpyDeviceToDevice, st),
+         "bos kv");
   }
 
   // Can the two-level scoring loop run as one layer-pipelined kernel on this model and GPU?
@@ -1077,7 +1131,7 @@ static void run_score(gem_model* m, size_t n, int head) {
     m->enqueue_body(0);
   }
   if (m->use_parallel()) {
-    m->score_parallel(m->toks, n, head, (uint32_t)off, m->lp, m->am);
+    m->score_parallel(m->toks, n + 1, 1, n, head, (uint32_t)off, m->lp, m->am);
     m->have_h = true;
     return;
   }
@@ -1148,6 +1202,60 @@ int gem_score_dev(gem_model* m, const uint32_t* toks_dev, size_t n, int head, fl
   run_score(m, n, head);
   ck(cudaMemcpyAsync(logprob_dev, m->lp, n * 4, cudaMemcpyDeviceToDevice, m->st), "lp");
   if (argmax_dev) ck(cudaMemcpyAsync(argmax_dev, m->am, n * 4, cudaMemcpyDeviceToDevice, m->st), "am");
+  API_END
+}
+
+// Batched scoring: nseq independent sequences of len + 1 ids (device buffers).
+static void run_score_batch(gem_model* m, const uint32_t* toks_d, size_t nseq, size_t len, int head, float* lp_d,
+                            uint32_t* am_d) {
+  if (head != 0 && head != 1) throw Error(GEM_E_ARG, "head must be 0 (full) or 1 (two-level)");
+  if (head == 1 && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  const size_t off = m->bos >= 0 ? 1 : 0;
+  if (len + off > (size_t)m->ctx) throw Error(GEM_E_RANGE, "sequence longer than ctx");
+  if (nseq > (size_t)INT32_MAX) throw Error(GEM_E_RANGE, "too many sequences");
+  if (m->use_parallel()) {
+    if (m->bos >= 0) {  // main.rs:270-272, once: every sequence shares the BOS position's K/V rows
+      *m->cur_host = StepCur{(uint32_t)m->bos, 0, 0, 0};
+      ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+      m->enqueue_body(0);
+    }
+    m->score_parallel(toks_d, len + 1, (int)nseq, len, head, (uint32_t)off, lp_d, am_d);
+    m->have_h = true;
+    return;
+  }
+  for (size_t s = 0; s < nseq; ++s) {  // per-token schedules: one sequence after another in slot 0
+    ck(cudaMemcpyAsync(m->toks, toks_d + s * (len + 1), (len + 1) * 4, cudaMemcpyDeviceToDevice, m->st), "toks");
+    run_score(m, len, head);
+    ck(cudaMemcpyAsync(lp_d + s * len, m->lp, len * 4, cudaMemcpyDeviceToDevice, m->st), "lp");
+    if (am_d) ck(cudaMemcpyAsync(am_d + s * len, m->am, len * 4, cudaMemcpyDeviceToDevice, m->st), "am");
+  }
+}
+
+int gem_score_batch(gem_model* m, const uint32_t* toks, size_t nseq, size_t len, int head, float* logprob_out,
+                    uint32_t* argmax_out) {
+  API_BEGIN
+  if (!m || !toks || !logprob_out) throw Error(GEM_E_ARG, "null argument");
+  if (nseq == 0 || len == 0) return GEM_OK;
+  const size_t nt = nseq * (len + 1);
+  for (size_t i = 0; i < nt; ++i)
+    if (toks[i] >= (uint32_t)m->vocab) throw Error(GEM_E_RANGE, "token id >= vocab");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->ensure_batch_io(nt, nseq * len);
+  ck(cudaMemcpyAsync(m->btoks, toks, nt * 4, cudaMemcpyHostToDevice, m->st), "toks");
+  run_score_batch(m, m->btoks, nseq, len, head, m->blp, m->bam);
+  ck(cudaMemcpyAsync(logprob_out, m->blp, nseq * len * 4, cudaMemcpyDeviceToHost, m->st), "lp");
+  if (argmax_out) ck(cudaMemcpyAsync(argmax_out, m->bam, nseq * len * 4, cudaMemcpyDeviceToHost, m->st), "am");
+  m->sync();
+  API_END
+}
+
+int gem_score_batch_dev(gem_model* m, const uint32_t* toks_dev, size_t nseq, size_t len, int head, float* logprob_dev,
+                        uint32_t* argmax_dev) {
+  API_BEGIN
+  if (!m || !toks_dev || !logprob_dev) throw Error(GEM_E_ARG, "null argument");
+  if (nseq == 0 || len == 0) return GEM_OK;
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  run_score_batch(m, toks_dev, nseq, len, head, logprob_dev, argmax_dev);
   API_END
 }
 

@@ -305,14 +305,25 @@ __global__ void __launch_bounds__(kGemmThreads, RN == 8 ? 2 : 3) k_seq_gemm(MatV
 }
 
 // ------------------------------------------------------------------------------------------------
-// Attention, exact, for positions pos0 .. pos0 + T - 1 of one sequence.
+// Attention, exact. The chunk holds `nseq` sequences of L positions each, rows ordered [seq][pos]:
+// row t is position pos0 + t % L of sequence t / L, whose K/V cache starts kv_stride floats after the
+// previous sequence's.
 // ------------------------------------------------------------------------------------------------
 // QK-norm, RoPE, scale, K/V append: one CTA per (position, kv group).
-__global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, uint32_t pos0, float* qn) {
+__device__ __forceinline__ AttnArgs seq_kv(const AttnArgs& A, int s, size_t kv_stride) {
+  AttnArgs a = A;
+  a.kcache += (size_t)s * kv_stride;
+  a.vcache += (size_t)s * kv_stride;
+  return a;
+}
+
+__global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, int L, uint32_t pos0, size_t kv_stride,
+                                float* qn) {
   extern __shared__ __align__(16) float smp[];
   __shared__ float s_r[17];
-  const int t = blockIdx.x;
-  attn_prep_token(A, qkv + (size_t)t * qkv_ld, pos0 + t, blockIdx.y, qn + (size_t)t * A.nh * A.hd, smp, s_r);
+  const int t = blockIdx.x, s = t / L;
+  attn_prep_token(seq_kv(A, s, kv_stride), qkv + (size_t)t * qkv_ld, pos0 + t % L, blockIdx.y,
+                  qn + (size_t)t * A.nh * A.hd, smp, s_r);
 }
 
 // Tiled scores: a CTA takes kAttnTQ consecutive positions (rows: position x query head of kv group
@@ -323,12 +334,16 @@ __global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, uint32
 constexpr int kAttnTQ = 8, kAttnPC = 64;
 
 template <int G>
-__global__ void __launch_bounds__(256) k_seq_scores_tile(AttnArgs A, const float* qn, int T, uint32_t pos0,
-                                                         uint32_t pbase, float* scores, int sstride) {
+__global__ void __launch_bounds__(256) k_seq_scores_tile(AttnArgs A0, const float* qn, int L, uint32_t pos0,
+                                                         size_t kv_stride, uint32_t pbase, float* scores, int sstride) {
   extern __shared__ __align__(16) float sm[];
-  constexpr int R = kAttnTQ * G;  // a multiple of 4 (kAttnTQ = 8)
+  constexpr int R = kAttnTQ * G;
+  const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
+  const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
   const int hd = A.hd, g = blockIdx.z, qs = hd + 4;  // padded query rows: 16 rows hit distinct banks
-  const int t0 = blockIdx.x * kAttnTQ, tn = min(kAttnTQ, T - t0);
+  const int t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0);  // positions inside the sequence
+  qn += (size_t)sq_i * L * A.nh * hd;                                        // this sequence's rows
+  scores += (size_t)sq_i * L * A.nh * sstride;
   const uint32_t p0 = pbase + blockIdx.y * kAttnPC;
   const uint32_t need_lo = window_lo(pos0 + t0, A.window), need_hi = pos0 + t0 + tn - 1;
   if (p0 > need_hi || p0 + kAttnPC <= need_lo) return;
@@ -392,13 +407,13 @@ __global__ void __launch_bounds__(256) k_seq_scores_tile(AttnArgs A, const float
 
 // Softmax per (position, head) with the reference's order: max, exp_fast(s - max), sequential sum,
 // multiply by 1/sum. One warp per (position, head).
-__global__ void k_seq_softmax(AttnArgs A, int T, uint32_t pos0, float* scores, int sstride) {
+__global__ void k_seq_softmax(AttnArgs A, int T, int L, uint32_t pos0, float* scores, int sstride) {
   extern __shared__ __align__(16) float ss[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int task = blockIdx.x * nw + warp;
   if (task >= T * A.nh) return;
   const int t = task / A.nh;
-  const uint32_t pos = pos0 + t, lo = window_lo(pos, A.window);
+  const uint32_t pos = pos0 + t % L, lo = window_lo(pos, A.window);
   const int n = (int)(pos + 1 - lo);
   float* s = scores + (size_t)task * sstride;
   float* e = ss + (size_t)warp * ((sstride + 3) & ~3);  // 16-byte aligned rows
@@ -435,12 +450,16 @@ __global__ void k_seq_softmax(AttnArgs A, int T, uint32_t pos0, float* scores, i
 constexpr int kPvRows = 32;
 
 template <int G>
-__global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A, int T, uint32_t pos0, const float* scores,
-                                                     int sstride, int threads, float* part) {
+__global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_t pos0, size_t kv_stride,
+                                                     const float* scores, int sstride, int threads, float* part) {
   constexpr int R = kAttnTQ * G;               // rows of the tile: position x head of the group
   extern __shared__ __align__(16) float sv[];  // V [kPvRows][hd], then probabilities P [R][kPvRows]
   __shared__ uint32_t s_lo[kAttnTQ], s_a[kAttnTQ], s_b[kAttnTQ];
-  const int hd = A.hd, h4 = hd / 4, t0 = blockIdx.x * kAttnTQ, tn = min(kAttnTQ, T - t0), r = blockIdx.y;
+  const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
+  const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
+  scores += (size_t)sq_i * L * A.nh * sstride;
+  part += (size_t)sq_i * L * A.nh * threads * A.hd;
+  const int hd = A.hd, h4 = hd / 4, t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0), r = blockIdx.y;
   const int j2 = threadIdx.x * 2;  // this thread's two output columns
   const int rw = A.nkv * hd;
   float* sp = sv + kPvRows * hd;
@@ -719,14 +738,16 @@ void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T,
 #undef F2
 }
 
-void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uint32_t pos0, float* qn, float* scores,
-                     int sstride, int threads, float* part, int8_t* aq, float* as, cudaStream_t st) {
-  const int G = A.nh / A.nkv;
+void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
+                     float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
+                     cudaStream_t st) {
+  const int G = A.nh / A.nkv, T = L * nseq;
   if (G != 1 && G != 2 && G != 4 && G != 8) return;  // rejected by the caller before any launch
-  k_seq_attn_prep<<<dim3(T, A.nkv), 256, (size_t)(G + 2) * A.hd * 4, st>>>(A, qkv, qkv_ld, pos0, qn);
+  k_seq_attn_prep<<<dim3(T, A.nkv), 256, (size_t)(G + 2) * A.hd * 4, st>>>(A, qkv, qkv_ld, L, pos0, kv_stride, qn);
   const uint32_t pbase = window_lo(pos0, A.window);
-  const int nchunk = (int)((pos0 + T - pbase + kAttnPC - 1) / kAttnPC);
-  const dim3 sgrid((T + kAttnTQ - 1) / kAttnTQ, nchunk, A.nkv), pgrid((T + kAttnTQ - 1) / kAttnTQ, threads);
+  const int nchunk = (int)((pos0 + L - pbase + kAttnPC - 1) / kAttnPC);
+  const int tps = (L + kAttnTQ - 1) / kAttnTQ;
+  const dim3 sgrid(tps * nseq, nchunk, A.nkv), pgrid(tps * nseq, threads);
   const size_t ssm = ((size_t)kAttnTQ * G * (A.hd + 4) + (size_t)kAttnPC * A.hd) * 4;
   const size_t psm = ((size_t)kPvRows * A.hd + (size_t)kAttnTQ * G * kPvRows) * 4;
   const int pth = A.hd / 2;
@@ -738,7 +759,7 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uin
       cudaFuncSetAttribute(k_seq_pv_tile<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);             \
       init = true;                                                                                                   \
     }                                                                                                                \
-    k_seq_scores_tile<GG><<<sgrid, 256, ssm, st>>>(A, qn, T, pos0, pbase, scores, sstride);                          \
+    k_seq_scores_tile<GG><<<sgrid, 256, ssm, st>>>(A, qn, L, pos0, kv_stride, pbase, scores, sstride);               \
   } while (0)
   if (G == 1) F(1);
   else if (G == 2) F(2);
@@ -753,13 +774,30 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int T, uin
     }
     const size_t es = ((size_t)sstride + 3) & ~(size_t)3;
     const int nw = (int)std::max<size_t>(1, std::min<size_t>(8, (size_t)(200 * 1024) / (es * 4)));
-    k_seq_softmax<<<(T * A.nh + nw - 1) / nw, nw * 32, (size_t)nw * es * 4, st>>>(A, T, pos0, scores, sstride);
+    k_seq_softmax<<<(T * A.nh + nw - 1) / nw, nw * 32, (size_t)nw * es * 4, st>>>(A, T, L, pos0, scores, sstride);
   }
-  if (G == 1) k_seq_pv_tile<1><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
-  else if (G == 2) k_seq_pv_tile<2><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
-  else if (G == 4) k_seq_pv_tile<4><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
-  else k_seq_pv_tile<8><<<pgrid, pth, psm, st>>>(A, T, pos0, scores, sstride, threads, part);
+#define P(GG) k_seq_pv_tile<GG><<<pgrid, pth, psm, st>>>(A, L, pos0, kv_stride, scores, sstride, threads, part)
+  if (G == 1) P(1);
+  else if (G == 2) P(2);
+  else if (G == 4) P(4);
+  else P(8);
+#undef P
   k_seq_pv_combine<<<dim3(T, A.nh), A.hd, 0, st>>>(A, part, threads, aq, as);
+}
+
+// Token ids and targets of a chunk: rows [seq][pos] read toks[seq * stride + c0 + pos] and the next id.
+__global__ void k_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin,
+                                    uint32_t* tgt) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const size_t i = (size_t)(t / L) * stride + c0 + t % L;
+  tin[t] = toks[i];
+  tgt[t] = toks[i + 1];
+}
+
+void launch_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin, uint32_t* tgt,
+                              cudaStream_t st) {
+  k_seq_gather_tokens<<<(T + 255) / 256, 256, 0, st>>>(toks, stride, L, c0, T, tin, tgt);
 }
 
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st) {

@@ -81,6 +81,8 @@ def lib():
     L.gem_twolevel_logprob.argtypes = [vp, C.c_uint32, _f32p, _u32p]
     L.gem_score.argtypes = [vp, _u32p, C.c_size_t, C.c_int, _f32p, _u32p]
     L.gem_score_dev.argtypes = [vp, vp, C.c_size_t, C.c_int, vp, vp]
+    L.gem_score_batch.argtypes = [vp, _u32p, C.c_size_t, C.c_size_t, C.c_int, _f32p, _u32p]
+    L.gem_score_batch_dev.argtypes = [vp, vp, C.c_size_t, C.c_size_t, C.c_int, vp, vp]
     L.gem_matvec_dev.argtypes = [vp, C.c_int, C.c_int, vp, vp]
     L.gem_head_full_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
     L.gem_head_twolevel_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
@@ -234,6 +236,19 @@ class Gemma:
     def score_dev(self, toks_ptr: int, n: int, head: int, lp_ptr: int, am_ptr: int | None):
         """Same loop on device buffers (ints: device addresses); asynchronous on the model's stream."""
         _check(lib().gem_score_dev(self._h, toks_ptr, n, head, lp_ptr, am_ptr))
+
+    def score_batch(self, toks: np.ndarray, head: int = TWO_LEVEL):
+        """Batched scoring: toks [nseq][len + 1] -> (logprob, argmax), each [nseq][len]."""
+        toks = np.ascontiguousarray(toks, np.uint32)
+        nseq, n = toks.shape[0], toks.shape[1] - 1
+        lp = np.zeros((nseq, n), np.float32)
+        am = np.zeros((nseq, n), np.uint32)
+        _check(lib().gem_score_batch(self._h, _p(toks, _u32p), nseq, n, head, _p(lp, _f32p), _p(am, _u32p)))
+        return lp, am
+
+    def score_batch_dev(self, toks_ptr: int, nseq: int, n: int, head: int, lp_ptr: int, am_ptr: int | None):
+        """Batched scoring on device buffers (toks [nseq][n + 1], outputs [nseq][n]); asynchronous."""
+        _check(lib().gem_score_batch_dev(self._h, toks_ptr, nseq, n, head, lp_ptr, am_ptr))
 
     def refresh_info(self):
         info = Info()
