@@ -46,6 +46,8 @@ def parse():
     p.add_argument("--numerics", default="exact", choices=["exact", "fast"])
     p.add_argument("--no-extras", action="store_true", help="skip the full-head / head-microbench / CPU legs")
     p.add_argument("--cpu-threads", type=int, default=0, help="oracle threads for the CPU legs (0 = all cores)")
+    p.add_argument("--workload", default="270m-two-level", choices=["270m-two-level", "1b-vocab-shard"],
+                   help="1b-vocab-shard: Gemma-3-1B geometry, 1024 positions, full head sharded over the ranks")
     return p.parse_args()
 
 
@@ -182,10 +184,89 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_vocab_shard(args):
+    """Gemma-3-1B geometry, one 1024-position sequence per step, the full head's vocabulary sharded
+    over the ranks (one GPU each) with an NCCL merge of the per-shard statistics. Every rank scores the
+    same sequence (the body is replicated), so the total work is fixed: strong scaling. The unsharded
+    two-level head on the same model is timed beside it."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from gem_b200 import FULL, TWO_LEVEL, Gemma, shard, synth
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
+    n = 1024
+    if rank == 0:
+        mf = synth.ensure("gemma3-1b", classes=2048)
+    barrier()
+    if rank != 0:
+        mf = synth.ensure("gemma3-1b", classes=2048)
+    g = Gemma(mf.gguf, ctx=2048, device=local)
+    g.load_twolevel(mf.twolevel)
+    if world > 1:
+        shard.init_vocab_shard(g)
+    stream = torch.cuda.ExternalStream(g.stream, device=local)
+    toks = torch.tensor(synth.tokens(n + 1, g.vocab, seed=3000).astype(np.int32), device="cuda")
+    lp = torch.empty(n, device="cuda")
+    am = torch.empty(n, dtype=torch.int32, device="cuda")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def timed(head, steps):
+        for _ in range(args.warmup):
+            g.score_dev(toks.data_ptr(), n, head, lp.data_ptr(), am.data_ptr())
+        torch.cuda.synchronize()
+        barrier()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in evs:
+            flush.zero_()
+            torch.cuda.synchronize()
+            a.record(stream)
+            g.score_dev(toks.data_ptr(), n, head, lp.data_ptr(), am.data_ptr())
+            b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / steps
+
+    with Clocks(local) as clk:
+        ms_full = timed(FULL, args.steps)
+    launches = g.last_launches()
+    ms_two = timed(TWO_LEVEL, args.steps)
+    if rank == 0:
+        first, rows = shard.row_range(g.vocab, world, rank)
+        line = {
+            "metric": "tokens/s scored (1B Q8_0, full head vocab-sharded across GPUs)", "value": round(n / (ms_full / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_full, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)",
+            "data": "synthetic", "numerics": "exact",
+            "config": {"workload": "gemma3-1b Q8_0, one 1024-position sequence per step, full head sharded by vocab rows",
+                       "model": "gemma3-1b geometry (d 1152, 26 layers, 4q/1kv heads, hd 256, ff 6912, vocab 262144), "
+                                "random init N(0,0.02) quantized to Q8_0",
+                       "global_batch": 1, "seq_len": n, "parallelism": f"vocab shard x{world} (body replicated)",
+                       "rows_per_rank": rows, "l2": "flushed (256 MiB write) before every step"},
+            "two_level_unsharded": {"value": round(n / (ms_two / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_two, 3)},
+            "gpu_launches": int(launches * args.steps), "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    g.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "1b-vocab-shard":
+        return run_vocab_shard(args)
     import torch
     import torch.distributed as dist
     from gem_b200 import EXACT, FAST, FULL, PARALLEL, TWO_LEVEL, Gemma, synth
@@ -307,7 +388,7 @@ def body_weights(info):
 
 def gemm_traffic():
     """DRAM bytes per step of the exact matrix products from the committed ncu summary, if present."""
-    tf = ROOT / "profiles" / "dram_bytes_per_token.txt"
+    tf = ROOT / "profiles" / "dram_traffic.txt"
     if tf.exists():
         for ln in tf.read_text().splitlines():
             if ln.startswith("k_seq_gemm per step:"):

@@ -153,6 +153,16 @@ int gem_score_batch(gem_model* m, const uint32_t* toks, size_t nseq, size_t len,
 int gem_score_batch_dev(gem_model* m, const uint32_t* toks_dev, size_t nseq, size_t len, int head,
                         float* logprob_dev, uint32_t* argmax_dev);
 
+/* Vocab-sharded full head across GPUs (one process and model handle per GPU, the body replicated):
+ * gem_shard_init splits the output matrix's rows into nranks contiguous ranges of ceil(vocab/nranks)
+ * and joins an NCCL communicator (id: 128 bytes from gem_nccl_unique_id on one rank, passed to all).
+ * Full-head scoring then computes this rank's logits, per-position partial log-sum-exp / argmax /
+ * target-logit statistics, all-gathers them over the ranks and merges them, so every rank returns the
+ * unsharded log-probs and argmax (ties: lowest token id). Needs the parallel schedule. NCCL is loaded
+ * at run time (libnccl.so.2). No counterpart in the reference, which has one CPU process. */
+int gem_nccl_unique_id(void* id_out);
+int gem_shard_init(gem_model* m, int nranks, int rank, const void* id);
+
 /* Kernel-level entry points on caller-provided DEVICE buffers, enqueued on the model's stream.
  * They stand in for q8::matvec (q8.rs:439-461) with Act::quantize (q8.rs:187-246) fused in front,
  * Full::run/logprob (main.rs:30-37) and TwoLevel::logprob (main.rs:101-107), for a batch of hidden

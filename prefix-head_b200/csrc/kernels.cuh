@@ -142,6 +142,9 @@ void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T,
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
                      float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
                      cudaStream_t st);
+void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
+                               float* out, int* err, cudaStream_t st);
+void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st);
 void launch_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin, uint32_t* tgt,
                               cudaStream_t st);
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st);

@@ -1,6 +1,8 @@
 // The C ABI of include/gem.h: model handle, load + upload, the per-token forward and heads as kernel
 // sequences on one stream, and the scoring loop as a CUDA graph per token.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -21,6 +23,32 @@
 using namespace gem;
 
 namespace {
+
+// NCCL, loaded at run time (the library has no link-time dependency on it): inside a process that
+// already uses NCCL (torch), dlopen returns that same library.
+struct Nccl {
+  void* h = nullptr;
+  decltype(&ncclGetUniqueId) get_id = nullptr;
+  decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclCommDestroy) destroy = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  bool load() {
+    if (h) return true;
+    h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return false;
+    get_id = (decltype(get_id))dlsym(h, "ncclGetUniqueId");
+    init_rank = (decltype(init_rank))dlsym(h, "ncclCommInitRank");
+    all_gather = (decltype(all_gather))dlsym(h, "ncclAllGather");
+    destroy = (decltype(destroy))dlsym(h, "ncclCommDestroy");
+    error_string = (decltype(error_string))dlsym(h, "ncclGetErrorString");
+    return get_id && init_rank && all_gather && destroy && error_string;
+  }
+};
+Nccl& nccl() {
+  static Nccl n;
+  return n;
+}
 
 thread_local std::string g_last_error;
 
@@ -138,6 +166,11 @@ struct gem_model {
   int8_t *s_aq = nullptr, *s_haq = nullptr;
   float *s_as = nullptr, *s_has = nullptr;
   std::string seq_why;  // why the sequence-parallel schedule is not used
+  // vocab-sharded full head (gem_shard_init): this rank's output-matrix rows and the communicator
+  int shard_rank = 0, shard_n = 1, shard_row0 = 0, shard_rows = 0;
+  ncclComm_t comm = nullptr;
+  float *s_spart = nullptr, *s_sgath = nullptr;
+  size_t spart_cap = 0;
   // per-category device time of parallel scoring (gem_set_profiling): events between launch groups
   enum { PAR_EMBED, PAR_NORM, PAR_QKV, PAR_ATTN, PAR_O, PAR_GU, PAR_GLU, PAR_DOWN, PAR_HEAD, PAR_CATS };
   bool par_prof = false;
@@ -177,6 +210,7 @@ struct gem_model {
   ~gem_model() {
     if (st) cudaStreamSynchronize(st);
     for (cudaEvent_t e : pev) cudaEventDestroy(e);
+    if (comm) nccl().destroy(comm);
     for (auto& g : score_graph)
       if (g) cudaGraphExecDestroy(g);
     for (void* p : owned) cudaFree(p);
@@ -367,6 +401,7 @@ struct gem_model {
       launch_tl_argmax(TL, T, top_of, top_inner, st);
       return 5;
     }
+    if (comm) return seq_head_sharded(targets, T, lpo, amo);
     if (!seq_gemm_supported(head.v)) {  // F16 output matrix: the per-position exact head kernels
       run_head(0, s_haq, s_has, s_h, targets, T, lpo, amo);
       return 2;
@@ -410,6 +445,38 @@ struct gem_model {
     }
     pcat.clear();
     ++par_calls;
+  }
+
+  // The full head over this rank's rows [shard_row0, shard_row0 + shard_rows): logits, per-position
+  // partial statistics, one all-gather of the partials over the ranks, and the merge (main.rs:30-37).
+  int seq_head_sharded(const uint32_t* targets, int T, float* lpo, uint32_t* amo) {
+    MatView w = head.v;
+    const size_t rowbytes = (size_t)w.cols * w.bits / 8, sbytes = (size_t)(w.cols / 32) * (w.scale_f32 ? 4 : 2);
+    w.q = (const unsigned char*)w.q + (size_t)shard_row0 * rowbytes;
+    w.s = (const unsigned char*)w.s + (size_t)shard_row0 * sbytes;
+    w.rows = shard_rows;
+    const int hc = std::min(T, kHeadChunk);
+    if (hc > logits_cap) {
+      s_logits = alloc<float>((size_t)hc * vocab);  // sized for the whole vocabulary: reusable unsharded
+      logits_cap = hc;
+    }
+    if ((size_t)T > spart_cap) {
+      s_spart = alloc<float>((size_t)T * 5);
+      s_sgath = alloc<float>((size_t)T * 5 * shard_n);
+      spart_cap = T;
+    }
+    int launches = 0;
+    for (int h0 = 0; h0 < T; h0 += hc) {
+      const int n = std::min(hc, T - h0);
+      launch_seq_gemm(w, s_haq + (size_t)h0 * d, s_has + (size_t)h0 * d / 32, n, s_logits, shard_rows, sms, st);
+      launch_seq_logit_partials(s_logits, shard_rows, (uint32_t)shard_row0, n, targets + h0, (uint32_t)vocab,
+                                s_spart + (size_t)h0 * 5, err, st);
+      launches += 2;
+    }
+    const ncclResult_t r = nccl().all_gather(s_spart, s_sgath, (size_t)T * 5, ncclFloat32, comm, st);
+    if (r != ncclSuccess) throw Error(GEM_E_CUDA, std::string("ncclAllGather: ") + nccl().error_string(r));
+    launch_seq_logit_combine(s_sgath, shard_n, T, lpo, amo, st);
+    return launches + 1;
   }
 
   // Scoring with every position of a chunk going through each layer together. toks_d holds nseq
@@ -1000,6 +1067,41 @@ int gem_get_schedule_kind(gem_model* m, int head, int* kind) {
   API_END
 }
 
+int gem_nccl_unique_id(void* id_out) {
+  API_BEGIN
+  if (!id_out) throw Error(GEM_E_ARG, "null argument");
+  if (!nccl().load()) throw Error(GEM_E_STATE, std::string("libnccl.so.2 not loadable: ") + dlerror());
+  ncclUniqueId id;
+  const ncclResult_t r = nccl().get_id(&id);
+  if (r != ncclSuccess) throw Error(GEM_E_CUDA, std::string("ncclGetUniqueId: ") + nccl().error_string(r));
+  std::memcpy(id_out, &id, sizeof(id));
+  API_END
+}
+
+int gem_shard_init(gem_model* m, int nranks, int rank, const void* id) {
+  API_BEGIN
+  if (!m || !id) throw Error(GEM_E_ARG, "null argument");
+  if (nranks < 1 || rank < 0 || rank >= nranks) throw Error(GEM_E_RANGE, "rank out of range");
+  if (m->comm) throw Error(GEM_E_STATE, "the head is already sharded");
+  if (!nccl().load()) throw Error(GEM_E_STATE, std::string("libnccl.so.2 not loadable: ") + dlerror());
+  if (m->head.v.bits == 16 || (!m->head.v.scale_f32 && (m->head.v.cols / 32) % 2))
+    throw Error(GEM_E_STATE, "vocab sharding needs a Q8_0/Q4_0 output matrix");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  const int per = (m->vocab + nranks - 1) / nranks;
+  m->shard_row0 = std::min(m->vocab, rank * per);
+  m->shard_rows = std::min(per, m->vocab - m->shard_row0);
+  if (m->shard_rows <= 0) throw Error(GEM_E_RANGE, "more ranks than vocabulary rows");
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclComm_t c = nullptr;
+  const ncclResult_t r = nccl().init_rank(&c, nranks, uid, rank);
+  if (r != ncclSuccess) throw Error(GEM_E_CUDA, std::string("ncclCommInitRank: ") + nccl().error_string(r));
+  m->comm = c;
+  m->shard_rank = rank, m->shard_n = nranks;
+  API_END
+}
+
 int gem_set_profiling(gem_model* m, int on) {
   API_BEGIN
   if (!m) throw Error(GEM_E_ARG, "null argument");
@@ -1135,6 +1237,7 @@ static void run_score(gem_model* m, size_t n, int head) {
     m->have_h = true;
     return;
   }
+  if (m->comm && head == 0) throw Error(GEM_E_STATE, "the vocab-sharded full head runs under the parallel schedule only");
   if (head == 1 && m->try_pipeline(m->toks, n, (uint32_t)off, m->lp, m->am)) {
     m->last_launches = 2;  // the pipelined kernel and the last hidden state's quantization
     m->have_h = true;

@@ -660,6 +660,62 @@ __global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* t
   }
 }
 
+// Vocab-sharded full head: this rank's rows [row0, row0 + V) of the output matrix give, per position,
+// the partial log-sum-exp state, the best logit with its token id and the target's logit (NaN when
+// the target is another rank's). out[t] = {m, s, best, best id bits, target logit}.
+__global__ void k_seq_logit_partials(const float* logits, int V, uint32_t row0, const uint32_t* targets, uint32_t vocab,
+                                     float* out, int* err) {
+  __shared__ float red_m[32], red_s[32], red_v[32];
+  __shared__ uint32_t red_t[32];
+  const int t = blockIdx.x;
+  const float* z = logits + (size_t)t * V;
+  Lse L{-INFINITY, 0.0f};
+  Best B{-INFINITY, 0xffffffffu};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = z[i];
+    L = lse_add(L, v);
+    B = best_merge(B, Best{v, row0 + (uint32_t)i});
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    L = lse_merge(L, Lse{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)});
+    B = best_merge(B, Best{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)});
+  }
+  if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i) {
+      L = lse_merge(L, Lse{red_m[i], red_s[i]});
+      B = best_merge(B, Best{red_v[i], red_t[i]});
+    }
+    uint32_t tg = targets[t];
+    if (tg >= vocab) {
+      atomicExch(err, ERR_RANGE);
+      tg = 0;
+    }
+    const float tl = tg >= row0 && tg < row0 + (uint32_t)V ? z[tg - row0] : __int_as_float(0x7fffffff);
+    float* o = out + (size_t)t * 5;
+    o[0] = L.m, o[1] = L.s, o[2] = B.v, o[3] = __uint_as_float(B.tok), o[4] = tl;
+  }
+}
+
+// Merges the ranks' partials (gathered [nranks][T][5]) into logprob and argmax (ties: lowest id).
+__global__ void k_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  Lse L{-INFINITY, 0.0f};
+  Best B{-INFINITY, 0xffffffffu};
+  float tl = __int_as_float(0x7fffffff);
+  for (int r = 0; r < nranks; ++r) {
+    const float* o = parts + ((size_t)r * T + t) * 5;
+    L = lse_merge(L, Lse{o[0], o[1]});
+    B = best_merge(B, Best{o[2], __float_as_uint(o[3])});
+    if (!isnan(o[4])) tl = o[4];
+  }
+  lp[t] = tl - (L.m + logf(L.s));
+  if (am) am[t] = B.tok;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Launchers
 // ------------------------------------------------------------------------------------------------
@@ -822,4 +878,14 @@ void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* 
   k_seq_logit_reduce<<<T, 1024, 0, st>>>(logits, V, targets, lp, am, err);
 }
 
+}  // namespace gem
+
+namespace gem {
+void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
+                               float* out, int* err, cudaStream_t st) {
+  k_seq_logit_partials<<<T, 1024, 0, st>>>(logits, V, row0, targets, vocab, out, err);
+}
+void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st) {
+  k_seq_logit_combine<<<(T + 127) / 128, 128, 0, st>>>(parts, nranks, T, lp, am);
+}
 }  // namespace gem

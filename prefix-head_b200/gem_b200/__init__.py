@@ -82,6 +82,8 @@ def lib():
     L.gem_score.argtypes = [vp, _u32p, C.c_size_t, C.c_int, _f32p, _u32p]
     L.gem_score_dev.argtypes = [vp, vp, C.c_size_t, C.c_int, vp, vp]
     L.gem_score_batch.argtypes = [vp, _u32p, C.c_size_t, C.c_size_t, C.c_int, _f32p, _u32p]
+    L.gem_nccl_unique_id.argtypes = [C.c_char_p]
+    L.gem_shard_init.argtypes = [vp, C.c_int, C.c_int, C.c_char_p]
     L.gem_score_batch_dev.argtypes = [vp, vp, C.c_size_t, C.c_size_t, C.c_int, vp, vp]
     L.gem_matvec_dev.argtypes = [vp, C.c_int, C.c_int, vp, vp]
     L.gem_head_full_dev.argtypes = [vp, vp, vp, C.c_int, vp, vp]
@@ -98,6 +100,16 @@ def _check(rc: int):
 
 def _p(a: np.ndarray, t):
     return a.ctypes.data_as(t)
+
+
+NCCL_UNIQUE_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL communicator id (one rank makes it; every rank passes it to Gemma.shard)."""
+    buf = C.create_string_buffer(NCCL_UNIQUE_ID_BYTES)
+    _check(lib().gem_nccl_unique_id(buf))
+    return buf.raw
 
 
 FULL, TWO_LEVEL = 0, 1
@@ -170,6 +182,13 @@ class Gemma:
         sc = (C.c_int * 2)()
         _check(lib().gem_get_schedule(self._h, head, C.byref(p), sc))
         return bool(p.value), sc[0], sc[1], lib().gem_last_error().decode()
+
+    def shard(self, nranks: int, rank: int, uid: bytes):
+        """Vocab-shard the full head: this rank scores output rows [rank*ceil(V/n), ...) and the ranks
+        merge their partial statistics over NCCL (the body stays replicated)."""
+        if len(uid) != NCCL_UNIQUE_ID_BYTES:
+            raise ValueError("uid must be the 128 bytes of nccl_unique_id()")
+        _check(lib().gem_shard_init(self._h, nranks, rank, uid))
 
     def test_withhold_stage(self, stage: int, wait_ms: int = 2000):
         """Failure-detection hook: layer stage `stage` withholds its output (-1 restores normal runs)."""
