@@ -153,6 +153,37 @@ int gem_score_batch(gem_model* m, const uint32_t* toks, size_t nseq, size_t len,
 int gem_score_batch_dev(gem_model* m, const uint32_t* toks_dev, size_t nseq, size_t len, int head,
                         float* logprob_dev, uint32_t* argmax_dev);
 
+/* Generation (lean.rs, main.rs:109-141; gem complete / gem gen), on the last forward's hidden state.
+ * gem_greedy: lean.rs Classes::next + next_token - the greedy token by screening the `top` most likely
+ * classes and the always-on rows (class-ordered row indices), highest raw logit wins; when the most
+ * likely class's probability is below min_confidence, the full head's argmax over the class-ordered
+ * rows instead (*fell_back = 1). gem_twolevel_sample: TwoLevel::sample - a class, then a member, drawn
+ * at `temperature` with the reference's xorshift64 generator (*rng_state is updated). */
+int gem_greedy(gem_model* m, int top, float min_confidence, const uint32_t* always, int n_always, uint32_t* token,
+               int* fell_back);
+int gem_twolevel_sample(gem_model* m, float temperature, uint64_t* rng_state, uint32_t* token);
+/* gem_greedy for `batch` hidden states on device buffers (always_dev, tok_dev, fallback_dev device). */
+int gem_greedy_dev(gem_model* m, const float* h_dev, int batch, int top, float min_confidence, const uint32_t* always_dev,
+                   int n_always, uint32_t* tok_dev, int* fallback_dev);
+/* The completion loop (lean.rs:113-200 without the tokenizer): BOS, the prompt (all positions at once
+ * under the parallel schedule), then up to max_new tokens, each chosen by `mode` from the hidden state
+ * and fed back; a token in `stops` ends the loop and is not emitted. Writes the tokens to out and
+ * their count to *n_out. */
+enum { GEM_GEN_GREEDY_FULL = 0, GEM_GEN_GREEDY_SCREEN = 1, GEM_GEN_SAMPLE = 2 };
+typedef struct gem_gen_opts {
+  int mode;
+  int top;               /* GREEDY_SCREEN: classes screened */
+  float min_confidence;  /* GREEDY_SCREEN: fall back to the full head below this class probability */
+  const uint32_t* always;
+  int n_always;
+  float temperature;     /* SAMPLE */
+  uint64_t seed;         /* SAMPLE: xorshift64 state */
+  const uint32_t* stops;
+  int n_stops;
+} gem_gen_opts;
+int gem_generate(gem_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new, const gem_gen_opts* opts,
+                 uint32_t* out, size_t* n_out);
+
 /* Vocab-sharded full head across GPUs (one process and model handle per GPU, the body replicated):
  * gem_shard_init splits the output matrix's rows into nranks contiguous ranges of ceil(vocab/nranks)
  * and joins an NCCL communicator (id: 128 bytes from gem_nccl_unique_id on one rank, passed to all).

@@ -1158,6 +1158,101 @@ int orc_twolevel(orc_model* om, const float* h, uint32_t target, float* lp, uint
   GUARD_END
 }
 
+// lean.rs:46-76 (Classes::next) and lean.rs:93-107 (next_token): the greedy token for hidden state h
+// by screening the `top` most likely classes and the always-on rows (indices into the class-ordered
+// rows of the permuted head), highest raw logit wins; when the most likely class's probability is
+// below min_confidence, the full head's argmax over the class-ordered rows instead (*fell_back = 1).
+int orc_greedy(orc_model* om, const float* h, int top, float min_confidence, const uint32_t* always, int n_always,
+               uint32_t* tok, int* fell_back) {
+  GUARD_BEGIN
+  if (!om->two) fail("two-level head not loaded");
+  TwoLevel& t = *om->two;
+  Pool& pool = *om->pool;
+  Isa isa = om->isa;
+  const size_t k = t.cl.size(), d = t.d, per = t.inner.size();
+  for (size_t c = 0; c < k; ++c) t.cl[c] = dotf(&t.a[c * d], h, d, isa) + t.b[c];
+  const float norm = lse(t.cl.data(), k);
+  t.act.quantize(h, d, isa);
+  std::vector<size_t> ranked(k);
+  for (size_t c = 0; c < k; ++c) ranked[c] = c;
+  std::stable_sort(ranked.begin(), ranked.end(), [&](size_t x, size_t y) { return t.cl[y] < t.cl[x]; });
+  if (fell_back) *fell_back = 0;
+  if (std::exp(t.cl[ranked[0]] - norm) < min_confidence) {
+    std::vector<float> z;  // the permuted head: class blocks in order
+    float best = -std::numeric_limits<float>::infinity();
+    size_t brow = 0, row = 0;
+    for (size_t c = 0; c < k; ++c) {
+      z.assign(t.blocks[c].rows, 0.0f);
+      matvec(pool, isa, t.blocks[c], t.act, z.data());
+      for (size_t j = 0; j < z.size(); ++j, ++row)
+        if (z[j] > best || row == 0) best = z[j], brow = row;
+    }
+    if (fell_back) *fell_back = 1;
+    *tok = t.members[brow / per][brow % per];
+    return 0;
+  }
+  float best = -std::numeric_limits<float>::infinity();
+  size_t brow = 0;
+  for (int i = 0; i < top && (size_t)i < k; ++i) {
+    const size_t c = ranked[(size_t)i];
+    std::vector<float> z(t.blocks[c].rows);
+    matvec(pool, isa, t.blocks[c], t.act, z.data());
+    const size_t j = argmax(z.data(), z.size());
+    if (z[j] > best) best = z[j], brow = c * per + j;
+  }
+  for (int i = 0; i < n_always; ++i) {
+    const size_t row = always[i], c = row / per;
+    if (c >= k || row % per >= t.blocks[c].rows) fail("always-on row out of range");
+    std::vector<float> z(t.blocks[c].rows);
+    matvec(pool, isa, t.blocks[c], t.act, z.data());
+    if (z[row % per] > best) best = z[row % per], brow = row;
+  }
+  *tok = t.members[brow / per][brow % per];
+  return 0;
+  GUARD_END
+}
+
+// main.rs:123-141: uniform (xorshift64, 24 bits) and draw (softmax at temperature, sequential scan).
+static float uniform01(uint64_t* rng) {
+  uint64_t x = *rng;
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  *rng = x;
+  return (float)(x >> 40) / (float)(1ull << 24);
+}
+static size_t draw(const float* l, size_t n, float temp, uint64_t* rng) {
+  float mx = -std::numeric_limits<float>::infinity();
+  for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, l[i]);
+  std::vector<float> w(n);
+  float sum = 0.0f;
+  for (size_t i = 0; i < n; ++i) w[i] = std::exp((l[i] - mx) / temp);
+  for (size_t i = 0; i < n; ++i) sum += w[i];
+  float r = uniform01(rng) * sum;
+  for (size_t i = 0; i < n; ++i) {
+    r -= w[i];
+    if (r <= 0.0f) return i;
+  }
+  return n - 1;
+}
+
+// TwoLevel::sample (main.rs:109-116): a class drawn from the class logits, then a member of it.
+int orc_twolevel_sample(orc_model* om, const float* h, float temp, uint64_t* rng, uint32_t* tok) {
+  GUARD_BEGIN
+  if (!om->two) fail("two-level head not loaded");
+  TwoLevel& t = *om->two;
+  Pool& pool = *om->pool;
+  const size_t k = t.cl.size(), d = t.d;
+  for (size_t c = 0; c < k; ++c) t.cl[c] = dotf(&t.a[c * d], h, d, om->isa) + t.b[c];
+  const size_t c = draw(t.cl.data(), k, temp, rng);
+  t.act.quantize(h, d, om->isa);
+  const size_t n = t.blocks[c].rows;
+  matvec(pool, om->isa, t.blocks[c], t.act, t.inner.data());
+  *tok = t.members[c][draw(t.inner.data(), n, temp, rng)];
+  return 0;
+  GUARD_END
+}
+
 int orc_score(orc_model* om, const uint32_t* toks, size_t n, int head, float* lp, uint32_t* am, double* body_s, double* head_s) {
   GUARD_BEGIN
   Gemma& m = om->m;

@@ -50,6 +50,14 @@ int orc_twolevel_load(orc_model* m, const char* prefix);
  * top class, returned as a token id. cl_out (k floats) / inner_out (per floats) are nullable. */
 int orc_twolevel(orc_model* m, const float* h, uint32_t target, float* logprob, uint32_t* argmax,
                  float* cl_out, float* inner_t_out);
+/* lean.rs:46-107 (Classes::next + next_token): greedy token by screening the `top` most likely classes
+ * and the always-on rows (class-ordered row indices); below min_confidence, the full head's argmax
+ * over the class-ordered rows (*fell_back = 1). */
+int orc_greedy(orc_model* m, const float* h, int top, float min_confidence, const uint32_t* always, int n_always,
+               uint32_t* tok, int* fell_back);
+/* TwoLevel::sample (main.rs:109-141): class, then member, drawn at temperature temp with the
+ * reference's xorshift64 generator (state updated in place). */
+int orc_twolevel_sample(orc_model* m, const float* h, float temp, uint64_t* rng, uint32_t* tok);
 /* gem bench's inner loop (main.rs:270-289): optional BOS forward, then for i < n: forward(toks[i],
  * i + off), head logprob of toks[i + 1]. head: 0 full, 1 two-level. body_s / head_s accumulate
  * wall time like tb / th. lp / am have n entries each (am nullable). */

@@ -46,6 +46,8 @@ def lib():
         L.orc_full.argtypes = [C.c_void_p, _f32p, C.c_uint32, _f32p, _u32p, _f32p]
         L.orc_twolevel_load.argtypes = [C.c_void_p, C.c_char_p]
         L.orc_twolevel.argtypes = [C.c_void_p, _f32p, C.c_uint32, _f32p, _u32p, _f32p, _f32p]
+        L.orc_greedy.argtypes = [C.c_void_p, _f32p, C.c_int, C.c_float, _u32p, C.c_int, _u32p, C.POINTER(C.c_int)]
+        L.orc_twolevel_sample.argtypes = [C.c_void_p, _f32p, C.c_float, C.POINTER(C.c_uint64), _u32p]
         L.orc_score.argtypes = [C.c_void_p, _u32p, C.c_size_t, C.c_int, _f32p, _u32p,
                                 C.POINTER(C.c_double), C.POINTER(C.c_double)]
         L.orc_mat_from_gguf.restype = C.c_void_p
@@ -132,6 +134,21 @@ class Model:
 
     def load_twolevel(self, prefix):
         _check(lib().orc_twolevel_load(self.h, str(prefix).encode()))
+
+    def greedy(self, h: np.ndarray, top: int = 1, min_confidence: float = 0.0, always=()):
+        """lean.rs Classes::next + next_token -> (token, fell_back)."""
+        h = np.ascontiguousarray(h, np.float32)
+        al = np.ascontiguousarray(np.asarray(always, np.uint32))
+        tok, fb = C.c_uint32(), C.c_int()
+        _check(lib().orc_greedy(self.h, _p(h, _f32p), top, min_confidence, _p(al, _u32p), len(al), C.byref(tok), C.byref(fb)))
+        return tok.value, bool(fb.value)
+
+    def sample(self, h: np.ndarray, temp: float, rng: int):
+        """TwoLevel::sample -> (token, new rng state)."""
+        h = np.ascontiguousarray(h, np.float32)
+        st, tok = C.c_uint64(rng), C.c_uint32()
+        _check(lib().orc_twolevel_sample(self.h, _p(h, _f32p), temp, C.byref(st), C.byref(tok)))
+        return tok.value, st.value
 
     def twolevel(self, h: np.ndarray, target: int):
         h = np.ascontiguousarray(h, np.float32)

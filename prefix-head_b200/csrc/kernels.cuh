@@ -145,6 +145,18 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
 void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
                                float* out, int* err, cudaStream_t st);
 void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st);
+// Generation-side heads (decode.cu).
+void launch_greedy_rank(const float* cl, int k, int top, float min_conf, int batch, uint32_t* sel, int* fallback,
+                        cudaStream_t st);
+void launch_greedy_rowlist(const uint32_t* sel, int top, int per, uint32_t total_rows, const uint32_t* always, int n_always,
+                           int batch, uint32_t* rows, cudaStream_t st);
+void launch_rows_exact(const MatView& w, const int8_t* aq, const float* as, const float* h, const uint32_t* rows, int nrows,
+                       int batch, float* out, cudaStream_t st);
+void launch_greedy_pick(const float* z, const uint32_t* rows, int top, int per, int n_always, const int* fallback,
+                        const uint32_t* fb_row, const uint32_t* order, int batch, uint32_t* tok, cudaStream_t st);
+void launch_sample_class(const float* cl, int k, float temp, unsigned long long* rng, uint32_t* cls, cudaStream_t st);
+void launch_sample_member(const float* inner, int per, uint32_t total_rows, const uint32_t* cls, float temp,
+                          unsigned long long* rng, const uint32_t* order, uint32_t* tok, cudaStream_t st);
 void launch_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin, uint32_t* tgt,
                               cudaStream_t st);
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st);

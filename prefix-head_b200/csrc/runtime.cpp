@@ -191,6 +191,15 @@ struct gem_model {
       }
   }
   bool have_h = false;
+  // generation-side heads (decode.cu): per-call scratch, grown on demand
+  struct GenScratch {
+    int8_t* q = nullptr;
+    float *s = nullptr, *cl = nullptr, *z = nullptr, *logits = nullptr, *lp = nullptr;
+    uint32_t *sel = nullptr, *rows = nullptr, *always = nullptr, *fb_row = nullptr, *tok = nullptr, *zeros = nullptr;
+    int* fallback = nullptr;
+    unsigned long long* rng = nullptr;
+    size_t batch = 0, nrows = 0, nalways = 0, nlogits = 0;
+  } gs;
   // host-buffer batched scoring: device copies of the ids and outputs
   uint32_t *btoks = nullptr, *bam = nullptr;
   float* blp = nullptr;
@@ -537,6 +546,7 @@ struct gem_model {
         }
         launch_seq_norm(s_x, s_dn, layers[nl - 1].post_ffw, out_norm, eps, d, T, s_haq, s_has, s_h, st);
         par_mark(PAR_NORM);
+        if (which < 0) continue;  // prefill only: no head
         nk += 4 + seq_head(which, s_tgt, T, s_lp, s_am);
         par_mark(PAR_HEAD);
         // rows [seq][Lc] of the chunk into [seq][len] of the caller's outputs
@@ -562,6 +572,87 @@ struct gem_model {
     for (float* c : {kc, vc})
       ck(cudaMemcpy2DAsync(c + (size_t)s * nl * le, le * 4, c, le * 4, rw * 4, nl, cudaMemcpyDeviceToDevice, st),
          "bos kv");
+  }
+
+  // lean.rs:46-107 for `batch` hidden states h_dev (device): greedy tokens by screening the `top` most
+  // likely classes and n_always always-on rows (class-ordered row indices, device); with
+  // min_conf > 0, items whose most likely class is below it take the full head's argmax over the
+  // class-ordered rows. Asynchronous on the model's stream.
+  void greedy(const float* h_dev, int batch, int top, float min_conf, const uint32_t* always_dev, int n_always,
+              uint32_t* tok_dev, int* fallback_dev) {
+    const int nrows = top * per + n_always;
+    if ((size_t)batch > gs.batch) {
+      gs.q = alloc<int8_t>((size_t)batch * d);
+      gs.s = alloc<float>((size_t)batch * d / 32);
+      gs.cl = alloc<float>((size_t)batch * k);
+      gs.fallback = alloc<int>(batch);
+      gs.fb_row = alloc<uint32_t>(batch);
+      gs.tok = alloc<uint32_t>(batch);
+      gs.lp = alloc<float>(batch);
+      gs.zeros = alloc<uint32_t>(batch);
+      ck(cudaMemsetAsync(gs.zeros, 0, (size_t)batch * 4, st), "memset");
+      gs.batch = batch;
+      gs.nrows = 0;
+    }
+    if ((size_t)batch * nrows > gs.nrows) {
+      gs.sel = alloc<uint32_t>((size_t)batch * std::max(top, 1));
+      gs.rows = alloc<uint32_t>((size_t)batch * nrows);
+      gs.z = alloc<float>((size_t)batch * nrows);
+      gs.nrows = (size_t)batch * nrows;
+    }
+    launch_quantize(h_dev, batch * d, gs.q, gs.s, st);
+    launch_seq_class_logits(A, b, k, h_dev, d, batch, gs.cl, st);
+    launch_greedy_rank(gs.cl, k, top, min_conf, batch, gs.sel, gs.fallback, st);
+    launch_greedy_rowlist(gs.sel, top, per, (uint32_t)blocks.v.rows, always_dev, n_always, batch, gs.rows, st);
+    launch_rows_exact(blocks.v, gs.q, gs.s, h_dev, gs.rows, nrows, batch, gs.z, st);
+    const bool fb = min_conf > 0.0f;
+    if (fb) {  // lean.rs:93-107: the full head over the class-ordered rows, argmax = first maximum
+      if ((size_t)batch * vocab > gs.nlogits) {
+        gs.logits = alloc<float>((size_t)batch * vocab);
+        gs.nlogits = (size_t)batch * vocab;
+      }
+      if (!seq_gemm_supported(blocks.v)) throw Error(GEM_E_STATE, "the fallback needs a Q8_0/Q4_0 output matrix");
+      launch_seq_gemm(blocks.v, gs.q, gs.s, batch, gs.logits, vocab, sms, st);
+      launch_seq_logit_reduce(gs.logits, vocab, batch, gs.zeros, gs.lp, gs.fb_row, err, st);
+    }
+    launch_greedy_pick(gs.z, gs.rows, top, per, n_always, gs.fallback, fb ? gs.fb_row : nullptr, order, batch, tok_dev, st);
+    if (fallback_dev) ck(cudaMemcpyAsync(fallback_dev, gs.fallback, (size_t)batch * 4, cudaMemcpyDeviceToDevice, st), "fb");
+  }
+
+  // TwoLevel::sample (main.rs:109-141) on the last forward's hidden state (h, haq, has).
+  uint32_t sample(float temp, uint64_t* rng_host) {
+    if (gs.batch < 1) greedy_scratch_min();
+    if (!gs.rng) gs.rng = alloc<unsigned long long>(1);
+    if (gs.nrows < (size_t)per) {
+      gs.sel = alloc<uint32_t>(1);
+      gs.rows = alloc<uint32_t>(per);
+      gs.z = alloc<float>(per);
+      gs.nrows = per;
+    }
+    ck(cudaMemcpyAsync(gs.rng, rng_host, 8, cudaMemcpyHostToDevice, st), "rng");
+    launch_seq_class_logits(A, b, k, h, d, 1, gs.cl, st);
+    launch_sample_class(gs.cl, k, temp, gs.rng, gs.sel, st);
+    launch_greedy_rowlist(gs.sel, 1, per, (uint32_t)blocks.v.rows, nullptr, 0, 1, gs.rows, st);
+    launch_rows_exact(blocks.v, haq, has, h, gs.rows, per, 1, gs.z, st);
+    launch_sample_member(gs.z, per, (uint32_t)blocks.v.rows, gs.sel, temp, gs.rng, order, gs.tok, st);
+    uint32_t t = 0;
+    ck(cudaMemcpyAsync(&t, gs.tok, 4, cudaMemcpyDeviceToHost, st), "tok");
+    ck(cudaMemcpyAsync(rng_host, gs.rng, 8, cudaMemcpyDeviceToHost, st), "rng");
+    sync();
+    return t;
+  }
+  void greedy_scratch_min() {
+    gs.q = alloc<int8_t>(d);
+    gs.s = alloc<float>(d / 32);
+    gs.cl = alloc<float>(k);
+    gs.fallback = alloc<int>(1);
+    gs.fb_row = alloc<uint32_t>(1);
+    gs.tok = alloc<uint32_t>(1);
+    gs.lp = alloc<float>(1);
+    gs.zeros = alloc<uint32_t>(1);
+    ck(cudaMemsetAsync(gs.zeros, 0, 4, st), "memset");
+    gs.batch = 1;
+    gs.nrows = 0;
   }
 
   // Can the two-level scoring loop run as one layer-pipelined kernel on this model and GPU?
@@ -1359,6 +1450,127 @@ int gem_score_batch_dev(gem_model* m, const uint32_t* toks_dev, size_t nseq, siz
   if (nseq == 0 || len == 0) return GEM_OK;
   ck(cudaSetDevice(m->device), "cudaSetDevice");
   run_score_batch(m, toks_dev, nseq, len, head, logprob_dev, argmax_dev);
+  API_END
+}
+
+int gem_greedy_dev(gem_model* m, const float* h_dev, int batch, int top, float min_confidence, const uint32_t* always_dev,
+                   int n_always, uint32_t* tok_dev, int* fallback_dev) {
+  API_BEGIN
+  if (!m || !h_dev || !tok_dev || batch <= 0) throw Error(GEM_E_ARG, "bad argument");
+  if (!m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  if (top < 1 || top > m->k) throw Error(GEM_E_RANGE, "top must be in 1..classes");
+  if (n_always < 0 || (n_always > 0 && !always_dev)) throw Error(GEM_E_ARG, "always-on rows");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->greedy(h_dev, batch, top, min_confidence, always_dev, n_always, tok_dev, fallback_dev);
+  m->check_launch();
+  API_END
+}
+
+int gem_greedy(gem_model* m, int top, float min_confidence, const uint32_t* always, int n_always, uint32_t* token,
+               int* fell_back) {
+  API_BEGIN
+  if (!m || !token) throw Error(GEM_E_ARG, "null argument");
+  if (!m->have_h) throw Error(GEM_E_STATE, "no hidden state: call gem_forward or gem_score first");
+  if (!m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  if (top < 1 || top > m->k) throw Error(GEM_E_RANGE, "top must be in 1..classes");
+  if (n_always < 0 || (n_always > 0 && !always)) throw Error(GEM_E_ARG, "always-on rows");
+  for (int i = 0; i < n_always; ++i)
+    if (always[i] >= (uint32_t)m->blocks.v.rows) throw Error(GEM_E_RANGE, "always-on row out of range");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  if ((size_t)n_always > m->gs.nalways) {
+    m->gs.always = m->alloc<uint32_t>(n_always);
+    m->gs.nalways = n_always;
+  }
+  if (n_always) ck(cudaMemcpyAsync(m->gs.always, always, (size_t)n_always * 4, cudaMemcpyHostToDevice, m->st), "always");
+  if (m->gs.batch < 1) m->greedy_scratch_min();
+  m->greedy(m->h, 1, top, min_confidence, m->gs.always, n_always, m->gs.tok, m->gs.fallback);
+  int fb = 0;
+  ck(cudaMemcpyAsync(token, m->gs.tok, 4, cudaMemcpyDeviceToHost, m->st), "tok");
+  ck(cudaMemcpyAsync(&fb, m->gs.fallback, 4, cudaMemcpyDeviceToHost, m->st), "fb");
+  m->sync();
+  if (fell_back) *fell_back = min_confidence > 0.0f ? fb : 0;
+  API_END
+}
+
+int gem_twolevel_sample(gem_model* m, float temperature, uint64_t* rng_state, uint32_t* token) {
+  API_BEGIN
+  if (!m || !rng_state || !token) throw Error(GEM_E_ARG, "null argument");
+  if (!m->have_h) throw Error(GEM_E_STATE, "no hidden state: call gem_forward or gem_score first");
+  if (!m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  if (!(temperature > 0.0f)) throw Error(GEM_E_ARG, "temperature must be > 0");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  *token = m->sample(temperature, rng_state);
+  API_END
+}
+
+int gem_generate(gem_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new, const gem_gen_opts* o, uint32_t* out,
+                 size_t* n_out) {
+  API_BEGIN
+  if (!m || !prompt || !o || !out || !n_out || n_prompt == 0) throw Error(GEM_E_ARG, "bad argument");
+  if (o->mode < GEM_GEN_GREEDY_FULL || o->mode > GEM_GEN_SAMPLE) throw Error(GEM_E_ARG, "unknown mode");
+  if (o->mode != GEM_GEN_GREEDY_FULL && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
+  for (size_t i = 0; i < n_prompt; ++i)
+    if (prompt[i] >= (uint32_t)m->vocab) throw Error(GEM_E_RANGE, "token id >= vocab");
+  const size_t off = m->bos >= 0 ? 1 : 0;
+  if (off + n_prompt + max_new > (size_t)m->ctx) throw Error(GEM_E_RANGE, "prompt + max_new longer than ctx");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  *n_out = 0;
+  if (m->bos >= 0) {  // main.rs:270-272
+    *m->cur_host = StepCur{(uint32_t)m->bos, 0, 0, 0};
+    ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+    m->enqueue_body(0);
+  }
+  // the prompt: every position at once when the parallel schedule applies, else one forward per token
+  if (m->use_parallel()) {
+    std::vector<uint32_t> ids(prompt, prompt + n_prompt);
+    ids.push_back(0);  // an unused target for the last position
+    m->ensure_batch_io(ids.size(), 0);
+    ck(cudaMemcpyAsync(m->btoks, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, m->st), "prompt");
+    m->score_parallel(m->btoks, ids.size(), 1, n_prompt, -1, (uint32_t)off, nullptr, nullptr);
+  } else {
+    for (size_t i = 0; i < n_prompt; ++i) {
+      m->sync();
+      *m->cur_host = StepCur{prompt[i], (uint32_t)(off + i), 0, 0};
+      ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+      m->enqueue_body(0);
+    }
+  }
+  m->check_launch();
+  m->sync();
+  m->have_h = true;
+  uint64_t rng = o->seed;
+  std::vector<uint32_t> always(o->always, o->always + (o->always ? o->n_always : 0));
+  size_t pos = off + n_prompt;
+  for (size_t i = 0; i < max_new; ++i) {
+    uint32_t t = 0;
+    if (o->mode == GEM_GEN_GREEDY_FULL) {  // next_token without classes: argmax of the full head
+      *m->cur_host = StepCur{0, (uint32_t)pos, 0, 0};
+      ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+      m->enqueue_head(0, m->lp, m->am);
+      ck(cudaMemcpyAsync(&t, m->am, 4, cudaMemcpyDeviceToHost, m->st), "am");
+      m->sync();
+    } else if (o->mode == GEM_GEN_GREEDY_SCREEN) {
+      int fb = 0;
+      const int rc = gem_greedy(m, o->top, o->min_confidence, always.data(), (int)always.size(), &t, &fb);
+      if (rc != GEM_OK) return rc;
+    } else {
+      t = m->sample(o->temperature, &rng);
+    }
+    bool stop = false;
+    for (int j = 0; j < o->n_stops; ++j) stop |= o->stops[j] == t;
+    if (stop) break;  // lean.rs: a stop token ends the completion and is not emitted
+    out[(*n_out)++] = t;
+    if (i + 1 == max_new) break;
+    *m->cur_host = StepCur{t, (uint32_t)pos, 0, 0};
+    ck(cudaMemcpyAsync(m->cur, m->cur_host, sizeof(StepCur), cudaMemcpyHostToDevice, m->st), "cur");
+    m->enqueue_body(0);
+    m->check_launch();
+    ++pos;
+  }
+  m->sync();
   API_END
 }
 

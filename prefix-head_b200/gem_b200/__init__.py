@@ -83,6 +83,10 @@ def lib():
     L.gem_score_dev.argtypes = [vp, vp, C.c_size_t, C.c_int, vp, vp]
     L.gem_score_batch.argtypes = [vp, _u32p, C.c_size_t, C.c_size_t, C.c_int, _f32p, _u32p]
     L.gem_nccl_unique_id.argtypes = [C.c_char_p]
+    L.gem_greedy.argtypes = [vp, C.c_int, C.c_float, _u32p, C.c_int, _u32p, C.POINTER(C.c_int)]
+    L.gem_twolevel_sample.argtypes = [vp, C.c_float, C.POINTER(C.c_uint64), _u32p]
+    L.gem_greedy_dev.argtypes = [vp, vp, C.c_int, C.c_int, C.c_float, vp, C.c_int, vp, vp]
+    L.gem_generate.argtypes = [vp, _u32p, C.c_size_t, C.c_size_t, C.POINTER(GenOpts), _u32p, C.POINTER(C.c_size_t)]
     L.gem_shard_init.argtypes = [vp, C.c_int, C.c_int, C.c_char_p]
     L.gem_score_batch_dev.argtypes = [vp, vp, C.c_size_t, C.c_size_t, C.c_int, vp, vp]
     L.gem_matvec_dev.argtypes = [vp, C.c_int, C.c_int, vp, vp]
@@ -102,6 +106,13 @@ def _p(a: np.ndarray, t):
     return a.ctypes.data_as(t)
 
 
+class GenOpts(C.Structure):
+    _fields_ = [("mode", C.c_int), ("top", C.c_int), ("min_confidence", C.c_float), ("always", C.POINTER(C.c_uint32)),
+                ("n_always", C.c_int), ("temperature", C.c_float), ("seed", C.c_uint64), ("stops", C.POINTER(C.c_uint32)),
+                ("n_stops", C.c_int)]
+
+
+GREEDY_FULL, GREEDY_SCREEN, SAMPLE = 0, 1, 2
 NCCL_UNIQUE_ID_BYTES = 128
 
 
@@ -182,6 +193,35 @@ class Gemma:
         sc = (C.c_int * 2)()
         _check(lib().gem_get_schedule(self._h, head, C.byref(p), sc))
         return bool(p.value), sc[0], sc[1], lib().gem_last_error().decode()
+
+    def greedy(self, top: int = 1, min_confidence: float = 0.0, always=()):
+        """lean.rs Classes::next + next_token on the last hidden state -> (token, fell_back)."""
+        al = np.ascontiguousarray(np.asarray(always, np.uint32))
+        tok, fb = C.c_uint32(), C.c_int()
+        _check(lib().gem_greedy(self._h, top, min_confidence, _p(al, _u32p), len(al), C.byref(tok), C.byref(fb)))
+        return tok.value, bool(fb.value)
+
+    def sample(self, temperature: float, rng: int):
+        """TwoLevel::sample on the last hidden state -> (token, new rng state)."""
+        st, tok = C.c_uint64(rng), C.c_uint32()
+        _check(lib().gem_twolevel_sample(self._h, temperature, C.byref(st), C.byref(tok)))
+        return tok.value, st.value
+
+    def greedy_dev(self, h_ptr: int, batch: int, top: int, min_confidence: float, always_ptr: int, n_always: int,
+                   tok_ptr: int, fb_ptr: int | None):
+        _check(lib().gem_greedy_dev(self._h, h_ptr, batch, top, min_confidence, always_ptr, n_always, tok_ptr, fb_ptr))
+
+    def generate(self, prompt, max_new: int, mode: int = GREEDY_FULL, top: int = 1, min_confidence: float = 0.0,
+                 always=(), temperature: float = 1.0, seed: int = 1, stops=()):
+        """The completion loop: prompt, then up to max_new tokens (a stop token ends it, not emitted)."""
+        prompt = np.ascontiguousarray(prompt, np.uint32)
+        al = np.ascontiguousarray(np.asarray(always, np.uint32))
+        sp = np.ascontiguousarray(np.asarray(stops, np.uint32))
+        o = GenOpts(mode, top, min_confidence, _p(al, _u32p), len(al), temperature, seed, _p(sp, _u32p), len(sp))
+        out = np.zeros(max(1, max_new), np.uint32)
+        n = C.c_size_t()
+        _check(lib().gem_generate(self._h, _p(prompt, _u32p), len(prompt), max_new, C.byref(o), _p(out, _u32p), C.byref(n)))
+        return out[:n.value]
 
     def shard(self, nranks: int, rank: int, uid: bytes):
         """Vocab-shard the full head: this rank scores output rows [rank*ceil(V/n), ...) and the ranks

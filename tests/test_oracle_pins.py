@@ -120,3 +120,34 @@ def test_matvec_isa_paths_agree(kind, qtype):
         ref = W @ (q.astype(np.float64) * np.repeat(s, 32))
     for isa, y in ys.items():
         np.testing.assert_allclose(y, ref, rtol=2e-5, atol=2e-6, err_msg=isa)
+
+
+def test_sampling_generator_is_the_references_xorshift(small):
+    """main.rs:123-128: x ^= x << 13; x ^= x >> 7; x ^= x << 17; uniform = (x >> 40) / 2^24. One
+    two-level sample draws twice (class, member), so the state advances by two steps."""
+    from oracle import oracle as orc
+    o = orc.Model(small.gguf, ctx=16, threads=1)
+    o.load_twolevel(small.twolevel)
+    h = np.random.default_rng(3).standard_normal(o.d).astype(np.float32)
+    m = (1 << 64) - 1
+
+    def step(x):
+        x ^= (x << 13) & m
+        x ^= x >> 7
+        x ^= (x << 17) & m
+        return x
+    seed = 0x0123456789ABCDEF
+    _, st = o.sample(h, 1.0, seed)
+    assert st == step(step(seed))
+
+
+def test_greedy_top1_equals_two_level_argmax(small):
+    """lean.rs:46-76 with top = 1 and no always-on rows is TwoLevel's argmax (main.rs:101-107 plus the
+    screening rule): the same token from both oracle entry points."""
+    from oracle import oracle as orc
+    o = orc.Model(small.gguf, ctx=16, threads=2)
+    o.load_twolevel(small.twolevel)
+    rng = np.random.default_rng(4)
+    for _ in range(8):
+        h = rng.standard_normal(o.d).astype(np.float32)
+        assert o.greedy(h, 1)[0] == o.twolevel(h, 0)[1]
