@@ -358,7 +358,7 @@ struct gem_model {
   bool seq_supported() {
     seq_why.clear();
     const int G = nkv > 0 ? nh / nkv : 0;
-    if (G != 1 && G != 2 && G != 4 && G != 8) seq_why = "query heads per kv head not 1, 2, 4 or 8";
+    if (G < 1 || G > 8) seq_why = "more than 8 query heads per kv head";
     else if (hd % 32 || hd > 256 || d % 32 || d > 1152 || ff % 32)
       seq_why = "head_dim above 256, hidden size above 1152 or dimensions not in 32-blocks";
     for (const Layer& L : layers)
@@ -483,7 +483,7 @@ struct gem_model {
       launches += 2;
     }
     const ncclResult_t r = nccl().all_gather(s_spart, s_sgath, (size_t)T * 5, ncclFloat32, comm, st);
-    if (r != ncclSuccess) throw Error(GEM_E_CUDA, std::string("ncclAllGather: ") + nccl().error_string(r));
+    if (r != ncclSuccess) throw Error(GEM_E_NCCL, std::string("ncclAllGather: ") + nccl().error_string(r));
     launch_seq_logit_combine(s_sgath, shard_n, T, lpo, amo, st);
     return launches + 1;
   }
@@ -893,6 +893,14 @@ void load_model(gem_model* m, const Gguf& g, int body_bits, int head_bits) {
         (int)mo.rows != m->d || (int)mo.cols != m->nh * m->hd || (int)mg.rows != m->ff || (int)md.cols != m->ff)
       throw Error(GEM_E_FORMAT, "layer " + std::to_string(l) + ": projection shapes do not match the metadata");
     for (HostMat* x : {&mq, &mk, &mv, &mo, &mg, &mu, &md}) m->body_bytes += canonical_bytes(*x);
+    // an odd number of f16 scales per row cannot be staged in 4-byte pieces: such planes are widened
+    // to f32 (exact), which every kernel reads the same way
+    for (HostMat* x : {&mq, &mk, &mv, &mo, &mg, &mu, &md})
+      if (x->bits != 16 && !x->scale_f32() && (x->cols / 32) % 2) {
+        x->s32.resize(x->s16.size());
+        for (size_t i = 0; i < x->s16.size(); ++i) x->s32[i] = f16_value(x->s16[i]);
+        x->s16.clear();
+      }
     Layer& L = m->layers[l];
     L.qkv = upload_mat(concat_rows({&mq, &mk, &mv}), m->owned);
     L.o = upload_mat(mo, m->owned);
@@ -1164,7 +1172,7 @@ int gem_nccl_unique_id(void* id_out) {
   if (!nccl().load()) throw Error(GEM_E_STATE, std::string("libnccl.so.2 not loadable: ") + dlerror());
   ncclUniqueId id;
   const ncclResult_t r = nccl().get_id(&id);
-  if (r != ncclSuccess) throw Error(GEM_E_CUDA, std::string("ncclGetUniqueId: ") + nccl().error_string(r));
+  if (r != ncclSuccess) throw Error(GEM_E_NCCL, std::string("ncclGetUniqueId: ") + nccl().error_string(r));
   std::memcpy(id_out, &id, sizeof(id));
   API_END
 }
@@ -1187,7 +1195,7 @@ int gem_shard_init(gem_model* m, int nranks, int rank, const void* id) {
   std::memcpy(&uid, id, sizeof(uid));
   ncclComm_t c = nullptr;
   const ncclResult_t r = nccl().init_rank(&c, nranks, uid, rank);
-  if (r != ncclSuccess) throw Error(GEM_E_CUDA, std::string("ncclCommInitRank: ") + nccl().error_string(r));
+  if (r != ncclSuccess) throw Error(GEM_E_NCCL, std::string("ncclCommInitRank: ") + nccl().error_string(r));
   m->comm = c;
   m->shard_rank = rank, m->shard_n = nranks;
   API_END

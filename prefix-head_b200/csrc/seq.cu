@@ -798,7 +798,7 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
                      float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
                      cudaStream_t st) {
   const int G = A.nh / A.nkv, T = L * nseq;
-  if (G != 1 && G != 2 && G != 4 && G != 8) return;  // rejected by the caller before any launch
+  if (G < 1 || G > 8) return;  // rejected by the caller before any launch
   k_seq_attn_prep<<<dim3(T, A.nkv), 256, (size_t)(G + 2) * A.hd * 4, st>>>(A, qkv, qkv_ld, L, pos0, kv_stride, qn);
   const uint32_t pbase = window_lo(pos0, A.window);
   const int nchunk = (int)((pos0 + L - pbase + kAttnPC - 1) / kAttnPC);
@@ -817,10 +817,16 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
     }                                                                                                                \
     k_seq_scores_tile<GG><<<sgrid, 256, ssm, st>>>(A, qn, L, pos0, kv_stride, pbase, scores, sstride);               \
   } while (0)
-  if (G == 1) F(1);
-  else if (G == 2) F(2);
-  else if (G == 4) F(4);
-  else F(8);
+  switch (G) {
+    case 1: F(1); break;
+    case 2: F(2); break;
+    case 3: F(3); break;
+    case 4: F(4); break;
+    case 5: F(5); break;
+    case 6: F(6); break;
+    case 7: F(7); break;
+    default: F(8); break;
+  }
 #undef F
   {
     static bool init = false;
@@ -833,10 +839,16 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
     k_seq_softmax<<<(T * A.nh + nw - 1) / nw, nw * 32, (size_t)nw * es * 4, st>>>(A, T, L, pos0, scores, sstride);
   }
 #define P(GG) k_seq_pv_tile<GG><<<pgrid, pth, psm, st>>>(A, L, pos0, kv_stride, scores, sstride, threads, part)
-  if (G == 1) P(1);
-  else if (G == 2) P(2);
-  else if (G == 4) P(4);
-  else P(8);
+  switch (G) {
+    case 1: P(1); break;
+    case 2: P(2); break;
+    case 3: P(3); break;
+    case 4: P(4); break;
+    case 5: P(5); break;
+    case 6: P(6); break;
+    case 7: P(7); break;
+    default: P(8); break;
+  }
 #undef P
   k_seq_pv_combine<<<dim3(T, A.nh), A.hd, 0, st>>>(A, part, threads, aq, as);
 }

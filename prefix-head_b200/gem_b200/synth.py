@@ -29,7 +29,12 @@ SMALL = dict(arch="gemma3", d=256, layers=6, nh=4, nkv=1, hd=256, ff=512, vocab=
              window=16, rope_base=1e6, eps=1e-6)
 SMALL_GQA2 = dict(arch="gemma3", d=512, layers=6, nh=4, nkv=2, hd=128, ff=1024, vocab=4096,
                   window=12, rope_base=1e6, eps=1e-6)
-CONFIGS = {"gemma3-270m": GEMMA3_270M, "gemma3-1b": GEMMA3_1B, "small": SMALL, "small-gqa2": SMALL_GQA2}
+# qwen2 branch (model.rs:160-161, 188-190, 311-315, 400-407): biases on q/k/v, SiLU gate, no norm
+# folding or post-norms, untied output matrix; 7 query heads per kv head as Qwen2.5-0.5B (14 / 2).
+SMALL_QWEN2 = dict(arch="qwen2", d=256, layers=4, nh=7, nkv=1, hd=32, ff=512, vocab=4096,
+                   rope_base=1e6, eps=1e-6, untied=True)
+CONFIGS = {"gemma3-270m": GEMMA3_270M, "gemma3-1b": GEMMA3_1B, "small": SMALL, "small-gqa2": SMALL_GQA2,
+           "small-qwen2": SMALL_QWEN2}
 
 
 @dataclasses.dataclass
@@ -60,14 +65,20 @@ def _quant(w: np.ndarray, kind: str):
 
 
 def write_model(path: str | os.PathLike, cfg: dict, seed: int = 1, body: str = "q8_0",
-                head: str = "q8_0", bos: bool = False) -> Path:
-    """Writes a random-init decoder as GGUF. `head` is the (tied) token_embd.weight type."""
+                head: str = "q8_0", bos: bool = False, alignment: int | None = None, vocab_strings: bool = False) -> Path:
+    """Writes a random-init decoder as GGUF. `head` is the (tied) token_embd.weight type. `alignment`
+    sets general.alignment (tensor data offsets padded to it); `vocab_strings` adds a
+    tokenizer.ggml.tokens array of `vocab` strings (a header of several MiB for large vocabularies)."""
     import gguf
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
     a = cfg["arch"]
     d, nl, nh, nkv, hd, ff, V = (cfg[k] for k in ("d", "layers", "nh", "nkv", "hd", "ff", "vocab"))
     w = gguf.GGUFWriter(str(path), arch=a)
+    if alignment:
+        w.add_custom_alignment(alignment)
+    if vocab_strings:
+        w.add_token_list([f"<tok-{i:06d}-{'x' * 24}>" for i in range(V)])
     w.add_uint32(f"{a}.context_length", 32768)
     w.add_uint32(f"{a}.embedding_length", d)
     w.add_uint32(f"{a}.block_count", nl)
@@ -100,23 +111,36 @@ def write_model(path: str | os.PathLike, cfg: dict, seed: int = 1, body: str = "
         idx += 1
         w.add_tensor(name, (np.float32(1.0) + _normal(seed, idx, (n,), 0.02)).astype(np.float32))
 
+    def bias(name, n):
+        nonlocal idx
+        idx += 1
+        w.add_tensor(name, _normal(seed, idx, (n,), 0.02).astype(np.float32))
+
+    gemma = a == "gemma3"
     mat("token_embd.weight", V, d, head)
+    if cfg.get("untied"):
+        mat("output.weight", V, d, head)
     norm("output_norm.weight", d)
     for l in range(nl):
         p = f"blk.{l}."
         mat(p + "attn_q.weight", nh * hd, d, body)
         mat(p + "attn_k.weight", nkv * hd, d, body)
         mat(p + "attn_v.weight", nkv * hd, d, body)
+        if not gemma:
+            bias(p + "attn_q.bias", nh * hd)
+            bias(p + "attn_k.bias", nkv * hd)
+            bias(p + "attn_v.bias", nkv * hd)
         mat(p + "attn_output.weight", d, nh * hd, body)
         mat(p + "ffn_gate.weight", ff, d, body)
         mat(p + "ffn_up.weight", ff, d, body)
         mat(p + "ffn_down.weight", d, ff, body)
         norm(p + "attn_norm.weight", d)
-        norm(p + "attn_q_norm.weight", hd)
-        norm(p + "attn_k_norm.weight", hd)
-        norm(p + "post_attention_norm.weight", d)
         norm(p + "ffn_norm.weight", d)
-        norm(p + "post_ffw_norm.weight", d)
+        if gemma:
+            norm(p + "attn_q_norm.weight", hd)
+            norm(p + "attn_k_norm.weight", hd)
+            norm(p + "post_attention_norm.weight", d)
+            norm(p + "post_ffw_norm.weight", d)
     w.write_header_to_file()
     w.write_kv_data_to_file()
     w.write_tensors_to_file()

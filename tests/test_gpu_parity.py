@@ -252,3 +252,31 @@ def test_parallel_requantized_formats(torch, isa, small, body_bits, head_bits):
         lp, am = g.score(toks, head)
         lpo, amo, _, _ = o.score(toks, head)
         assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo), (head, np.abs(lp - lpo).max())
+
+
+@pytest.fixture(scope="module")
+def small_qwen2(model_dir):
+    return synth.ensure("small-qwen2", classes=64, directory=model_dir)
+
+
+@pytest.mark.parametrize("schedule", ["sequential", "parallel"])
+@pytest.mark.parametrize("head", [FULL, TWO_LEVEL])
+def test_qwen2_scoring_exact(torch, isa, small_qwen2, head, schedule):
+    """The qwen2 branch (biases, SiLU, untied output, 7 query heads per kv head) under both schedules."""
+    from gem_b200 import PARALLEL, SEQUENTIAL
+    g = Gemma(small_qwen2.gguf, ctx=128)
+    g.load_twolevel(small_qwen2.twolevel)
+    g.set_schedule(SEQUENTIAL if schedule == "sequential" else PARALLEL)
+    o = orc.Model(small_qwen2.gguf, ctx=128, threads=REF_THREADS, isa="avx512")
+    o.load_twolevel(small_qwen2.twolevel)
+    toks = synth.tokens(45, g.vocab, seed=77)
+    lp, am = g.score(toks, head)
+    lpo, amo, _, _ = o.score(toks, head)
+    assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo), np.abs(lp - lpo).max()
+
+
+def test_qwen2_forward_bit_exact(torch, isa, small_qwen2):
+    g = Gemma(small_qwen2.gguf, ctx=64)
+    o = orc.Model(small_qwen2.gguf, ctx=64, threads=REF_THREADS, isa="avx512")
+    for i, t in enumerate(synth.tokens(20, g.vocab, seed=78)):
+        assert np.array_equal(g.forward(int(t), i).view(np.uint32), o.forward(int(t), i).view(np.uint32)), i

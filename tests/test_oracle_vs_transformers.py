@@ -89,3 +89,55 @@ def test_oracle_matches_numpy_restatement(small):
     # float64 reductions in numpy vs sequential float32 in the oracle: ~1e-7 until an int8 code flips;
     # a flip is bounded by the quantization noise (see the cross-ISA spread documented in DESIGN.md)
     assert worst < 2e-2
+
+
+@pytest.fixture(scope="module")
+def small_qwen2(model_dir):
+    return synth.ensure("small-qwen2", classes=64, directory=model_dir)
+
+
+def test_oracle_qwen2_forward_matches_transformers(small_qwen2, threads):
+    """The qwen2 branch (model.rs:160-161, 188-190, 311-315, 400-407: q/k/v biases, SiLU, untied output,
+    no embedding scale, every layer global) against transformers' Qwen2 on the same weights."""
+    torch = pytest.importorskip("torch")
+    tr = pytest.importorskip("transformers")
+    import gguf
+    from gguf import quants
+    cfg = small_qwen2.cfg
+    r = gguf.GGUFReader(str(small_qwen2.gguf))
+    T = {t.name: t for t in r.tensors}
+
+    def deq(name):
+        t = T[name]
+        a = np.asarray(quants.dequantize(t.data, t.tensor_type), np.float32)
+        if len(t.shape) == 2:
+            a = a.reshape(int(t.shape[1]), int(t.shape[0]))
+        return torch.tensor(a.reshape(-1) if len(t.shape) == 1 else a)
+
+    c = tr.Qwen2Config(vocab_size=cfg["vocab"], hidden_size=cfg["d"], intermediate_size=cfg["ff"],
+                       num_hidden_layers=cfg["layers"], num_attention_heads=cfg["nh"], num_key_value_heads=cfg["nkv"],
+                       head_dim=cfg["hd"], rms_norm_eps=cfg["eps"], rope_theta=cfg["rope_base"],
+                       max_position_embeddings=4096, tie_word_embeddings=False, attn_implementation="eager")
+    sd = {"model.embed_tokens.weight": deq("token_embd.weight"), "lm_head.weight": deq("output.weight"),
+          "model.norm.weight": deq("output_norm.weight")}
+    names = {"attn_q.weight": "self_attn.q_proj.weight", "attn_k.weight": "self_attn.k_proj.weight",
+             "attn_v.weight": "self_attn.v_proj.weight", "attn_q.bias": "self_attn.q_proj.bias",
+             "attn_k.bias": "self_attn.k_proj.bias", "attn_v.bias": "self_attn.v_proj.bias",
+             "attn_output.weight": "self_attn.o_proj.weight", "ffn_gate.weight": "mlp.gate_proj.weight",
+             "ffn_up.weight": "mlp.up_proj.weight", "ffn_down.weight": "mlp.down_proj.weight",
+             "attn_norm.weight": "input_layernorm.weight", "ffn_norm.weight": "post_attention_layernorm.weight"}
+    for l in range(cfg["layers"]):
+        for a, b in names.items():
+            sd[f"model.layers.{l}.{b}"] = deq(f"blk.{l}.{a}")
+    m = tr.Qwen2ForCausalLM(c).float().eval()
+    missing, unexpected = m.load_state_dict(sd, strict=False)
+    assert not unexpected and all("rotary" in k for k in missing), (missing, unexpected)
+    n = 40
+    toks = synth.tokens(n + 1, cfg["vocab"], seed=9)
+    o = orc.Model(small_qwen2.gguf, ctx=128, threads=threads)
+    lp, _, _, _ = o.score(toks, 0)
+    with torch.no_grad():
+        lg = m(torch.tensor(toks[None, :n].astype(np.int64))).logits[0].double()
+    want = torch.log_softmax(lg, -1)[torch.arange(n), torch.tensor(toks[1:n + 1].astype(np.int64))].numpy()
+    d = np.abs(lp - want)
+    assert d.max() < 0.05 and d.mean() < 0.015, (d.max(), d.mean())
