@@ -71,17 +71,26 @@ __global__ void k_seq_embed(MatView E, const uint32_t* toks, int vocab, float sc
 // ------------------------------------------------------------------------------------------------
 constexpr int kNormWarps = 4;
 
+// n a multiple of 32. The next 16 values are loaded while the current 16 are added, so the chain of
+// dependent adds is the only latency left.
 __device__ __forceinline__ float warp_seq_sum(const float* sq, int n, int lane) {
   float s = 0.0f;
-  if (lane == 0)
-#pragma unroll 8
-    for (int j = 0; j < n; j += 4) {
-      float4 v = *(const float4*)(sq + j);
-      s = add(s, v.x);
-      s = add(s, v.y);
-      s = add(s, v.z);
-      s = add(s, v.w);
+  if (lane == 0) {
+    const float4* p = (const float4*)sq;
+    const int n4 = n / 4;
+    float4 a[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = p[u];
+    for (int j = 4; j <= n4; j += 4) {
+      float4 nx[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) nx[u] = j < n4 ? p[j + u] : a[u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s = add(add(add(add(s, a[u].x), a[u].y), a[u].z), a[u].w);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = nx[u];
     }
+  }
   return __shfl_sync(0xffffffffu, s, 0);
 }
 
@@ -90,7 +99,7 @@ constexpr int kNormMaxV = 9;  // float4 per lane: d <= 1152
 __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const float* delta, const float* w_post,
                                                               const float* w_pre, float eps, int d, int T, int8_t* aq,
                                                               float* as, float* xn_out) {
-  extern __shared__ __align__(16) float sn[];  // w_post [d], w_pre [d], then per warp xs [d], sq [d]
+  extern __shared__ __align__(16) float sn[];  // w_post [d], w_pre [d], then per warp [2 d] (sq in the second half)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n4 = d / 4;
   float* swpost = sn;
   float* swpre = sn + d;
@@ -101,8 +110,7 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const fl
   __syncthreads();
   const int t = blockIdx.x * kNormWarps + warp;
   if (t >= T) return;
-  float* xs = sn + 2 * d + (size_t)warp * 2 * d;
-  float* sq = xs + d;
+  float* sq = sn + 2 * d + (size_t)warp * 2 * d + d;
   float4* xt = (float4*)(x + (size_t)t * d);
   float4 xv[kNormMaxV], dv[kNormMaxV];
 #pragma unroll
@@ -140,20 +148,40 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const fl
 #pragma unroll
   for (int k = 0; k < kNormMaxV; ++k) {
     const int i = lane + 32 * k;
-    if (i < n4) {
-      ((float4*)xs)[i] = xv[k];
-      ((float4*)sq)[i] = sq4(xv[k]);
-    }
+    if (i < n4) ((float4*)sq)[i] = sq4(xv[k]);
   }
   __syncwarp();
   const float r = rms_r_exact(warp_seq_sum(sq, d, lane), d, eps);
+  // rmsnorm (model.rs:81-87), then Act::quantize from registers: the 32-block b is float4s 8b .. 8b + 7,
+  // held by 8 consecutive lanes, so a warp quantizes four blocks at once (block max over 8 lanes; a
+  // max is exact in any order). d is a multiple of 32, so a group of 8 lanes is wholly in or out.
   const int nb = d / 32;
-#pragma unroll 4
-  for (int b = 0; b < nb; ++b) {
-    const int j = b * 32 + lane;
-    const float v = mul(mul(xs[j], r), swpre[j]);  // rmsnorm (model.rs:81-87)
-    if (xn_out) xn_out[(size_t)t * d + j] = v;
-    if (aq) quant_block_warp_x(v, lane, aq + (size_t)t * d + b * 32, as + (size_t)t * nb + b);
+#pragma unroll
+  for (int k = 0; k < kNormMaxV; ++k) {
+    if (32 * k >= n4) break;
+    const int i = lane + 32 * k;
+    const bool in = i < n4;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (in) {
+      const float4 w = ((const float4*)swpre)[i];
+      v = make_float4(mul(mul(xv[k].x, r), w.x), mul(mul(xv[k].y, r), w.y), mul(mul(xv[k].z, r), w.z),
+                      mul(mul(xv[k].w, r), w.w));
+      if (xn_out) ((float4*)(xn_out + (size_t)t * d))[i] = v;
+    }
+    if (aq) {
+      float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+      if (in) {  // quant_block_warp_x's arithmetic: d = amax / 127, q = rn(v * (1 / d))
+        const float dd = div(m, 127.0f);
+        const float inv = dd > 0.0f ? div(1.0f, dd) : 0.0f;
+        const uint32_t q0 = (uint32_t)__float2int_rn(mul(v.x, inv)) & 0xffu, q1 = (uint32_t)__float2int_rn(mul(v.y, inv)) & 0xffu,
+                       q2 = (uint32_t)__float2int_rn(mul(v.z, inv)) & 0xffu, q3 = (uint32_t)__float2int_rn(mul(v.w, inv)) & 0xffu;
+        ((uint32_t*)(aq + (size_t)t * d))[i] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+        if ((lane & 7) == 0) as[(size_t)t * nb + (i >> 3)] = dd;
+      }
+    }
   }
 }
 
@@ -275,9 +303,14 @@ __global__ void __launch_bounds__(kGemmThreads, RN == 8 ? 2 : 3) k_seq_gemm(MatV
       const float swb = ld_scale(wsc, b);
       float sa[RN];
 #pragma unroll
-      for (int k = 0; k < RN; k += 4) {
-        const float4 v = *(const float4*)(asc + b * G::BN + k);
-        sa[k] = v.x, sa[k + 1] = v.y, sa[k + 2] = v.z, sa[k + 3] = v.w;
+      for (int k = 0; k < RN; k += (RN % 4 == 0 ? 4 : 2)) {  // this thread's RN scales start at a multiple of RN
+        if constexpr (RN % 4 == 0) {
+          const float4 v = *(const float4*)(asc + b * G::BN + k);
+          sa[k] = v.x, sa[k + 1] = v.y, sa[k + 2] = v.z, sa[k + 3] = v.w;
+        } else {
+          const float2 v = *(const float2*)(asc + b * G::BN + k);
+          sa[k] = v.x, sa[k + 1] = v.y;
+        }
       }
 #pragma unroll
       for (int k = 0; k < RN; ++k) {
@@ -757,17 +790,24 @@ bool seq_gemm_supported(const MatView& w) {
 // Tile choice: estimated time = waves x time of one wave, with 2 resident CTAs per SM for 8 positions
 // per thread and 3 for 4 (register-bound occupancy); a wave of 4-position tiles (48 positions per SM)
 // takes about 0.78 of a wave of 8-position tiles (64 per SM), as measured on B200.
+// Positions per thread (RN; a CTA takes 32 rows x 4 RN positions) for a projection of `rows` rows over
+// T positions: the fewest estimated wave-times, a wave of RN = 8 (2 CTAs per SM) taking 8 units and a
+// wave of RN = 4 or 6 (3 CTAs per SM) 1.55 units per position of RN (measured: the three shapes give
+// the same throughput per SM when their last wave is full).
 static int gemm_rn(int rows, int T, int sms) {
-  static const int forced = [] {  // tuning override: GEM_GEMM_RN=4 or 8
+  static const int forced = [] {  // tuning override: GEM_GEMM_RN=4, 6 or 8
     const char* e = std::getenv("GEM_GEMM_RN");
     return e ? std::atoi(e) : 0;
   }();
-  if (forced == 4 || forced == 8) return forced;
-  const long long c8 = (long long)((T + 31) / 32) * ((rows + kGemmBM - 1) / kGemmBM);
-  const long long c4 = (long long)((T + 15) / 16) * ((rows + kGemmBM - 1) / kGemmBM);
-  const double t8 = (double)((c8 + 2LL * sms - 1) / (2LL * sms));
-  const double t4 = 0.78 * (double)((c4 + 3LL * sms - 1) / (3LL * sms));
-  return t4 < t8 ? 4 : 8;
+  if (forced == 4 || forced == 6 || forced == 8) return forced;
+  const long long rt = (rows + kGemmBM - 1) / kGemmBM;
+  auto cost = [&](int rn, int occ, double unit) {
+    const long long ctas = (long long)((T + 4 * rn - 1) / (4 * rn)) * rt;
+    return (double)((ctas + (long long)occ * sms - 1) / ((long long)occ * sms)) * unit * rn;
+  };
+  const double c8 = cost(8, 2, 1.0), c6 = cost(6, 3, 1.55), c4 = cost(4, 3, 1.55);
+  if (c8 <= c6 && c8 <= c4) return 8;
+  return c6 < c4 ? 6 : 4;
 }
 
 void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
@@ -784,10 +824,11 @@ void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T,
     dim3 grid((T + GT::BN - 1) / GT::BN, (w.rows + kGemmBM - 1) / kGemmBM);                                    \
     k_seq_gemm<B, S, RNV><<<grid, kGemmThreads, GT::SMEM, st>>>(w, aq, as, T, y, ldy);                          \
   } while (0)
-#define F(B, S)             \
-  do {                      \
-    if (rn == 8) F2(B, S, 8); \
-    else F2(B, S, 4);        \
+#define F(B, S)                 \
+  do {                          \
+    if (rn == 8) F2(B, S, 8);     \
+    else if (rn == 6) F2(B, S, 6); \
+    else F2(B, S, 4);            \
   } while (0)
   GEM_DISPATCH_Q(w.bits, w.scale_f32, F);
 #undef F
