@@ -359,81 +359,114 @@ __global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, int L,
                   qn + (size_t)t * A.nh * A.hd, smp, s_r);
 }
 
-// Tiled scores: a CTA takes kAttnTQ consecutive positions (rows: position x query head of kv group
-// blockIdx.z) against kAttnPC key positions starting at pbase + blockIdx.y * kAttnPC, with the queries
-// and the key rows staged in shared memory, so each key row is read once per tile instead of once
-// per position. A thread pair computes one row against 8 keys with dot512_pair's lanes. Only keys in
-// a row's window [lo, pos] are written.
-constexpr int kAttnTQ = 8, kAttnPC = 64;
+// Tiled scores: a CTA takes kAttnTQ consecutive positions (R = kAttnTQ * G rows: position x query head
+// of kv group blockIdx.z) against kScKC key positions from pbase + blockIdx.y * kScKC, both staged in
+// shared memory (rows padded to hd + 4 floats, so 8 consecutive rows start in distinct banks), each
+// key row read once per tile. dot512's 16 lanes are split over a quad: thread u holds lanes 4u .. 4u + 3
+// (elements 16c + 4u .. + 3) of a block of 4 rows x 4 keys, each lane's FMAs in the reference's order.
+// A warp's 8 quads cover 8 rows x 16 keys (2 row groups x 4 key groups), so a query load serves 4 quads
+// and a key load 2. The halving reduction (lane i + lane i + 8, then + 4, + 2, + 1) runs over the quad
+// with shuffles, each thread finishing the 4 pairs of one row. Only keys in a row's window [lo, pos]
+// are written.
+constexpr int kAttnTQ = 8, kScKC = 32;
 
 template <int G>
-__global__ void __launch_bounds__(256) k_seq_scores_tile(AttnArgs A0, const float* qn, int L, uint32_t pos0,
-                                                         size_t kv_stride, uint32_t pbase, float* scores, int sstride) {
+__global__ void __launch_bounds__(256, 2) k_seq_scores_tile(AttnArgs A0, const float* qn, int L, uint32_t pos0,
+                                                            size_t kv_stride, uint32_t pbase, float* scores,
+                                                            int sstride) {
   extern __shared__ __align__(16) float sm[];
-  constexpr int R = kAttnTQ * G;
+  constexpr int R = kAttnTQ * G;  // a multiple of 8
   const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
   const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
-  const int hd = A.hd, g = blockIdx.z, qs = hd + 4;  // padded query rows: 16 rows hit distinct banks
+  const int hd = A.hd, g = blockIdx.z, rs = hd + 4;
   const int t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0);  // positions inside the sequence
   qn += (size_t)sq_i * L * A.nh * hd;                                        // this sequence's rows
   scores += (size_t)sq_i * L * A.nh * sstride;
-  const uint32_t p0 = pbase + blockIdx.y * kAttnPC;
+  const uint32_t p0 = pbase + blockIdx.y * kScKC;
   const uint32_t need_lo = window_lo(pos0 + t0, A.window), need_hi = pos0 + t0 + tn - 1;
-  if (p0 > need_hi || p0 + kAttnPC <= need_lo) return;
-  float* sq = sm;              // [R][hd + 4]
-  float* sk = sm + R * qs;     // [PC][hd]
+  if (p0 > need_hi || p0 + kScKC <= need_lo) return;
+  float* sq = sm;           // [R][hd + 4]
+  float* sk = sm + R * rs;  // [kScKC][hd + 4]
   const int rw = A.nkv * hd, h4 = hd / 4;
-  for (int i = threadIdx.x; i < R * h4; i += blockDim.x) {
-    const int row = i / h4, e = i % h4, tt = row / G, h = row % G;
+  // staging: thread i copies 16-byte column i % h4 of rows i / h4, i / h4 + step, ... (one division)
+  const int e = (int)threadIdx.x % h4, step = (int)blockDim.x / h4;
+  const bool whole = (int)blockDim.x % h4 == 0;
+  for (int i = threadIdx.x, row = (int)threadIdx.x / h4; i < R * h4; i += blockDim.x, row += step) {
+    const int rr = whole ? row : i / h4, ee = whole ? e : i % h4, tt = rr / G, h = rr % G;
     const bool ok = tt < tn;
-    cp16(sq + row * qs + e * 4, qn + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * hd + e * 4 : 0), ok);
+    cp16(sq + rr * rs + ee * 4, qn + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * hd + ee * 4 : 0), ok);
   }
-  for (int i = threadIdx.x; i < kAttnPC * h4; i += blockDim.x) {
-    const int pr = i / h4, e = i % h4;
-    const uint32_t p = p0 + pr;
+  for (int i = threadIdx.x, pr = (int)threadIdx.x / h4; i < kScKC * h4; i += blockDim.x, pr += step) {
+    const int rr = whole ? pr : i / h4, ee = whole ? e : i % h4;
+    const uint32_t p = p0 + rr;
     const bool ok = p <= need_hi;
-    cp16(sk + i * 4, A.kcache + (ok ? (size_t)p * rw + g * hd + e * 4 : 0), ok);
+    cp16(sk + rr * rs + ee * 4, A.kcache + (ok ? (size_t)p * rw + g * hd + ee * 4 : 0), ok);
   }
   cp_commit();
   cp_wait<0>();
   __syncthreads();
-  // A thread pair takes one row against 8 keys (dot512_pair's lanes); a warp's 16 pairs share the keys,
-  // so key reads are broadcasts and query rows (padded) hit distinct banks.
-  const int half = threadIdx.x & 1, pairs = blockDim.x / 2;
-  constexpr int ntask = R * (kAttnPC / 8);
-  for (int base = 0; base < ntask; base += pairs) {
-    const int task = base + (int)threadIdx.x / 2;
-    const bool ok = task < ntask;
-    const int tk = ok ? task : 0;
-    const int row = tk % R, pg = tk / R;
-    const float* q = sq + row * qs + half * 8;
-    const float* k = sk + (pg * 8) * hd + half * 8;
-    float2 acc[8][4];
+  const int lane = threadIdx.x & 31, u = lane & 3, qd = lane >> 2, rg = qd >> 2, kg = qd & 3;
+  constexpr int KCW = kScKC / 16, NWT = (R / 8) * KCW;  // warp tiles of 8 rows x 16 keys
+  for (int wt = (int)threadIdx.x >> 5; wt < NWT; wt += (int)blockDim.x >> 5) {
+    const int r0 = (wt / KCW) * 8 + rg * 4, k0 = (wt % KCW) * 16 + kg * 4;
+    const float* qp = sq + r0 * rs + 4 * u;
+    const float* kp = sk + k0 * rs + 4 * u;
+    float2 acc[4][4][2];  // [row][key][lanes (4u, 4u + 1), (4u + 2, 4u + 3)]
 #pragma unroll
-    for (int u = 0; u < 8; ++u)
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[u][e] = make_float2(0.0f, 0.0f);
+      for (int k = 0; k < 4; ++k) acc[r][k][0] = acc[r][k][1] = make_float2(0.0f, 0.0f);
     for (int c = 0; c < hd / 16; ++c) {
-      const float4 q0 = *(const float4*)(q + c * 16), q1 = *(const float4*)(q + c * 16 + 4);
-      const float2 qv[4] = {make_float2(q0.x, q0.y), make_float2(q0.z, q0.w), make_float2(q1.x, q1.y), make_float2(q1.z, q1.w)};
+      float4 qv[4], kv[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float4 k0 = *(const float4*)(k + u * hd + c * 16), k1 = *(const float4*)(k + u * hd + c * 16 + 4);
-        acc[u][0] = __ffma2_rn(qv[0], make_float2(k0.x, k0.y), acc[u][0]);
-        acc[u][1] = __ffma2_rn(qv[1], make_float2(k0.z, k0.w), acc[u][1]);
-        acc[u][2] = __ffma2_rn(qv[2], make_float2(k1.x, k1.y), acc[u][2]);
-        acc[u][3] = __ffma2_rn(qv[3], make_float2(k1.z, k1.w), acc[u][3]);
-      }
+      for (int r = 0; r < 4; ++r) qv[r] = *(const float4*)(qp + r * rs + 16 * c);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) kv[k] = *(const float4*)(kp + k * rs + 16 * c);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[r][k][0] = __ffma2_rn(make_float2(qv[r].x, qv[r].y), make_float2(kv[k].x, kv[k].y), acc[r][k][0]);
+          acc[r][k][1] = __ffma2_rn(make_float2(qv[r].z, qv[r].w), make_float2(kv[k].z, kv[k].w), acc[r][k][1]);
+        }
     }
-    const int tt = row / G, h = row % G;
-    const uint32_t pos = pos0 + t0 + tt, lo = window_lo(pos, A.window);
+    // Round 1 (partner u ^ 2 holds lanes i + 8): threads 0, 1 keep rows 0, 1 and threads 2, 3 rows 2, 3;
+    // b = lane i + lane i + 8 for i = 4 (u & 1) + j.
+    float b[2][4][4];  // [kept row][key][j]
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float a8[8] = {acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y, acc[u][2].x, acc[u][2].y, acc[u][3].x, acc[u][3].y};
-      const float sc = reduce16_pair(a8);
-      const uint32_t p = p0 + pg * 8 + u;
-      if (ok && half == 0 && tt < tn && p >= lo && p <= pos)
-        scores[((size_t)(t0 + tt) * A.nh + g * G + h) * sstride + (p - lo)] = sc;
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float l[4] = {acc[m][k][0].x, acc[m][k][0].y, acc[m][k][1].x, acc[m][k][1].y};
+        const float h[4] = {acc[m + 2][k][0].x, acc[m + 2][k][0].y, acc[m + 2][k][1].x, acc[m + 2][k][1].y};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float got = __shfl_xor_sync(0xffffffffu, u < 2 ? h[j] : l[j], 2);
+          b[m][k][j] = add(u < 2 ? l[j] : h[j], got);
+        }
+      }
+    // Round 2 (partner u ^ 1 holds i + 4): even threads keep row 0 of their pair of rows, odd row 1;
+    // c = b_i + b_i+4 for i = j, then (c0 + c2) + (c1 + c3).
+    float res[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float cc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float got = __shfl_xor_sync(0xffffffffu, (u & 1) ? b[0][k][j] : b[1][k][j], 1);
+        cc[j] = add((u & 1) ? b[1][k][j] : b[0][k][j], got);
+      }
+      res[k] = add(add(cc[0], cc[2]), add(cc[1], cc[3]));
+    }
+    const int row = r0 + u, tt = row / G, h = row % G;  // thread u finishes row r0 + u, keys k0 .. k0 + 3
+    if (tt < tn) {
+      const uint32_t pos = pos0 + t0 + tt, lo = window_lo(pos, A.window);
+      float* out = scores + ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t p = p0 + k0 + k;
+        if (p >= lo && p <= pos) out[p - lo] = res[k];
+      }
     }
   }
 }
@@ -494,6 +527,7 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
   part += (size_t)sq_i * L * A.nh * threads * A.hd;
   const int hd = A.hd, h4 = hd / 4, t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0), r = blockIdx.y;
   const int j2 = threadIdx.x * 2;  // this thread's two output columns
+  const int ve = (int)threadIdx.x % h4, vr0 = (int)threadIdx.x / h4;  // V staging: column, first row
   const int rw = A.nkv * hd;
   float* sp = sv + kPvRows * hd;
   if (threadIdx.x < kAttnTQ) {
@@ -519,10 +553,9 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
     for (uint32_t c0 = ua; c0 < ub; c0 += kPvRows) {
       const int rows = (int)min((uint32_t)kPvRows, ub - c0), rows4 = (rows + 3) & ~3;
       __syncthreads();
-      for (int i = threadIdx.x; i < rows4 * h4; i += blockDim.x) {  // rows past `rows` are zero
-        const int pr = i / h4, e = i % h4;
-        const bool ok = pr < rows;
-        cp16(sv + pr * hd + e * 4, A.vcache + (ok ? (size_t)(c0 + pr) * rw + g * hd + e * 4 : 0), ok);
+      for (int pr = vr0; pr < rows4; pr += 2) {  // blockDim.x = 2 h4: a thread keeps its 16-byte column
+        const bool ok = pr < rows;                // rows past `rows` are zero
+        cp16(sv + pr * hd + ve * 4, A.vcache + (ok ? (size_t)(c0 + pr) * rw + g * hd + ve * 4 : 0), ok);
       }
       // a row's probabilities are zero outside its range, which makes its FMAs there exact no-ops
       // (a range's sum starts at +0 and never becomes -0, so adding 0 * v changes nothing)
@@ -842,10 +875,10 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
   if (G < 1 || G > 8) return;  // rejected by the caller before any launch
   k_seq_attn_prep<<<dim3(T, A.nkv), 256, (size_t)(G + 2) * A.hd * 4, st>>>(A, qkv, qkv_ld, L, pos0, kv_stride, qn);
   const uint32_t pbase = window_lo(pos0, A.window);
-  const int nchunk = (int)((pos0 + L - pbase + kAttnPC - 1) / kAttnPC);
+  const int nchunk = (int)((pos0 + L - pbase + kScKC - 1) / kScKC);
   const int tps = (L + kAttnTQ - 1) / kAttnTQ;
   const dim3 sgrid(tps * nseq, nchunk, A.nkv), pgrid(tps * nseq, threads);
-  const size_t ssm = ((size_t)kAttnTQ * G * (A.hd + 4) + (size_t)kAttnPC * A.hd) * 4;
+  const size_t ssm = ((size_t)kAttnTQ * G + kScKC) * (A.hd + 4) * 4;
   const size_t psm = ((size_t)kPvRows * A.hd + (size_t)kAttnTQ * G * kPvRows) * 4;
   const int pth = A.hd / 2;
 #define F(GG)                                                                                                        \
