@@ -49,6 +49,14 @@ __host__ __device__ __forceinline__ uint32_t window_lo(uint32_t pos, int window)
   return (window > 0 && pos + 1 > (uint32_t)window) ? pos + 1 - window : 0;
 }
 
+// Programmatic dependent launch: every kernel of this file is launched so that the next one may be
+// scheduled while it drains, and each kernel's first action waits for its predecessor's completion and
+// memory (a no-op when launched without the attribute), so nothing reads a predecessor's output early.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------
@@ -56,6 +64,7 @@ __host__ __device__ __forceinline__ uint32_t window_lo(uint32_t pos, int window)
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
 __global__ void k_seq_embed(MatView E, const uint32_t* toks, int vocab, float scale, float* x, int* err) {
+  pdl_wait();
   const int t = blockIdx.x;
   uint32_t tok = toks[t];
   if (tok >= (uint32_t)vocab) {
@@ -99,6 +108,7 @@ constexpr int kNormMaxV = 9;  // float4 per lane: d <= 1152
 __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const float* delta, const float* w_post,
                                                               const float* w_pre, float eps, int d, int T, int8_t* aq,
                                                               float* as, float* xn_out) {
+  pdl_wait();
   extern __shared__ __align__(16) float sn[];  // w_post [d], w_pre [d], then per warp [2 d] (sq in the second half)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n4 = d / 4;
   float* swpost = sn;
@@ -247,6 +257,7 @@ __device__ __forceinline__ void gemm_issue(unsigned char* stage, const MatView& 
 template <int BITS, typename ST, int RN>
 __global__ void __launch_bounds__(kGemmThreads, RN == 8 ? 2 : 3) k_seq_gemm(MatView w, const int8_t* aq,
                                                                              const float* as, int T, float* y, int ldy) {
+  pdl_wait();
   using G = GemmTile<BITS, ST, RN>;
   extern __shared__ __align__(128) unsigned char sg[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane & 1;
@@ -352,6 +363,7 @@ __device__ __forceinline__ AttnArgs seq_kv(const AttnArgs& A, int s, size_t kv_s
 
 __global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, int L, uint32_t pos0, size_t kv_stride,
                                 float* qn) {
+  pdl_wait();
   extern __shared__ __align__(16) float smp[];
   __shared__ float s_r[17];
   const int t = blockIdx.x, s = t / L;
@@ -374,6 +386,7 @@ template <int G>
 __global__ void __launch_bounds__(256, 2) k_seq_scores_tile(AttnArgs A0, const float* qn, int L, uint32_t pos0,
                                                             size_t kv_stride, uint32_t pbase, float* scores,
                                                             int sstride) {
+  pdl_wait();
   extern __shared__ __align__(16) float sm[];
   constexpr int R = kAttnTQ * G;  // a multiple of 8
   const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
@@ -474,6 +487,7 @@ __global__ void __launch_bounds__(256, 2) k_seq_scores_tile(AttnArgs A0, const f
 // Softmax per (position, head) with the reference's order: max, exp_fast(s - max), sequential sum,
 // multiply by 1/sum. One warp per (position, head).
 __global__ void k_seq_softmax(AttnArgs A, int T, int L, uint32_t pos0, float* scores, int sstride) {
+  pdl_wait();
   extern __shared__ __align__(16) float ss[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int task = blockIdx.x * nw + warp;
@@ -518,6 +532,7 @@ constexpr int kPvRows = 32;
 template <int G>
 __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_t pos0, size_t kv_stride,
                                                      const float* scores, int sstride, int threads, float* part) {
+  pdl_wait();
   constexpr int R = kAttnTQ * G;               // rows of the tile: position x head of the group
   extern __shared__ __align__(16) float sv[];  // V [kPvRows][hd], then probabilities P [R][kPvRows]
   __shared__ uint32_t s_lo[kAttnTQ], s_a[kAttnTQ], s_b[kAttnTQ];
@@ -593,6 +608,7 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
 // att[t][h][j] = partials summed in range order (from 0), then Act::quantize. One CTA per
 // (position, head), all partial loads in flight before the ordered adds.
 __global__ void k_seq_pv_combine(AttnArgs A, const float* part, int threads, int8_t* aq, float* as) {
+  pdl_wait();
   const int t = blockIdx.x, h = blockIdx.y, hd = A.hd, j = threadIdx.x, lane = j & 31;
   const int nbh = A.nh * hd / 32;
   const float* pp = part + ((size_t)t * A.nh + h) * threads * hd + j;
@@ -613,6 +629,7 @@ __global__ void k_seq_pv_combine(AttnArgs A, const float* part, int threads, int
 // Gate (k_glu_quant per position): v = gelu_tanh(g) * u (or silu(g) * u), then Act::quantize.
 // ------------------------------------------------------------------------------------------------
 __global__ void k_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int nbk = ff / 32;
   const long long warps = (long long)(blockDim.x >> 5) * gridDim.x;
@@ -642,6 +659,7 @@ __global__ void k_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t
 // ------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256, 2) k_seq_class_logits(const float* A, const float* bias, int k, const float* h,
                                                              int d, int T, float* cl) {
+  pdl_wait();
   extern __shared__ __align__(16) float sh[];  // [32][d]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane & 1;
   const int tok0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
@@ -693,6 +711,7 @@ __global__ void __launch_bounds__(256, 2) k_seq_class_logits(const float* A, con
 // ------------------------------------------------------------------------------------------------
 __global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* targets, float* lp, uint32_t* am,
                                    int* err) {
+  pdl_wait();
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
   const int t = blockIdx.x;
@@ -731,6 +750,7 @@ __global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* t
 // the target is another rank's). out[t] = {m, s, best, best id bits, target logit}.
 __global__ void k_seq_logit_partials(const float* logits, int V, uint32_t row0, const uint32_t* targets, uint32_t vocab,
                                      float* out, int* err) {
+  pdl_wait();
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
   const int t = blockIdx.x;
@@ -767,6 +787,7 @@ __global__ void k_seq_logit_partials(const float* logits, int V, uint32_t row0, 
 
 // Merges the ranks' partials (gathered [nranks][T][5]) into logprob and argmax (ties: lowest id).
 __global__ void k_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am) {
+  pdl_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   Lse L{-INFINITY, 0.0f};
@@ -793,9 +814,33 @@ __global__ void k_seq_logit_combine(const float* parts, int nranks, int T, float
     else { F(4, float); }                                     \
   } while (0)
 
+
+// Launches `k` with programmatic stream serialization (see pdl_wait); GEM_PDL=0 turns it off.
+static bool pdl_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("GEM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+template <typename... KArgs, typename... Args>
+static void launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  if (!pdl_on()) {
+    k<<<grid, block, smem, st>>>(args...);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid, cfg.blockDim = block, cfg.dynamicSmemBytes = smem, cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at, cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, float scale, float* x, int* err,
                       cudaStream_t st) {
-#define F(B, S) k_seq_embed<B, S><<<T, 256, 0, st>>>(E, toks, vocab, scale, x, err)
+#define F(B, S) launch_k(k_seq_embed<B, S>, dim3(T), dim3(256), 0, st, E, toks, vocab, scale, x, err)
   if (E.bits == 16) F(16, __half);
   else GEM_DISPATCH_Q(E.bits, E.scale_f32, F);
 #undef F
@@ -809,7 +854,7 @@ void launch_seq_norm(float* x, const float* delta, const float* w_post, const fl
     cudaFuncSetAttribute(k_seq_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     init = true;
   }
-  k_seq_norm<<<(T + kNormWarps - 1) / kNormWarps, kNormWarps * 32, sm, st>>>(x, delta, w_post, w_pre, eps, d, T, aq, as,
+  launch_k(k_seq_norm, dim3((T + kNormWarps - 1) / kNormWarps), dim3(kNormWarps * 32), sm, st, x, delta, w_post, w_pre, eps, d, T, aq, as,
                                                                               xn_out);
 }
 
@@ -855,7 +900,7 @@ void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T,
       init = true;                                                                                              \
     }                                                                                                           \
     dim3 grid((T + GT::BN - 1) / GT::BN, (w.rows + kGemmBM - 1) / kGemmBM);                                    \
-    k_seq_gemm<B, S, RNV><<<grid, kGemmThreads, GT::SMEM, st>>>(w, aq, as, T, y, ldy);                          \
+    launch_k(k_seq_gemm<B, S, RNV>, dim3(grid), dim3(kGemmThreads), GT::SMEM, st, w, aq, as, T, y, ldy);                          \
   } while (0)
 #define F(B, S)                 \
   do {                          \
@@ -873,7 +918,7 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
                      cudaStream_t st) {
   const int G = A.nh / A.nkv, T = L * nseq;
   if (G < 1 || G > 8) return;  // rejected by the caller before any launch
-  k_seq_attn_prep<<<dim3(T, A.nkv), 256, (size_t)(G + 2) * A.hd * 4, st>>>(A, qkv, qkv_ld, L, pos0, kv_stride, qn);
+  launch_k(k_seq_attn_prep, dim3(dim3(T, A.nkv)), dim3(256), (size_t)(G + 2) * A.hd * 4, st, A, qkv, qkv_ld, L, pos0, kv_stride, qn);
   const uint32_t pbase = window_lo(pos0, A.window);
   const int nchunk = (int)((pos0 + L - pbase + kScKC - 1) / kScKC);
   const int tps = (L + kAttnTQ - 1) / kAttnTQ;
@@ -889,7 +934,7 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
       cudaFuncSetAttribute(k_seq_pv_tile<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);             \
       init = true;                                                                                                   \
     }                                                                                                                \
-    k_seq_scores_tile<GG><<<sgrid, 256, ssm, st>>>(A, qn, L, pos0, kv_stride, pbase, scores, sstride);               \
+    launch_k(k_seq_scores_tile<GG>, dim3(sgrid), dim3(256), ssm, st, A, qn, L, pos0, kv_stride, pbase, scores, sstride);               \
   } while (0)
   switch (G) {
     case 1: F(1); break;
@@ -910,9 +955,9 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
     }
     const size_t es = ((size_t)sstride + 3) & ~(size_t)3;
     const int nw = (int)std::max<size_t>(1, std::min<size_t>(8, (size_t)(200 * 1024) / (es * 4)));
-    k_seq_softmax<<<(T * A.nh + nw - 1) / nw, nw * 32, (size_t)nw * es * 4, st>>>(A, T, L, pos0, scores, sstride);
+    launch_k(k_seq_softmax, dim3((T * A.nh + nw - 1) / nw), dim3(nw * 32), (size_t)nw * es * 4, st, A, T, L, pos0, scores, sstride);
   }
-#define P(GG) k_seq_pv_tile<GG><<<pgrid, pth, psm, st>>>(A, L, pos0, kv_stride, scores, sstride, threads, part)
+#define P(GG) launch_k(k_seq_pv_tile<GG>, dim3(pgrid), dim3(pth), psm, st, A, L, pos0, kv_stride, scores, sstride, threads, part)
   switch (G) {
     case 1: P(1); break;
     case 2: P(2); break;
@@ -924,12 +969,13 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
     default: P(8); break;
   }
 #undef P
-  k_seq_pv_combine<<<dim3(T, A.nh), A.hd, 0, st>>>(A, part, threads, aq, as);
+  launch_k(k_seq_pv_combine, dim3(dim3(T, A.nh)), dim3(A.hd), 0, st, A, part, threads, aq, as);
 }
 
 // Token ids and targets of a chunk: rows [seq][pos] read toks[seq * stride + c0 + pos] and the next id.
 __global__ void k_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin,
                                     uint32_t* tgt) {
+  pdl_wait();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const size_t i = (size_t)(t / L) * stride + c0 + t % L;
@@ -939,13 +985,13 @@ __global__ void k_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, 
 
 void launch_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0, int T, uint32_t* tin, uint32_t* tgt,
                               cudaStream_t st) {
-  k_seq_gather_tokens<<<(T + 255) / 256, 256, 0, st>>>(toks, stride, L, c0, T, tin, tgt);
+  launch_k(k_seq_gather_tokens, dim3((T + 255) / 256), dim3(256), 0, st, toks, stride, L, c0, T, tin, tgt);
 }
 
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st) {
   const long long tasks = (long long)T * (ff / 32);
   const int blocks = (int)std::min<long long>((tasks + 7) / 8, 1LL << 30);
-  k_seq_glu_quant<<<blocks, 256, 0, st>>>(gu, ff, T, silu, aq, as);
+  launch_k(k_seq_glu_quant, dim3(blocks), dim3(256), 0, st, gu, ff, T, silu, aq, as);
 }
 
 void launch_seq_class_logits(const float* A, const float* b, int k, const float* h, int d, int T, float* cl,
@@ -956,12 +1002,12 @@ void launch_seq_class_logits(const float* A, const float* b, int k, const float*
     init = true;
   }
   dim3 grid((T + 31) / 32, (k + 31) / 32);
-  k_seq_class_logits<<<grid, 256, (size_t)32 * d * 4, st>>>(A, b, k, h, d, T, cl);
+  launch_k(k_seq_class_logits, dim3(grid), dim3(256), (size_t)32 * d * 4, st, A, b, k, h, d, T, cl);
 }
 
 void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, float* lp, uint32_t* am, int* err,
                              cudaStream_t st) {
-  k_seq_logit_reduce<<<T, 1024, 0, st>>>(logits, V, targets, lp, am, err);
+  launch_k(k_seq_logit_reduce, dim3(T), dim3(1024), 0, st, logits, V, targets, lp, am, err);
 }
 
 }  // namespace gem
@@ -969,9 +1015,9 @@ void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* 
 namespace gem {
 void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
                                float* out, int* err, cudaStream_t st) {
-  k_seq_logit_partials<<<T, 1024, 0, st>>>(logits, V, row0, targets, vocab, out, err);
+  launch_k(k_seq_logit_partials, dim3(T), dim3(1024), 0, st, logits, V, row0, targets, vocab, out, err);
 }
 void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st) {
-  k_seq_logit_combine<<<(T + 127) / 128, 128, 0, st>>>(parts, nranks, T, lp, am);
+  launch_k(k_seq_logit_combine, dim3((T + 127) / 128), dim3(128), 0, st, parts, nranks, T, lp, am);
 }
 }  // namespace gem
