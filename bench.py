@@ -454,13 +454,17 @@ def token_roofline(g, info, mf, am_h, toks_h, ms_step, args, kind):
 
 
 def time_dev(torch, stream, fn, iters, flush):
+    """Mean device time of fn() over `iters` calls, each after an L2 flush. The flush runs on the timed
+    stream itself, so the host enqueues each call while the flush is still executing and the start
+    event marks the call's first kernel, not the host's launch latency."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
-    for a, b in evs:
-        flush.zero_()
-        torch.cuda.synchronize()
-        a.record(stream)
-        fn()
-        b.record(stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            fn()
+            b.record(stream)
     torch.cuda.synchronize()
     return sum(a.elapsed_time(b) for a, b in evs) / iters
 
@@ -517,7 +521,7 @@ def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
         lp = torch.empty(batch, device="cuda")
         am = torch.empty(batch, dtype=torch.int32, device="cuda")
         for name, fn in (("full", g.head_full_dev), ("two_level", g.head_twolevel_dev)):
-            call = lambda: fn(H.data_ptr(), T.data_ptr(), batch, lp.data_ptr(), am.data_ptr())
+            call = lambda: fn(H.data_ptr(), T.data_ptr(), batch, lp.data_ptr(), am.data_ptr(), sync=False)
             call()
             us = time_dev(torch, stream, call, 5, flush) * 1e3
             e = {"us": round(us, 2)}

@@ -201,10 +201,12 @@ int gem_shard_init(gem_model* m, int nranks, int rank, const void* id);
 /* y = layer matrix `which` of layer `layer` (0 q, 1 k, 2 v, 3 o, 4 gate, 5 up, 6 down; layer -1 = the
  * output matrix in token order) times x: x has cols floats, y rows floats. */
 int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float* y_dev);
-/* Full head for `batch` hidden states h_dev[batch][d] with targets_dev[batch]. */
+/* Full head for `batch` hidden states h_dev[batch][d] with targets_dev[batch]. Enqueued on the model's
+ * stream (gem_sync, or the stream from gem_get_stream, before reading the outputs); calls on one model
+ * share its head scratch in stream order. */
 int gem_head_full_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
                       float* logprob_dev, uint32_t* argmax_dev);
-/* Two-level head for `batch` hidden states. */
+/* Two-level head for `batch` hidden states; enqueued like gem_head_full_dev. */
 int gem_head_twolevel_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
                           float* logprob_dev, uint32_t* argmax_dev);
 /* gem_head_full_dev for callers that cannot allocate device memory when they call it (a process whose

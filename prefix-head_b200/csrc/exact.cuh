@@ -106,6 +106,7 @@ __device__ __forceinline__ float dot512_pair(const float* a, const float* b, int
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll 8
   for (int c = 0; c < n / 16; ++c) {
     const float4 a0 = *(const float4*)(a + c * 16 + half * 8), a1 = *(const float4*)(a + c * 16 + half * 8 + 4);
     const float4 b0 = *(const float4*)(b + c * 16 + half * 8), b1 = *(const float4*)(b + c * 16 + half * 8 + 4);

@@ -241,7 +241,8 @@ __global__ void k_tl_stage1_exact(TwoLevelArgs T) {
     float* sh = (float*)smem_raw;
     for (int j = threadIdx.x; j < d; j += blockDim.x) sh[j] = h[j];
     __syncthreads();
-    for (int base = (blockIdx.x * nw + warp) * 16; base < T.k; base += T.class_ctas * nw * 16) {
+    // task (warp w, CTA x) = w * class_ctas + x: the first class_ctas tasks land on distinct SMs
+    for (int base = (warp * T.class_ctas + (int)blockIdx.x) * 16; base < T.k; base += T.class_ctas * nw * 16) {
       int c = base + (lane >> 1);
       bool ok = c < T.k;
       float z = dot512_pair(T.A + (size_t)(ok ? c : 0) * d, sh, d, half);

@@ -133,6 +133,8 @@ struct gem_model {
   // heads
   int hbatch = 0;
   float *head_part = nullptr, *tlogit = nullptr, *cl = nullptr, *inner = nullptr;
+  int8_t* hb_q = nullptr;  // batched head calls: quantized hidden states [batch][d] and their scales
+  float* hb_s = nullptr;
   // two-level (main.rs:40-51)
   bool two = false;
   int k = 0, per = 0;
@@ -246,6 +248,8 @@ struct gem_model {
     int parts = head_full_parts(sms);
     head_part = alloc<float>((size_t)batch * parts * 4);
     tlogit = alloc<float>(batch);
+    hb_q = alloc<int8_t>((size_t)batch * d);
+    hb_s = alloc<float>((size_t)batch * d / 32);
     if (two) {
       cl = alloc<float>((size_t)batch * k);
       inner = alloc<float>((size_t)batch * per);
@@ -344,7 +348,7 @@ struct gem_model {
       launch_head_twolevel(T, batch, sms, st);
       return;
     }
-    int class_ctas = std::max(1, std::min(sms, (k + 127) / 128));
+    int class_ctas = std::max(1, std::min(sms, (k + 15) / 16));  // one 16-class task per CTA where possible
     int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
     T.class_ctas = class_ctas;
     launch_tl_stage1_exact(T, batch, class_ctas, block_ctas, st);
@@ -415,6 +419,12 @@ struct gem_model {
       run_head(0, s_haq, s_has, s_h, targets, T, lpo, amo);
       return 2;
     }
+    return full_head_gemm(s_haq, s_has, targets, T, lpo, amo);
+  }
+  // Full head for T quantized hidden states as exact matrix products over chunks of kHeadChunk
+  // positions (the output matrix read once per chunk), then log-sum-exp, argmax and the target logit
+  // per position. Returns the kernels launched.
+  int full_head_gemm(const int8_t* q, const float* s, const uint32_t* targets, int T, float* lpo, uint32_t* amo) {
     const int hc = std::min(T, kHeadChunk);
     if (hc > logits_cap) {
       s_logits = alloc<float>((size_t)hc * vocab);
@@ -423,7 +433,7 @@ struct gem_model {
     int launches = 0;
     for (int h0 = 0; h0 < T; h0 += hc) {
       const int n = std::min(hc, T - h0);
-      launch_seq_gemm(head.v, s_haq + (size_t)h0 * d, s_has + (size_t)h0 * d / 32, n, s_logits, vocab, sms, st);
+      launch_seq_gemm(head.v, q + (size_t)h0 * d, s + (size_t)h0 * d / 32, n, s_logits, vocab, sms, st);
       launch_seq_logit_reduce(s_logits, vocab, n, targets + h0, lpo + h0, amo ? amo + h0 : nullptr, err, st);
       launches += 2;
     }
@@ -1610,23 +1620,22 @@ int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float
   API_END
 }
 
+constexpr int kHeadGemmMin = 12;  // ~30 us per streamed state vs ~0.37 ms per 32-state product tile
 static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_t* targets_dev, int batch, float* lp_dev,
                       uint32_t* am_dev) {
   API_BEGIN
   if (!m || !h_dev || !targets_dev || batch <= 0) throw Error(GEM_E_ARG, "bad argument");
   if (which == 1 && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
   ck(cudaSetDevice(m->device), "cudaSetDevice");
-  m->ensure_head_batch(batch);
-  int8_t* q = m->alloc<int8_t>((size_t)batch * m->d);
-  float* s = m->alloc<float>((size_t)batch * m->d / 32);
-  launch_quantize(h_dev, batch * m->d, q, s, m->st);
-  m->run_head(which, q, s, h_dev, targets_dev, batch, lp_dev, am_dev);
+  m->ensure_head_batch(batch);  // the quantized hidden states live in the model's head scratch
+  launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
+  // from kHeadGemmMin hidden states on, the full head is cheaper as a matrix product (the output
+  // matrix read once per 256 states) than as one streamed pass over it per state
+  if (which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && seq_gemm_supported(m->head.v))
+    m->full_head_gemm(m->hb_q, m->hb_s, targets_dev, batch, lp_dev, am_dev);
+  else
+    m->run_head(which, m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   m->check_launch();
-  m->sync();
-  m->owned.pop_back();
-  m->owned.pop_back();
-  cudaFree(q);
-  cudaFree(s);
   API_END
 }
 

@@ -496,7 +496,7 @@ __global__ void k_seq_softmax(AttnArgs A, int T, int L, uint32_t pos0, float* sc
   const uint32_t pos = pos0 + t % L, lo = window_lo(pos, A.window);
   const int n = (int)(pos + 1 - lo);
   float* s = scores + (size_t)task * sstride;
-  float* e = ss + (size_t)warp * ((sstride + 3) & ~3);  // 16-byte aligned rows
+  float* e = ss + (size_t)warp * (((sstride + 3) & ~3) + 16);  // 16-byte aligned rows, 16 floats of slack for the prefetch
   for (int i = lane; i < n; i += 32) cp4(e + i, s + i, true);
   cp_commit();
   cp_wait<0>();
@@ -507,17 +507,22 @@ __global__ void k_seq_softmax(AttnArgs A, int T, int L, uint32_t pos0, float* sc
   for (int i = lane; i < n; i += 32) e[i] = exp_fast(sub(e[i], m));
   __syncwarp();
   float sum = 0.0f;
-  if (lane == 0) {
-    int i = 0;
-#pragma unroll 4
-    for (; i + 4 <= n; i += 4) {
-      const float4 v = *(const float4*)(e + i);
-      sum = add(sum, v.x);
-      sum = add(sum, v.y);
-      sum = add(sum, v.z);
-      sum = add(sum, v.w);
+  if (lane == 0) {  // in order; the next 16 values load while the current 16 are added
+    const int n16 = n & ~15;
+    const float4* p = (const float4*)e;
+    float4 a[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = p[u];  // a row has 16 floats of slack: loads past n are never added
+    for (int j = 0; j < n16; j += 16) {
+      float4 nx[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) nx[u] = p[j / 4 + 4 + u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) sum = add(add(add(add(sum, a[u].x), a[u].y), a[u].z), a[u].w);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = nx[u];
     }
-    for (; i < n; ++i) sum = add(sum, e[i]);
+    for (int i = n16; i < n; ++i) sum = add(sum, e[i]);
   }
   const float inv = div(1.0f, __shfl_sync(0xffffffffu, sum, 0));
   for (int i = lane; i < n; i += 32) s[i] = mul(e[i], inv);
@@ -534,7 +539,7 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
                                                      const float* scores, int sstride, int threads, float* part) {
   pdl_wait();
   constexpr int R = kAttnTQ * G;               // rows of the tile: position x head of the group
-  extern __shared__ __align__(16) float sv[];  // V [kPvRows][hd], then probabilities P [R][kPvRows]
+  extern __shared__ __align__(16) float sv[];  // V [kPvRows][hd], then probabilities P [kPvRows][R] (rows adjacent)
   __shared__ uint32_t s_lo[kAttnTQ], s_a[kAttnTQ], s_b[kAttnTQ];
   const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
   const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
@@ -562,9 +567,9 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
   for (int tt = 0; tt < tn; ++tt)
     if (s_a[tt] < s_b[tt]) ua = min(ua, s_a[tt]), ub = max(ub, s_b[tt]);
   for (int g = 0; g < A.nkv; ++g) {
-    float2 acc[R];  // columns j2, j2 + 1
+    float2 ac0[R / 2], ac1[R / 2];  // columns j2, j2 + 1: rows (2i, 2i + 1)
 #pragma unroll
-    for (int i = 0; i < R; ++i) acc[i] = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < R / 2; ++i) ac0[i] = ac1[i] = make_float2(0.0f, 0.0f);
     for (uint32_t c0 = ua; c0 < ub; c0 += kPvRows) {
       const int rows = (int)min((uint32_t)kPvRows, ub - c0), rows4 = (rows + 3) & ~3;
       __syncthreads();
@@ -578,29 +583,32 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
         const int row = i / kPvRows, pi = i % kPvRows, tt = row / G, h = row % G;
         const uint32_t p = c0 + pi;
         const bool ok = tt < tn && pi < rows && p >= s_a[tt] && p < s_b[tt];
-        cp4(sp + i, scores + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride + (p - s_lo[tt]) : 0), ok);
+        cp4(sp + pi * R + row, scores + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride + (p - s_lo[tt]) : 0), ok);
       }
       cp_commit();
       cp_wait<0>();
       __syncthreads();
-      for (int p4 = 0; p4 < rows4; p4 += 4) {
-        const float2 v0 = *(const float2*)(sv + (p4 + 0) * hd + j2), v1 = *(const float2*)(sv + (p4 + 1) * hd + j2);
-        const float2 v2 = *(const float2*)(sv + (p4 + 2) * hd + j2), v3 = *(const float2*)(sv + (p4 + 3) * hd + j2);
+      // per position: V's two columns duplicated once, then every pair of adjacent rows in one FMA each
+      for (int p = 0; p < rows; ++p) {
+        const float2 v = *(const float2*)(sv + p * hd + j2);
+        const float2 v0 = make_float2(v.x, v.x), v1 = make_float2(v.y, v.y);
+        const float* pp = sp + p * R;
 #pragma unroll
-        for (int i = 0; i < R; ++i) {
-          const float4 pp = *(const float4*)(sp + i * kPvRows + p4);
-          acc[i] = __ffma2_rn(make_float2(pp.x, pp.x), v0, acc[i]);
-          acc[i] = __ffma2_rn(make_float2(pp.y, pp.y), v1, acc[i]);
-          acc[i] = __ffma2_rn(make_float2(pp.z, pp.z), v2, acc[i]);
-          acc[i] = __ffma2_rn(make_float2(pp.w, pp.w), v3, acc[i]);
+        for (int i = 0; i < R; i += 4) {
+          const float4 q = *(const float4*)(pp + i);
+          ac0[i / 2] = __ffma2_rn(make_float2(q.x, q.y), v0, ac0[i / 2]);
+          ac0[i / 2 + 1] = __ffma2_rn(make_float2(q.z, q.w), v0, ac0[i / 2 + 1]);
+          ac1[i / 2] = __ffma2_rn(make_float2(q.x, q.y), v1, ac1[i / 2]);
+          ac1[i / 2 + 1] = __ffma2_rn(make_float2(q.z, q.w), v1, ac1[i / 2 + 1]);
         }
       }
     }
 #pragma unroll
     for (int i = 0; i < R; ++i) {
       const int tt = i / G, h = i % G;
+      const float2 o = (i & 1) ? make_float2(ac0[i / 2].y, ac1[i / 2].y) : make_float2(ac0[i / 2].x, ac1[i / 2].x);
       if (tt < tn)
-        *(float2*)(part + (((size_t)(t0 + tt) * A.nh + g * G + h) * threads + r) * hd + j2) = acc[i];
+        *(float2*)(part + (((size_t)(t0 + tt) * A.nh + g * G + h) * threads + r) * hd + j2) = o;
     }
   }
 }
@@ -953,7 +961,7 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
       cudaFuncSetAttribute(k_seq_softmax, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
       init = true;
     }
-    const size_t es = ((size_t)sstride + 3) & ~(size_t)3;
+    const size_t es = (((size_t)sstride + 3) & ~(size_t)3) + 16;  // the kernel's row stride
     const int nw = (int)std::max<size_t>(1, std::min<size_t>(8, (size_t)(200 * 1024) / (es * 4)));
     launch_k(k_seq_softmax, dim3((T * A.nh + nw - 1) / nw), dim3(nw * 32), (size_t)nw * es * 4, st, A, T, L, pos0, scores, sstride);
   }

@@ -328,11 +328,17 @@ class Gemma:
     def matvec_dev(self, layer: int, which: int, x_ptr: int, y_ptr: int):
         _check(lib().gem_matvec_dev(self._h, layer, which, x_ptr, y_ptr))
 
-    def head_full_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
+    def head_full_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int, sync: bool = True):
+        """Full head on device buffers; the C call is stream-ordered, `sync` waits for the results."""
         _check(lib().gem_head_full_dev(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
+        if sync:
+            self.sync()
 
-    def head_twolevel_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
+    def head_twolevel_dev(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int, sync: bool = True):
+        """Two-level head on device buffers; stream-ordered like head_full_dev."""
         _check(lib().gem_head_twolevel_dev(self._h, h_ptr, targets_ptr, batch, lp_ptr, am_ptr))
+        if sync:
+            self.sync()
 
     def head_full_noalloc(self, h_ptr: int, targets_ptr: int, batch: int, lp_ptr: int, am_ptr: int):
         """gem_head_full_dev without any device allocation (static scratch; asynchronous)."""
