@@ -91,6 +91,14 @@ __device__ __forceinline__ Best best_merge(Best a, Best b) {
 __device__ __forceinline__ float ld_scale(const __half* s, size_t i) { return __half2float(s[i]); }
 __device__ __forceinline__ float ld_scale(const float* s, size_t i) { return s[i]; }
 
+// Programmatic dependent launch: a kernel launched with launch_k may be scheduled while its
+// predecessor drains; its first action waits for the predecessor's completion and memory (a no-op when
+// launched without the attribute), so nothing reads a predecessor's output early.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ----- int8 block dot: 32 weights (two 16-byte words) against 32 activation bytes -----
 __device__ __forceinline__ int dot32_i8(int4 w0, int4 w1, const int4 a0, const int4 a1) {
   int s = 0;

@@ -88,6 +88,7 @@ __global__ void k_residual_norm_quant(float* x, const float* delta, const float*
 
 // Quantize an fp32 vector (Act::quantize) for the kernel-level entry points.
 __global__ void k_quantize(const float* x, int n, int8_t* aq, float* as) {
+  pdl_wait();
   int lane = threadIdx.x & 31;
   int warps = (blockDim.x >> 5) * gridDim.x;
   for (int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n / 32; b += warps)
@@ -408,6 +409,7 @@ __global__ void k_head_full(HeadArgs H) {
 }
 
 __global__ void k_head_full_merge(HeadArgs H, int nparts) {
+  pdl_wait();
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
   const int bi = blockIdx.x;
@@ -586,6 +588,7 @@ __global__ void k_tl_stage2(TwoLevelArgs T) {
 // maximum), target logprob (main.rs:101-107); argmax = best raw logit inside the top class block
 // (lean.rs:46-76 with top = 1), whose logits another kernel wrote to top_inner.
 __global__ void k_tl_select(TwoLevelArgs T, uint32_t* top_of) {
+  pdl_wait();
   __shared__ float rm[32], rs[32], rv[32];
   __shared__ uint32_t rc[32];
   __shared__ float s_lse_cl;
@@ -635,6 +638,7 @@ __global__ void k_tl_select(TwoLevelArgs T, uint32_t* top_of) {
 }
 
 __global__ void k_tl_argmax(TwoLevelArgs T, const uint32_t* top_of, const float* top_inner) {
+  pdl_wait();
   __shared__ float rv[32];
   __shared__ uint32_t rj[32];
   const int bi = blockIdx.x;
@@ -687,7 +691,7 @@ void launch_residual_norm_quant(float* x, const float* delta, const float* w_pos
 }
 void launch_quantize(const float* x, int n, int8_t* aq, float* as, cudaStream_t st) {
   int blocks = (n / 32 + 7) / 8;
-  k_quantize<<<blocks, 256, 0, st>>>(x, n, aq, as);
+  launch_k(k_quantize, dim3(blocks), dim3(256), 0, st, x, n, aq, as);
 }
 void launch_gemv(const MatView& w, const int8_t* aq, const float* as, const float* x, float* y, int sms, cudaStream_t st) {
   const int threads = 256, nw = threads / 32;
@@ -738,14 +742,14 @@ void launch_head_full(const HeadArgs& H, int batch, int sms, cudaStream_t st) {
 }
 
 void launch_head_full_merge(const HeadArgs& H, int batch, int parts, cudaStream_t st) {
-  k_head_full_merge<<<batch, 256, 0, st>>>(H, parts);
+  launch_k(k_head_full_merge, dim3(batch), dim3(256), 0, st, H, parts);
 }
 
 void launch_tl_select(const TwoLevelArgs& T, int batch, uint32_t* top_of, cudaStream_t st) {
-  k_tl_select<<<batch, 256, 0, st>>>(T, top_of);
+  launch_k(k_tl_select, dim3(batch), dim3(256), 0, st, T, top_of);
 }
 void launch_tl_argmax(const TwoLevelArgs& T, int batch, const uint32_t* top_of, const float* top_inner, cudaStream_t st) {
-  k_tl_argmax<<<batch, 256, 0, st>>>(T, top_of, top_inner);
+  launch_k(k_tl_argmax, dim3(batch), dim3(256), 0, st, T, top_of, top_inner);
 }
 
 void launch_head_twolevel(const TwoLevelArgs& T, int batch, int sms, cudaStream_t st) {

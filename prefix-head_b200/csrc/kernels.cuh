@@ -113,6 +113,13 @@ void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, 
                        cudaStream_t st);
 void launch_end_step(uint32_t* step, cudaStream_t st);
 int head_full_parts(int sms);
+// Full head streamed through shared memory for Q8_0 output matrices with f16 scales: the matrix's GEMV
+// copy ([16-row group][block][row][32 B] quants, [group][block][16] scales) and the launcher (batch items
+// in blockIdx.y, partials merged as for launch_head_full_exact).
+bool head_bulk_supported(const MatView& w);
+size_t head_bulk_bytes(const MatView& w);
+void launch_head_bulk_layout(const MatView& w, unsigned char* wq, __half* ws, cudaStream_t st);
+void launch_head_full_bulk(const HeadArgs& H, const unsigned char* wq, const __half* ws, int batch, int sms, cudaStream_t st);
 void launch_head_full(const HeadArgs& H, int batch, int sms, cudaStream_t st);
 void launch_head_twolevel(const TwoLevelArgs& T, int batch, int sms, cudaStream_t st);
 void launch_head_full_merge(const HeadArgs& H, int batch, int parts, cudaStream_t st);
@@ -164,5 +171,24 @@ void launch_seq_class_logits(const float* A, const float* b, int k, const float*
                              cudaStream_t st);
 void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, float* lp, uint32_t* am, int* err,
                              cudaStream_t st);
+
+#ifdef __CUDACC__
+// Launches `k` with programmatic stream serialization (see pdl_wait); GEM_PDL=0 turns it off.
+bool pdl_on();
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  if (!pdl_on()) {
+    k<<<grid, block, smem, st>>>(args...);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid, cfg.blockDim = block, cfg.dynamicSmemBytes = smem, cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at, cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, args...);
+}
+#endif
 
 }  // namespace gem

@@ -13,6 +13,7 @@
 //   - rmsnorm / softmax sums: sequential fp32 additions (Rust's Iterator::sum), one thread.
 //   - P.V: the pool's per-thread position ranges, FMA per element (axpy512), partials summed in
 //     thread order.
+#include <algorithm>
 #include "kernels.cuh"
 #include "exact.cuh"
 
@@ -228,10 +229,179 @@ __global__ void k_head_full_exact(HeadArgs H) {
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Full head streamed through shared memory (Q8_0 output matrix with f16 scales, a few hidden states).
+// The matrix's GEMV copy is laid out [16-row group][block][row][32 bytes], its scales [group][block][16
+// rows], so G consecutive groups (a stage) are two contiguous bulk copies, and a warp reads one block
+// of its 16 rows as 512 contiguous bytes. NS stages per CTA: the next lands while one is used. A
+// thread pair takes a row, lanes 0-7 / 8-15, with row_dot_exact's additions in row_dot_exact's order.
+// ------------------------------------------------------------------------------------------------
+namespace {
+__device__ __forceinline__ unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool hb_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  unsigned long long t0 = 0;
+  for (int i = 0;; ++i) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(done) : "r"(a), "r"(parity) : "memory");
+    if (done) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    if (i == 0) t0 = t;
+    else if (t - t0 > 1000000000ull) return false;  // 1 s: the copy never landed
+  }
+}
+__device__ __forceinline__ void hb_issue(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+}  // namespace
+
+__global__ void k_head_bulk_layout(MatView w, unsigned char* wq, __half* ws) {
+  const int nb = w.cols / 32, ng = (w.rows + 15) / 16;
+  const size_t n = (size_t)ng * nb * 16 * 2;  // 16-byte pieces: (group, block, row, half)
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int h = (int)(i & 1), row = (int)((i >> 1) & 15);
+    const size_t gb = i >> 5;
+    const int b = (int)(gb % nb), g = (int)(gb / nb), r = g * 16 + row;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (r < w.rows) v = *(const int4*)((const int8_t*)w.q + (size_t)r * w.cols + b * 32 + h * 16);
+    *(int4*)(wq + i * 16) = v;
+    if (h == 0) ws[gb * 16 + row] = r < w.rows ? ((const __half*)w.s)[(size_t)r * nb + b] : __float2half(0.0f);
+  }
+}
+
+template <int G, int NS>
+__global__ void __launch_bounds__(G * 32) k_head_full_bulk(HeadArgs H, const unsigned char* __restrict__ wq,
+                                                          const __half* __restrict__ wsc, int ng) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  __shared__ __align__(8) uint64_t full[NS];
+  __shared__ float red_m[32], red_s[32], red_v[32];
+  __shared__ uint32_t red_t[32];
+  const MatView& w = H.w;
+  const int bi = blockIdx.y, nb = w.cols / 32;
+  const size_t qst = (size_t)G * nb * 512, sst = (size_t)G * nb * 32;  // one stage's quants and scales
+  int8_t* saq = (int8_t*)sm;
+  float* sas = (float*)(sm + w.cols);
+  unsigned char* buf = sm + ((w.cols + nb * 4 + 127) & ~127);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane & 1;
+  const int nst = (ng + G - 1) / G;
+  auto issue = [&](int s, int k) {  // stage s into buffer k
+    const int gc = min(G, ng - s * G);
+    unsigned char* q = buf + (size_t)k * (qst + sst);
+    const uint32_t qb = (uint32_t)gc * nb * 512, sb = (uint32_t)gc * nb * 32;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[k])), "r"(qb + sb) : "memory");
+    hb_issue(q, wq + (size_t)s * qst, qb, &full[k]);
+    hb_issue(q + qst, wsc + (size_t)s * G * nb * 16, sb, &full[k]);
+  };
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < NS; ++k) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[k])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)  // the output matrix depends on no earlier kernel: its first stages load during the wait
+    for (int k = 0; k < NS; ++k)
+      if ((int)(blockIdx.x + k * gridDim.x) < nst) issue(blockIdx.x + k * gridDim.x, k);
+  pdl_wait();
+  for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)(H.aq + (size_t)bi * w.cols))[j];
+  for (int j = threadIdx.x; j < nb; j += blockDim.x) sas[j] = H.as[(size_t)bi * nb + j];
+  __syncthreads();
+  uint32_t target = H.targets ? H.targets[bi] : H.cur->target;
+  if (target >= (uint32_t)w.rows) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(H.err, ERR_RANGE);
+    target = 0;
+  }
+  const uint32_t trow = H.row_of ? H.row_of[target] : target;
+  Lse L{-INFINITY, 0.0f};
+  Best B{-INFINITY, 0xffffffffu};
+  bool ok = true;
+  int i = 0;
+  for (int s = blockIdx.x; s < nst && ok; s += gridDim.x, ++i) {
+    const int k = i % NS;
+    ok = hb_wait(&full[k], (uint32_t)((i / NS) & 1));
+    if (!ok) {
+      if (lane == 0) atomicExch(H.err, ERR_TIMEOUT);
+      break;
+    }
+    const int g = s * G + warp;
+    if (g < ng) {
+      const unsigned char* q = buf + (size_t)k * (qst + sst) + (size_t)warp * nb * 512 + (lane >> 1) * 32 + half * 16;
+      const __half* sc = (const __half*)(buf + (size_t)k * (qst + sst) + qst) + (size_t)warp * nb * 16 + (lane >> 1);
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll 4
+      for (int b = 0; b < nb; ++b)
+        block_fma(acc, *(const int4*)(q + (size_t)b * 512), *(const int4*)(saq + b * 32 + half * 16),
+                  mul(__half2float(sc[b * 16]), sas[b]));
+      const float z = reduce16_pair(acc);
+      const int r = g * 16 + (lane >> 1);
+      if (r < w.rows && half == 0) {
+        const uint32_t tok = H.row_tok ? H.row_tok[r] : (uint32_t)r;
+        L = lse_add(L, z);
+        B = best_merge(B, Best{z, tok});
+        if ((uint32_t)r == trow) H.tlogit[bi] = z;
+      }
+    }
+    __syncthreads();  // every warp is done with buffer k
+    if (threadIdx.x == 0 && s + NS * (int)gridDim.x < nst) issue(s + NS * gridDim.x, k);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
+    Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
+    L = lse_merge(L, l2);
+    B = best_merge(B, b2);
+  }
+  if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int j = 1; j < G; ++j) {
+      L = lse_merge(L, Lse{red_m[j], red_s[j]});
+      B = best_merge(B, Best{red_v[j], red_t[j]});
+    }
+    float4* p = (float4*)(H.part + ((size_t)bi * gridDim.x + blockIdx.x) * 4);
+    *p = make_float4(L.m, L.s, B.v, __uint_as_float(B.tok));
+  }
+}
+
+// rows of a stage in 16-row groups (one warp each), two stages: G * 2 * nb * 544 bytes <= ~200 KB
+static int head_bulk_groups(int nb) { return nb * 544 * 8 * 2 <= 196 * 1024 ? 8 : 4; }
+
+size_t head_bulk_bytes(const MatView& w) {
+  const size_t ng = ((size_t)w.rows + 15) / 16, nb = w.cols / 32;
+  return ng * nb * 512 + ng * nb * 32;
+}
+bool head_bulk_supported(const MatView& w) {
+  const int nb = w.cols / 32;
+  return w.bits == 8 && !w.scale_f32 && w.cols % 32 == 0 && (size_t)head_bulk_groups(nb) * nb * 544 * 2 + w.cols * 2 + 256 <= 200 * 1024;
+}
+void launch_head_bulk_layout(const MatView& w, unsigned char* wq, __half* ws, cudaStream_t st) {
+  k_head_bulk_layout<<<1184, 256, 0, st>>>(w, wq, ws);
+}
+void launch_head_full_bulk(const HeadArgs& H, const unsigned char* wq, const __half* ws, int batch, int sms, cudaStream_t st) {
+  const int nb = H.w.cols / 32, ng = (H.w.rows + 15) / 16, G = head_bulk_groups(nb);
+  const int nst = (ng + G - 1) / G, ctas = std::min(nst, std::min(sms, head_full_parts(sms)));
+  const size_t sm = (size_t)((H.w.cols + nb * 4 + 127) & ~127) + (size_t)2 * G * nb * 544;
+  dim3 grid(ctas, batch);
+  if (G == 8) {
+    static bool init = false;
+    if (!init) { cudaFuncSetAttribute(k_head_full_bulk<8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); init = true; }
+    launch_k(k_head_full_bulk<8, 2>, grid, dim3(256), sm, st, H, wq, ws, ng);
+  } else {
+    static bool init = false;
+    if (!init) { cudaFuncSetAttribute(k_head_full_bulk<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); init = true; }
+    launch_k(k_head_full_bulk<4, 2>, grid, dim3(128), sm, st, H, wq, ws, ng);
+  }
+  launch_head_full_merge(H, batch, ctas, st);
+}
+
 // Two-level stage 1, exact: class logits dot512(A[c], h) + b[c] (main.rs:82-93) and the target
 // class's block rows.
 template <int BITS, typename ST>
 __global__ void k_tl_stage1_exact(TwoLevelArgs T) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int bi = blockIdx.y;
   const int d = T.w.cols;
@@ -277,6 +447,7 @@ __global__ void k_tl_stage1_exact(TwoLevelArgs T) {
 // Stage 2 reuses the fast kernel's logic but recomputes the top class block with exact rows.
 template <int BITS, typename ST>
 __global__ void k_tl_top_exact(TwoLevelArgs T, const uint32_t* top_of, float* top_inner) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int bi = blockIdx.y;
   const int d = T.w.cols;
@@ -372,7 +543,7 @@ void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, in
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_tl_stage1_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_tl_stage1_exact<B, S><<<grid, 256, sm, st>>>(T);                                              \
+    launch_k(k_tl_stage1_exact<B, S>, grid, dim3(256), sm, st, T);                                  \
   } while (0)
   GEM_DISPATCH_X(T.w.bits, T.w.scale_f32, F);
 #undef F
@@ -386,7 +557,7 @@ void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_o
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_tl_top_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_tl_top_exact<B, S><<<grid, 128, sm, st>>>(T, top_of, top_inner);                              \
+    launch_k(k_tl_top_exact<B, S>, grid, dim3(128), sm, st, T, top_of, top_inner);                  \
   } while (0)
   GEM_DISPATCH_X(T.w.bits, T.w.scale_f32, F);
 #undef F

@@ -116,6 +116,8 @@ struct gem_model {
   size_t body_bytes = 0;
   std::vector<Layer> layers;
   DevMat head, emb;  // emb used only when the file has a separate output matrix
+  unsigned char* head_bulk_q = nullptr;  // the output matrix's GEMV copy for the streamed full head, built on first use
+  __half* head_bulk_s = nullptr;
   float* out_norm = nullptr;
   float *rope_sin[2] = {nullptr, nullptr}, *rope_cos[2] = {nullptr, nullptr};
   float *kc = nullptr, *vc = nullptr;  // [seq][layer][ctx][nkv*hd]
@@ -339,8 +341,13 @@ struct gem_model {
     ensure_head_batch(batch);
     if (which == 0) {
       HeadArgs H = head_args(qa, sa, hh, targets, lpo, amo);
-      if (exact) launch_head_full_exact(H, batch, sms, st);
-      else launch_head_full(H, batch, sms, st);
+      if (exact && head_bulk_q) {
+        launch_head_full_bulk(H, head_bulk_q, head_bulk_s, batch, sms, st);
+      } else if (exact) {
+        launch_head_full_exact(H, batch, sms, st);
+      } else {
+        launch_head_full(H, batch, sms, st);
+      }
       return;
     }
     TwoLevelArgs T = tl_args(qa, sa, hh, targets, lpo, amo);
@@ -886,6 +893,13 @@ void load_model(gem_model* m, const Gguf& g, int body_bits, int head_bits) {
   else if (head_bits != 0) throw Error(GEM_E_ARG, "head_bits must be 0, 4 or 8");
   if (body_bits != 8 && body_bits != 4) throw Error(GEM_E_ARG, "body_bits must be 8 or 4");
   m->head = upload_mat(head, m->owned);
+  if (head_bulk_supported(m->head.v)) {  // the streamed full head's copy, built once (never during a capture)
+    const size_t ng = ((size_t)m->head.v.rows + 15) / 16, nb = m->head.v.cols / 32;
+    m->head_bulk_q = m->alloc<unsigned char>(ng * nb * 512);
+    m->head_bulk_s = m->alloc<__half>(ng * nb * 16);
+    launch_head_bulk_layout(m->head.v, m->head_bulk_q, m->head_bulk_s, 0);
+    ck(cudaStreamSynchronize(0), "head layout");  // done before any use on the model's (non-blocking) stream
+  }
   m->vocab = (int)head.rows;
   m->head_bits = head.bits;
   if (head.cols != (size_t)m->d) throw Error(GEM_E_FORMAT, "output matrix width != embedding_length");

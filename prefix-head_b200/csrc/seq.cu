@@ -49,14 +49,6 @@ __host__ __device__ __forceinline__ uint32_t window_lo(uint32_t pos, int window)
   return (window > 0 && pos + 1 > (uint32_t)window) ? pos + 1 - window : 0;
 }
 
-// Programmatic dependent launch: every kernel of this file is launched so that the next one may be
-// scheduled while it drains, and each kernel's first action waits for its predecessor's completion and
-// memory (a no-op when launched without the attribute), so nothing reads a predecessor's output early.
-__device__ __forceinline__ void pdl_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------
@@ -823,27 +815,12 @@ __global__ void k_seq_logit_combine(const float* parts, int nranks, int T, float
   } while (0)
 
 
-// Launches `k` with programmatic stream serialization (see pdl_wait); GEM_PDL=0 turns it off.
-static bool pdl_on() {
+bool pdl_on() {
   static const bool on = [] {
     const char* e = std::getenv("GEM_PDL");
     return !(e && e[0] == '0');
   }();
   return on;
-}
-template <typename... KArgs, typename... Args>
-static void launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
-  if (!pdl_on()) {
-    k<<<grid, block, smem, st>>>(args...);
-    return;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid, cfg.blockDim = block, cfg.dynamicSmemBytes = smem, cfg.stream = st;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at, cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, float scale, float* x, int* err,
