@@ -280,3 +280,27 @@ def test_qwen2_forward_bit_exact(torch, isa, small_qwen2):
     o = orc.Model(small_qwen2.gguf, ctx=64, threads=REF_THREADS, isa="avx512")
     for i, t in enumerate(synth.tokens(20, g.vocab, seed=78)):
         assert np.array_equal(g.forward(int(t), i).view(np.uint32), o.forward(int(t), i).view(np.uint32)), i
+
+
+@pytest.mark.parametrize("batch", [1, 3, 13])
+def test_head_full_partial_row_groups(torch, isa, threads, tmp_path, batch):
+    """An output matrix whose rows fill neither 16-row groups nor 8-group stages (1000 rows): the
+    streamed full head (batches below 12) reads a short last stage and a half-filled last group, the
+    matrix-product path (12 and more) a partial row tile; both against the oracle."""
+    cfg = dict(synth.SMALL, vocab=1000, layers=1)
+    path = synth.write_model(tmp_path / "v1000.gguf", cfg, seed=5)
+    g = Gemma(path, ctx=64)
+    o = orc.Model(path, ctx=64, threads=threads, isa="avx512")
+    rng = np.random.default_rng(70 + batch)
+    H = rng.standard_normal((batch, g.d)).astype(np.float32)
+    T = rng.integers(0, g.vocab, batch).astype(np.uint32)
+    Hd, Td = torch.tensor(H, device="cuda"), torch.tensor(T.astype(np.int32), device="cuda")
+    lp = torch.empty(batch, device="cuda")
+    am = torch.empty(batch, dtype=torch.int32, device="cuda")
+    g.head_full_dev(Hd.data_ptr(), Td.data_ptr(), batch, lp.data_ptr(), am.data_ptr())
+    lp, am = lp.cpu().numpy(), am.cpu().numpy().astype(np.uint32)
+    for b in range(batch):
+        want = o.full(H[b], int(T[b]))
+        assert abs(lp[b] - want[0]) < 2e-5, (b, lp[b], want[0])
+        assert am[b] == want[1], b
+    g.close()
