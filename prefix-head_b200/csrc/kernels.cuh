@@ -146,6 +146,10 @@ void launch_seq_norm(float* x, const float* delta, const float* w_post, const fl
 bool seq_gemm_supported(const MatView& w);
 void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
                      cudaStream_t st);
+// Full-head logits y[p][r] (p < T, row stride ldy) of an F16 output matrix against fp32 hidden states
+// x [T][cols], each the exact dot16; needs cols a multiple of 16 and a 16-byte aligned matrix.
+bool seq_head_f16_supported(const MatView& w);
+void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int ldy, cudaStream_t st);
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
                      float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
                      cudaStream_t st);

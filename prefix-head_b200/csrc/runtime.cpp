@@ -422,25 +422,33 @@ struct gem_model {
       return 5;
     }
     if (comm) return seq_head_sharded(targets, T, lpo, amo);
-    if (!seq_gemm_supported(head.v)) {  // F16 output matrix: the per-position exact head kernels
+    if (!full_head_gemm_supported()) {  // the per-position exact head kernels
       run_head(0, s_haq, s_has, s_h, targets, T, lpo, amo);
       return 2;
     }
-    return full_head_gemm(s_haq, s_has, targets, T, lpo, amo);
+    return full_head_gemm(s_haq, s_has, s_h, targets, T, lpo, amo);
   }
-  // Full head for T quantized hidden states as exact matrix products over chunks of kHeadChunk
-  // positions (the output matrix read once per chunk), then log-sum-exp, argmax and the target logit
-  // per position. Returns the kernels launched.
-  int full_head_gemm(const int8_t* q, const float* s, const uint32_t* targets, int T, float* lpo, uint32_t* amo) {
+  // Whether the full head has a matrix-product path: Q8_0/Q4_0 output matrices against the quantized
+  // hidden states, F16 ones against the fp32 hidden states.
+  bool full_head_gemm_supported() const { return seq_gemm_supported(head.v) || seq_head_f16_supported(head.v); }
+  // Full head for T hidden states (quantized q, s; fp32 h) as exact matrix products over chunks of
+  // kHeadChunk positions (the output matrix read once per chunk), then log-sum-exp, argmax and the
+  // target logit per position. Returns the kernels launched.
+  int full_head_gemm(const int8_t* q, const float* s, const float* h, const uint32_t* targets, int T, float* lpo,
+                     uint32_t* amo) {
     const int hc = std::min(T, kHeadChunk);
     if (hc > logits_cap) {
       s_logits = alloc<float>((size_t)hc * vocab);
       logits_cap = hc;
     }
+    const bool f16 = !seq_gemm_supported(head.v);
     int launches = 0;
     for (int h0 = 0; h0 < T; h0 += hc) {
       const int n = std::min(hc, T - h0);
-      launch_seq_gemm(head.v, q + (size_t)h0 * d, s + (size_t)h0 * d / 32, n, s_logits, vocab, sms, st);
+      if (f16)
+        launch_seq_head_f16(head.v, h + (size_t)h0 * d, n, s_logits, vocab, st);
+      else
+        launch_seq_gemm(head.v, q + (size_t)h0 * d, s + (size_t)h0 * d / 32, n, s_logits, vocab, sms, st);
       launch_seq_logit_reduce(s_logits, vocab, n, targets + h0, lpo + h0, amo ? amo + h0 : nullptr, err, st);
       launches += 2;
     }
@@ -1645,8 +1653,8 @@ static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_
   launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
   // from kHeadGemmMin hidden states on, the full head is cheaper as a matrix product (the output
   // matrix read once per 256 states) than as one streamed pass over it per state
-  if (which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && seq_gemm_supported(m->head.v))
-    m->full_head_gemm(m->hb_q, m->hb_s, targets_dev, batch, lp_dev, am_dev);
+  if (which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && m->full_head_gemm_supported())
+    m->full_head_gemm(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   else
     m->run_head(which, m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   m->check_launch();

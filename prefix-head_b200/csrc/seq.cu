@@ -363,6 +363,39 @@ __global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, int L,
                   qn + (size_t)t * A.nh * A.hd, smp, s_r);
 }
 
+// The halving reduction of dot512 (lane i + lane i + 8, then + 4, + 2, + 1) over a quad of threads:
+// thread u holds lanes 4u .. 4u + 3 of a block of 4 rows x 4 columns as
+// acc[row][column][(4u, 4u + 1), (4u + 2, 4u + 3)] and returns row u's 4 columns in res.
+__device__ __forceinline__ void quad_reduce16(const float2 (&acc)[4][4][2], int u, float (&res)[4]) {
+  // Round 1 (partner u ^ 2 holds lanes i + 8): threads 0, 1 keep rows 0, 1 and threads 2, 3 rows 2, 3;
+  // b = lane i + lane i + 8 for i = 4 (u & 1) + j.
+  float b[2][4][4];  // [kept row][column][j]
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float l[4] = {acc[m][k][0].x, acc[m][k][0].y, acc[m][k][1].x, acc[m][k][1].y};
+      const float h[4] = {acc[m + 2][k][0].x, acc[m + 2][k][0].y, acc[m + 2][k][1].x, acc[m + 2][k][1].y};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float got = __shfl_xor_sync(0xffffffffu, u < 2 ? h[j] : l[j], 2);
+        b[m][k][j] = add(u < 2 ? l[j] : h[j], got);
+      }
+    }
+  // Round 2 (partner u ^ 1 holds i + 4): even threads keep row 0 of their pair of rows, odd row 1;
+  // c = b_i + b_i+4 for i = j, then (c0 + c2) + (c1 + c3).
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float cc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float got = __shfl_xor_sync(0xffffffffu, (u & 1) ? b[0][k][j] : b[1][k][j], 1);
+      cc[j] = add((u & 1) ? b[1][k][j] : b[0][k][j], got);
+    }
+    res[k] = add(add(cc[0], cc[2]), add(cc[1], cc[3]));
+  }
+}
+
 // Tiled scores: a CTA takes kAttnTQ consecutive positions (R = kAttnTQ * G rows: position x query head
 // of kv group blockIdx.z) against kScKC key positions from pbase + blockIdx.y * kScKC, both staged in
 // shared memory (rows padded to hd + 4 floats, so 8 consecutive rows start in distinct banks), each
@@ -435,34 +468,8 @@ __global__ void __launch_bounds__(256, 2) k_seq_scores_tile(AttnArgs A0, const f
           acc[r][k][1] = __ffma2_rn(make_float2(qv[r].z, qv[r].w), make_float2(kv[k].z, kv[k].w), acc[r][k][1]);
         }
     }
-    // Round 1 (partner u ^ 2 holds lanes i + 8): threads 0, 1 keep rows 0, 1 and threads 2, 3 rows 2, 3;
-    // b = lane i + lane i + 8 for i = 4 (u & 1) + j.
-    float b[2][4][4];  // [kept row][key][j]
-#pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float l[4] = {acc[m][k][0].x, acc[m][k][0].y, acc[m][k][1].x, acc[m][k][1].y};
-        const float h[4] = {acc[m + 2][k][0].x, acc[m + 2][k][0].y, acc[m + 2][k][1].x, acc[m + 2][k][1].y};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float got = __shfl_xor_sync(0xffffffffu, u < 2 ? h[j] : l[j], 2);
-          b[m][k][j] = add(u < 2 ? l[j] : h[j], got);
-        }
-      }
-    // Round 2 (partner u ^ 1 holds i + 4): even threads keep row 0 of their pair of rows, odd row 1;
-    // c = b_i + b_i+4 for i = j, then (c0 + c2) + (c1 + c3).
     float res[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float cc[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float got = __shfl_xor_sync(0xffffffffu, (u & 1) ? b[0][k][j] : b[1][k][j], 1);
-        cc[j] = add((u & 1) ? b[1][k][j] : b[0][k][j], got);
-      }
-      res[k] = add(add(cc[0], cc[2]), add(cc[1], cc[3]));
-    }
+    quad_reduce16(acc, u, res);
     const int row = r0 + u, tt = row / G, h = row % G;  // thread u finishes row r0 + u, keys k0 .. k0 + 3
     if (tt < tn) {
       const uint32_t pos = pos0 + t0 + tt, lo = window_lo(pos, A.window);
@@ -843,6 +850,107 @@ void launch_seq_norm(float* x, const float* delta, const float* w_post, const fl
                                                                               xn_out);
 }
 
+// Full head over an F16 output matrix for T positions, exact: y[p][r] = dot16 (q8.rs:358-369) of row r,
+// each f16 weight converted to fp32, with the fp32 hidden state of position p -- lane i sums
+// w[16c+i] * x[16c+i] by FMA in order of c, then the halving reduction. A CTA takes kH16Rows rows x
+// kH16Pos positions in stages of kH16Kc columns, double-buffered: the weights pass through registers
+// (converted once per CTA and stored as fp32 rows), the hidden states arrive by asynchronous copies.
+// Warp w computes rows 8 (w % 8) .. + 8 and positions 16 (w / 8) .. + 16 with the quad tile of the
+// scores kernel (thread u of a quad holds lanes 4u .. 4u + 3 of 4 rows x 4 positions).
+constexpr int kH16Rows = 64, kH16Pos = 32, kH16Kc = 128, kH16Stride = kH16Kc + 4, kH16Threads = 512;
+constexpr size_t kH16Smem = (size_t)2 * (kH16Rows + kH16Pos) * kH16Stride * 4;
+
+__global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w, int rows, int d, const float* x, int T,
+                                                                  float* y, int ldy) {
+  pdl_wait();
+  extern __shared__ __align__(16) float sm[];
+  float* sw = sm;                                // [2][kH16Rows][kH16Stride]
+  float* sx = sm + 2 * kH16Rows * kH16Stride;    // [2][kH16Pos][kH16Stride]
+  const int tid = threadIdx.x, r0 = blockIdx.y * kH16Rows, p0 = blockIdx.x * kH16Pos;
+  const int nk = (d + kH16Kc - 1) / kH16Kc;
+  // staging: thread t copies halves 8 (t % 16) .. + 8 of rows t / 16 and t / 16 + 32, and floats
+  // 4 (t % 16) .. + 4 and + 64 .. of position t / 16, of each stage
+  const int sr = tid >> 4, sc = (tid & 15) * 8, xc = (tid & 15) * 4;
+  const bool ok0 = r0 + sr < rows, ok1 = r0 + sr + 32 < rows, okx = p0 + sr < T;
+  const int4* w0 = (const int4*)(w + (size_t)(ok0 ? r0 + sr : 0) * d);
+  const int4* w1 = (const int4*)(w + (size_t)(ok1 ? r0 + sr + 32 : 0) * d);
+  const float* xs = x + (size_t)(okx ? p0 + sr : 0) * d;
+  int4 wv[2];
+  auto load_w = [&](int kc) {
+    const int c = kc * kH16Kc + sc;  // d is a multiple of 16: an 8-half piece is whole or outside
+    wv[0] = ok0 && c < d ? ldg_stream(w0 + c / 8) : make_int4(0, 0, 0, 0);
+    wv[1] = ok1 && c < d ? ldg_stream(w1 + c / 8) : make_int4(0, 0, 0, 0);
+  };
+  auto store_w = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __half2* h2 = (const __half2*)&wv[h];
+      const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]), f2 = __half22float2(h2[2]),
+                   f3 = __half22float2(h2[3]);
+      float* dst = sw + (buf * kH16Rows + sr + 32 * h) * kH16Stride + sc;
+      *(float4*)dst = make_float4(f0.x, f0.y, f1.x, f1.y);
+      *(float4*)(dst + 4) = make_float4(f2.x, f2.y, f3.x, f3.y);
+    }
+  };
+  auto load_x = [&](int kc, int buf) {
+    float* dst = sx + (buf * kH16Pos + sr) * kH16Stride + xc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = kc * kH16Kc + xc + 64 * h;
+      const bool ok = okx && c < d;
+      cp16(dst + 64 * h, xs + (ok ? c : 0), ok);
+    }
+  };
+  load_w(0);
+  load_x(0, 0);
+  cp_commit();
+  store_w(0);
+  const int lane = tid & 31, warp = tid >> 5, u = lane & 3, qd = lane >> 2, rg = qd >> 2, kg = qd & 3;
+  const int tr = (warp & 7) * 8 + rg * 4, tp = (warp >> 3) * 16 + kg * 4;
+  float2 acc[4][4][2];  // [row][position][lanes (4u, 4u + 1), (4u + 2, 4u + 3)]
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[r][k][0] = acc[r][k][1] = make_float2(0.0f, 0.0f);
+  for (int kc = 0; kc < nk; ++kc) {
+    const int buf = kc & 1;
+    cp_wait<0>();
+    __syncthreads();  // stage kc is in place; every warp is done with stage kc - 1's buffers
+    if (kc + 1 < nk) {
+      load_w(kc + 1);
+      load_x(kc + 1, buf ^ 1);
+      cp_commit();
+    }
+    const float* qp = sw + (buf * kH16Rows + tr) * kH16Stride + 4 * u;
+    const float* kp = sx + (buf * kH16Pos + tp) * kH16Stride + 4 * u;
+    const int nc = min(kH16Kc, d - kc * kH16Kc) / 16;
+#pragma unroll 2
+    for (int c = 0; c < nc; ++c) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qv[r] = *(const float4*)(qp + r * kH16Stride + 16 * c);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) kv[k] = *(const float4*)(kp + k * kH16Stride + 16 * c);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[r][k][0] = __ffma2_rn(make_float2(qv[r].x, qv[r].y), make_float2(kv[k].x, kv[k].y), acc[r][k][0]);
+          acc[r][k][1] = __ffma2_rn(make_float2(qv[r].z, qv[r].w), make_float2(kv[k].z, kv[k].w), acc[r][k][1]);
+        }
+    }
+    if (kc + 1 < nk) store_w(buf ^ 1);
+  }
+  float res[4];
+  quad_reduce16(acc, u, res);
+  const int row = r0 + tr + u;  // thread u finishes row tr + u, positions tp .. tp + 3
+  if (row < rows) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (p0 + tp + k < T) y[(size_t)(p0 + tp + k) * ldy + row] = res[k];
+  }
+}
+
 bool seq_gemm_supported(const MatView& w) {
   if (w.bits != 8 && w.bits != 4) return false;
   if (w.cols % 32) return false;
@@ -896,6 +1004,21 @@ void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T,
   GEM_DISPATCH_Q(w.bits, w.scale_f32, F);
 #undef F
 #undef F2
+}
+
+bool seq_head_f16_supported(const MatView& w) {
+  return w.bits == 16 && w.cols > 0 && w.cols % 16 == 0 && (uintptr_t)w.q % 16 == 0 &&
+         (w.rows + kH16Rows - 1) / kH16Rows <= 65535;
+}
+
+void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int ldy, cudaStream_t st) {
+  static bool init = false;
+  if (!init) {
+    cudaFuncSetAttribute(k_seq_head_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kH16Smem);
+    init = true;
+  }
+  const dim3 grid((T + kH16Pos - 1) / kH16Pos, (w.rows + kH16Rows - 1) / kH16Rows);
+  launch_k(k_seq_head_f16, grid, dim3(kH16Threads), kH16Smem, st, (const __half*)w.q, w.rows, w.cols, x, T, y, ldy);
 }
 
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,

@@ -304,3 +304,47 @@ def test_head_full_partial_row_groups(torch, isa, threads, tmp_path, batch):
         assert abs(lp[b] - want[0]) < 2e-5, (b, lp[b], want[0])
         assert am[b] == want[1], b
     g.close()
+
+
+@pytest.fixture(scope="module")
+def f16_head(tmp_path_factory):
+    """Q4_0 body with an F16 output matrix of 1000 rows (a partial 64-row tile) and a hidden size of
+    352 (two whole 128-column stages and a short third one)."""
+    cfg = dict(synth.SMALL, d=352, nh=4, nkv=1, hd=64, ff=512, vocab=1000, layers=2)
+    return synth.write_model(tmp_path_factory.mktemp("f16head") / "f16head.gguf", cfg, seed=11, body="q4_0", head="f16")
+
+
+@pytest.mark.parametrize("n", [1, 33, 300])
+def test_parallel_f16_head_full(torch, isa, f16_head, n):
+    """The full head of an F16 output matrix as a matrix product (dot16 per row and position) under
+    the parallel schedule: one position, a ragged 32-position tile, and two 256-position chunks."""
+    from gem_b200 import PARALLEL
+    g = Gemma(f16_head, ctx=320)
+    g.set_schedule(PARALLEL)
+    o = orc.Model(f16_head, ctx=320, threads=REF_THREADS, isa="avx512")
+    toks = synth.tokens(n + 1, g.vocab, seed=120 + n)
+    lp, am = g.score(toks, FULL)
+    lpo, amo, _, _ = o.score(toks, FULL)
+    assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo), np.abs(lp - lpo).max()
+    g.close()
+
+
+@pytest.mark.parametrize("batch", [5, 13, 40])
+def test_head_full_f16_batches(torch, isa, threads, f16_head, batch):
+    """Batched full-head calls on an F16 output matrix: streamed per state below 12 states, the
+    matrix product from 12 on (a ragged position tile at 13 and 40)."""
+    g = Gemma(f16_head, ctx=64)
+    o = orc.Model(f16_head, ctx=64, threads=threads, isa="avx512")
+    rng = np.random.default_rng(90 + batch)
+    H = rng.standard_normal((batch, g.d)).astype(np.float32)
+    T = rng.integers(0, g.vocab, batch).astype(np.uint32)
+    Hd, Td = torch.tensor(H, device="cuda"), torch.tensor(T.astype(np.int32), device="cuda")
+    lp = torch.empty(batch, device="cuda")
+    am = torch.empty(batch, dtype=torch.int32, device="cuda")
+    g.head_full_dev(Hd.data_ptr(), Td.data_ptr(), batch, lp.data_ptr(), am.data_ptr())
+    lp, am = lp.cpu().numpy(), am.cpu().numpy().astype(np.uint32)
+    for b in range(batch):
+        want = o.full(H[b], int(T[b]))
+        assert abs(lp[b] - want[0]) < 2e-5, (b, lp[b], want[0])
+        assert am[b] == want[1], b
+    g.close()
