@@ -850,14 +850,32 @@ void launch_seq_norm(float* x, const float* delta, const float* w_post, const fl
                                                                               xn_out);
 }
 
+// The halving reduction of dot512/dot16 over the 16 threads of a half-warp, as a reduce-scatter: thread
+// l of the half holds lane l of 64 sums v[0..64); each round (partner l ^ 8, ^ 4, ^ 2, ^ 1) adds the
+// partner's lane to the half of the sums this thread keeps, so the pairs are lane i + lane i + 8, then
+// + 4, + 2, + 1 as in the reference. Thread l ends with sums 4l .. 4l + 3 in v[0..4).
+__device__ __forceinline__ void half_reduce16(float (&v)[64], int l) {
+#pragma unroll
+  for (int m = 8, n = 32; m >= 1; m >>= 1, n >>= 1) {
+    const bool up = (l & m) != 0;  // keep the upper n sums, send the lower ones
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+      const float keep = up ? v[i + n] : v[i], send = up ? v[i] : v[i + n];
+      v[i] = add(keep, __shfl_xor_sync(0xffffffffu, send, m));
+    }
+  }
+}
+
 // Full head over an F16 output matrix for T positions, exact: y[p][r] = dot16 (q8.rs:358-369) of row r,
 // each f16 weight converted to fp32, with the fp32 hidden state of position p -- lane i sums
 // w[16c+i] * x[16c+i] by FMA in order of c, then the halving reduction. A CTA takes kH16Rows rows x
 // kH16Pos positions in stages of kH16Kc columns, double-buffered: the weights pass through registers
 // (converted once per CTA and stored as fp32 rows), the hidden states arrive by asynchronous copies.
-// Warp w computes rows 8 (w % 8) .. + 8 and positions 16 (w / 8) .. + 16 with the quad tile of the
-// scores kernel (thread u of a quad holds lanes 4u .. 4u + 3 of 4 rows x 4 positions).
-constexpr int kH16Rows = 64, kH16Pos = 32, kH16Kc = 128, kH16Stride = kH16Kc + 4, kH16Threads = 512;
+// Thread l of half h of warp w holds lane l of 8 rows (8 (w % 8) + r) x 8 positions
+// (16 (w / 8) + 2p + h): 16 loaded values per 64 FMAs, the ratio at which loads into registers and
+// the FMA pipe run at the same rate. Rows are padded to kH16Kc + 16 floats, so the two halves' position
+// rows (adjacent) fall in opposite halves of the banks and the shared row loads broadcast.
+constexpr int kH16Rows = 64, kH16Pos = 32, kH16Kc = 128, kH16Stride = kH16Kc + 16, kH16Threads = 512;
 constexpr size_t kH16Smem = (size_t)2 * (kH16Rows + kH16Pos) * kH16Stride * 4;
 
 __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w, int rows, int d, const float* x, int T,
@@ -905,13 +923,13 @@ __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w
   load_x(0, 0);
   cp_commit();
   store_w(0);
-  const int lane = tid & 31, warp = tid >> 5, u = lane & 3, qd = lane >> 2, rg = qd >> 2, kg = qd & 3;
-  const int tr = (warp & 7) * 8 + rg * 4, tp = (warp >> 3) * 16 + kg * 4;
-  float2 acc[4][4][2];  // [row][position][lanes (4u, 4u + 1), (4u + 2, 4u + 3)]
+  const int lane = tid & 31, warp = tid >> 5, l = lane & 15, hh = lane >> 4;
+  const int tr = (warp & 7) * 8, tp = (warp >> 3) * 16 + hh;
+  float2 acc[8][4];  // [row][position pair (2j, 2j + 1)], lane l
 #pragma unroll
-  for (int r = 0; r < 4; ++r)
+  for (int r = 0; r < 8; ++r)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) acc[r][k][0] = acc[r][k][1] = make_float2(0.0f, 0.0f);
+    for (int j = 0; j < 4; ++j) acc[r][j] = make_float2(0.0f, 0.0f);
   for (int kc = 0; kc < nk; ++kc) {
     const int buf = kc & 1;
     cp_wait<0>();
@@ -921,33 +939,37 @@ __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w
       load_x(kc + 1, buf ^ 1);
       cp_commit();
     }
-    const float* qp = sw + (buf * kH16Rows + tr) * kH16Stride + 4 * u;
-    const float* kp = sx + (buf * kH16Pos + tp) * kH16Stride + 4 * u;
+    const float* qp = sw + (buf * kH16Rows + tr) * kH16Stride + l;
+    const float* kp = sx + (buf * kH16Pos + tp) * kH16Stride + l;
     const int nc = min(kH16Kc, d - kc * kH16Kc) / 16;
 #pragma unroll 2
     for (int c = 0; c < nc; ++c) {
-      float4 qv[4], kv[4];
+      float wr[8], xp[8];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) qv[r] = *(const float4*)(qp + r * kH16Stride + 16 * c);
+      for (int r = 0; r < 8; ++r) wr[r] = qp[r * kH16Stride + 16 * c];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) kv[k] = *(const float4*)(kp + k * kH16Stride + 16 * c);
+      for (int p = 0; p < 8; ++p) xp[p] = kp[2 * p * kH16Stride + 16 * c];
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int r = 0; r < 8; ++r)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          acc[r][k][0] = __ffma2_rn(make_float2(qv[r].x, qv[r].y), make_float2(kv[k].x, kv[k].y), acc[r][k][0]);
-          acc[r][k][1] = __ffma2_rn(make_float2(qv[r].z, qv[r].w), make_float2(kv[k].z, kv[k].w), acc[r][k][1]);
-        }
+        for (int j = 0; j < 4; ++j)
+          acc[r][j] = __ffma2_rn(make_float2(wr[r], wr[r]), make_float2(xp[2 * j], xp[2 * j + 1]), acc[r][j]);
     }
     if (kc + 1 < nk) store_w(buf ^ 1);
   }
-  float res[4];
-  quad_reduce16(acc, u, res);
-  const int row = r0 + tr + u;  // thread u finishes row tr + u, positions tp .. tp + 3
+  float v[64];  // sum o = 8 row + position
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[8 * r + 2 * j] = acc[r][j].x, v[8 * r + 2 * j + 1] = acc[r][j].y;
+  half_reduce16(v, l);
+  const int row = r0 + tr + (l >> 1);  // sums 4l .. 4l + 3: row l / 2, positions 4 (l % 2) + i
   if (row < rows) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      if (p0 + tp + k < T) y[(size_t)(p0 + tp + k) * ldy + row] = res[k];
+    for (int i = 0; i < 4; ++i) {
+      const int p = p0 + tp + 2 * (4 * (l & 1) + i);
+      if (p < T) y[(size_t)p * ldy + row] = v[i];
+    }
   }
 }
 
@@ -1017,7 +1039,7 @@ void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int 
     cudaFuncSetAttribute(k_seq_head_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kH16Smem);
     init = true;
   }
-  const dim3 grid((T + kH16Pos - 1) / kH16Pos, (w.rows + kH16Rows - 1) / kH16Rows);
+  const dim3 grid((T + kH16Pos - 1) / kH16Pos, (w.rows + kH16Rows - 1) / kH16Rows);  // position tiles fastest
   launch_k(k_seq_head_f16, grid, dim3(kH16Threads), kH16Smem, st, (const __half*)w.q, w.rows, w.cols, x, T, y, ldy);
 }
 
