@@ -15,15 +15,18 @@
 //   k_seq_norm         residual + post-norm, pre-norm, Act::quantize; warp per position
 //   k_seq_gemm         Y[t][r] = row r . act[t] with the reference's 16-lane order (q8.rs:248-292)
 //   k_seq_attn_prep    QK-norm, RoPE, q scale, K/V append                           (model.rs:316-335)
-//   k_seq_scores_tile  dot512(q[t][h], K[p]) for p in the window of t             (model.rs:344-353)
+//   k_seq_scores_tile8 dot512(q[t][h], K[p]) for p in the window of t             (model.rs:344-353)
 //   k_seq_softmax      max, exp_fast, sequential sum, 1/sum                         (model.rs:354-361)
-//   k_seq_pv_tile      P.V partial sums over the pool's position ranges             (model.rs:362-382)
+//   k_seq_pv_tile8     P.V partial sums over the pool's position ranges             (model.rs:362-382)
+//                      (k_seq_pv_tile for head dims other than 256)
 //   k_seq_pv_combine   partials added in range order, then Act::quantize
 //   k_seq_glu_quant    GELU-tanh (or SiLU) gate * up, Act::quantize                 (model.rs:408-416)
-//   k_seq_class_logits two-level class logits dot512(A[c], h[t]) + b[c]            (main.rs:82-93)
+//   k_seq_dot16_gemm   two-level class logits dot512(A[c], h[t]) + b[c]            (main.rs:82-93)
+//                      and the full head of an F16 output matrix, dot16           (q8.rs:358-369)
 //   k_seq_logit_reduce full-head log-sum-exp, argmax and target logit per position  (main.rs:30-37)
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "exact.cuh"
@@ -363,125 +366,9 @@ __global__ void k_seq_attn_prep(AttnArgs A, const float* qkv, int qkv_ld, int L,
                   qn + (size_t)t * A.nh * A.hd, smp, s_r);
 }
 
-// The halving reduction of dot512 (lane i + lane i + 8, then + 4, + 2, + 1) over a quad of threads:
-// thread u holds lanes 4u .. 4u + 3 of a block of 4 rows x 4 columns as
-// acc[row][column][(4u, 4u + 1), (4u + 2, 4u + 3)] and returns row u's 4 columns in res.
-__device__ __forceinline__ void quad_reduce16(const float2 (&acc)[4][4][2], int u, float (&res)[4]) {
-  // Round 1 (partner u ^ 2 holds lanes i + 8): threads 0, 1 keep rows 0, 1 and threads 2, 3 rows 2, 3;
-  // b = lane i + lane i + 8 for i = 4 (u & 1) + j.
-  float b[2][4][4];  // [kept row][column][j]
-#pragma unroll
-  for (int m = 0; m < 2; ++m)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float l[4] = {acc[m][k][0].x, acc[m][k][0].y, acc[m][k][1].x, acc[m][k][1].y};
-      const float h[4] = {acc[m + 2][k][0].x, acc[m + 2][k][0].y, acc[m + 2][k][1].x, acc[m + 2][k][1].y};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float got = __shfl_xor_sync(0xffffffffu, u < 2 ? h[j] : l[j], 2);
-        b[m][k][j] = add(u < 2 ? l[j] : h[j], got);
-      }
-    }
-  // Round 2 (partner u ^ 1 holds i + 4): even threads keep row 0 of their pair of rows, odd row 1;
-  // c = b_i + b_i+4 for i = j, then (c0 + c2) + (c1 + c3).
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    float cc[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float got = __shfl_xor_sync(0xffffffffu, (u & 1) ? b[0][k][j] : b[1][k][j], 1);
-      cc[j] = add((u & 1) ? b[1][k][j] : b[0][k][j], got);
-    }
-    res[k] = add(add(cc[0], cc[2]), add(cc[1], cc[3]));
-  }
-}
-
-// Tiled scores: a CTA takes kAttnTQ consecutive positions (R = kAttnTQ * G rows: position x query head
-// of kv group blockIdx.z) against kScKC key positions from pbase + blockIdx.y * kScKC, both staged in
-// shared memory (rows padded to hd + 4 floats, so 8 consecutive rows start in distinct banks), each
-// key row read once per tile. dot512's 16 lanes are split over a quad: thread u holds lanes 4u .. 4u + 3
-// (elements 16c + 4u .. + 3) of a block of 4 rows x 4 keys, each lane's FMAs in the reference's order.
-// A warp's 8 quads cover 8 rows x 16 keys (2 row groups x 4 key groups), so a query load serves 4 quads
-// and a key load 2. The halving reduction (lane i + lane i + 8, then + 4, + 2, + 1) runs over the quad
-// with shuffles, each thread finishing the 4 pairs of one row. Only keys in a row's window [lo, pos]
-// are written.
+// Score tiles: a CTA takes kAttnTQ consecutive positions x the G query heads of kv group blockIdx.z
+// (R rows) against kScKC key positions from pbase + blockIdx.y * kScKC (k_seq_scores_tile8 below).
 constexpr int kAttnTQ = 8, kScKC = 32;
-
-template <int G>
-__global__ void __launch_bounds__(256, 2) k_seq_scores_tile(AttnArgs A0, const float* qn, int L, uint32_t pos0,
-                                                            size_t kv_stride, uint32_t pbase, float* scores,
-                                                            int sstride) {
-  pdl_wait();
-  extern __shared__ __align__(16) float sm[];
-  constexpr int R = kAttnTQ * G;  // a multiple of 8
-  const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
-  const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
-  const int hd = A.hd, g = blockIdx.z, rs = hd + 4;
-  const int t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0);  // positions inside the sequence
-  qn += (size_t)sq_i * L * A.nh * hd;                                        // this sequence's rows
-  scores += (size_t)sq_i * L * A.nh * sstride;
-  const uint32_t p0 = pbase + blockIdx.y * kScKC;
-  const uint32_t need_lo = window_lo(pos0 + t0, A.window), need_hi = pos0 + t0 + tn - 1;
-  if (p0 > need_hi || p0 + kScKC <= need_lo) return;
-  float* sq = sm;           // [R][hd + 4]
-  float* sk = sm + R * rs;  // [kScKC][hd + 4]
-  const int rw = A.nkv * hd, h4 = hd / 4;
-  // staging: thread i copies 16-byte column i % h4 of rows i / h4, i / h4 + step, ... (one division)
-  const int e = (int)threadIdx.x % h4, step = (int)blockDim.x / h4;
-  const bool whole = (int)blockDim.x % h4 == 0;
-  for (int i = threadIdx.x, row = (int)threadIdx.x / h4; i < R * h4; i += blockDim.x, row += step) {
-    const int rr = whole ? row : i / h4, ee = whole ? e : i % h4, tt = rr / G, h = rr % G;
-    const bool ok = tt < tn;
-    cp16(sq + rr * rs + ee * 4, qn + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * hd + ee * 4 : 0), ok);
-  }
-  for (int i = threadIdx.x, pr = (int)threadIdx.x / h4; i < kScKC * h4; i += blockDim.x, pr += step) {
-    const int rr = whole ? pr : i / h4, ee = whole ? e : i % h4;
-    const uint32_t p = p0 + rr;
-    const bool ok = p <= need_hi;
-    cp16(sk + rr * rs + ee * 4, A.kcache + (ok ? (size_t)p * rw + g * hd + ee * 4 : 0), ok);
-  }
-  cp_commit();
-  cp_wait<0>();
-  __syncthreads();
-  const int lane = threadIdx.x & 31, u = lane & 3, qd = lane >> 2, rg = qd >> 2, kg = qd & 3;
-  constexpr int KCW = kScKC / 16, NWT = (R / 8) * KCW;  // warp tiles of 8 rows x 16 keys
-  for (int wt = (int)threadIdx.x >> 5; wt < NWT; wt += (int)blockDim.x >> 5) {
-    const int r0 = (wt / KCW) * 8 + rg * 4, k0 = (wt % KCW) * 16 + kg * 4;
-    const float* qp = sq + r0 * rs + 4 * u;
-    const float* kp = sk + k0 * rs + 4 * u;
-    float2 acc[4][4][2];  // [row][key][lanes (4u, 4u + 1), (4u + 2, 4u + 3)]
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[r][k][0] = acc[r][k][1] = make_float2(0.0f, 0.0f);
-    for (int c = 0; c < hd / 16; ++c) {
-      float4 qv[4], kv[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) qv[r] = *(const float4*)(qp + r * rs + 16 * c);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) kv[k] = *(const float4*)(kp + k * rs + 16 * c);
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          acc[r][k][0] = __ffma2_rn(make_float2(qv[r].x, qv[r].y), make_float2(kv[k].x, kv[k].y), acc[r][k][0]);
-          acc[r][k][1] = __ffma2_rn(make_float2(qv[r].z, qv[r].w), make_float2(kv[k].z, kv[k].w), acc[r][k][1]);
-        }
-    }
-    float res[4];
-    quad_reduce16(acc, u, res);
-    const int row = r0 + u, tt = row / G, h = row % G;  // thread u finishes row r0 + u, keys k0 .. k0 + 3
-    if (tt < tn) {
-      const uint32_t pos = pos0 + t0 + tt, lo = window_lo(pos, A.window);
-      float* out = scores + ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t p = p0 + k0 + k;
-        if (p >= lo && p <= pos) out[p - lo] = res[k];
-      }
-    }
-  }
-}
 
 // Softmax per (position, head) with the reference's order: max, exp_fast(s - max), sequential sum,
 // multiply by 1/sum. One warp per (position, head).
@@ -612,6 +499,94 @@ __global__ void __launch_bounds__(128) k_seq_pv_tile(AttnArgs A0, int L, uint32_
   }
 }
 
+// P.V by range for head_dim 256, with a register tile that feeds the FMA pipe: as k_seq_pv_tile (a
+// CTA takes range r of every row of a tile of kAttnTQ positions x G heads, stages the range's V rows
+// and probabilities in chunks of kPvRows, writes the partial sums), but warp w holds rows 8w .. + 8 and
+// lane l columns 4l .. + 4 and 128 + 4l .. + 4, so per key 16 loaded values feed 64 FMAs (a row's
+// probabilities are a broadcast, a lane's V columns 16-byte pieces of one contiguous row).
+template <int G>
+__global__ void __launch_bounds__(32 * G, G <= 4 ? 3 : 2) k_seq_pv_tile8(AttnArgs A0, int L, uint32_t pos0, size_t kv_stride,
+                                                        const float* scores, int sstride, int threads, float* part) {
+  pdl_wait();
+  constexpr int R = kAttnTQ * G, HD = 256;
+  extern __shared__ __align__(16) float sv[];  // V [kPvRows][HD], then probabilities P [kPvRows][R]
+  __shared__ uint32_t s_lo[kAttnTQ], s_a[kAttnTQ], s_b[kAttnTQ];
+  const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
+  const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
+  scores += (size_t)sq_i * L * A.nh * sstride;
+  part += (size_t)sq_i * L * A.nh * threads * HD;
+  const int t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0), r = blockIdx.y;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, rw = A.nkv * HD;
+  float* sp = sv + kPvRows * HD;
+  if (threadIdx.x < kAttnTQ) {
+    const int tt = threadIdx.x;
+    uint32_t lo = 0, a = 0, b = 0;
+    if (tt < tn) {
+      const uint32_t pos = pos0 + t0 + tt;
+      lo = window_lo(pos, A.window);
+      const int n = (int)(pos + 1 - lo), per = (n + threads - 1) / threads;
+      a = lo + min(r * per, n);
+      b = lo + min((r + 1) * per, n);
+    }
+    s_lo[tt] = lo, s_a[tt] = a, s_b[tt] = b;
+  }
+  __syncthreads();
+  uint32_t ua = 0xffffffffu, ub = 0;
+  for (int tt = 0; tt < tn; ++tt)
+    if (s_a[tt] < s_b[tt]) ua = min(ua, s_a[tt]), ub = max(ub, s_b[tt]);
+  for (int g = 0; g < A.nkv; ++g) {
+    float2 acc[8][4];  // [row][(4l, 4l+1), (4l+2, 4l+3), (128+4l, +1), (128+4l+2, +3)]
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
+    for (uint32_t c0 = ua; c0 < ub; c0 += kPvRows) {
+      const int rows = (int)min((uint32_t)kPvRows, ub - c0);
+      __syncthreads();  // the previous chunk's reads are done
+      for (int e = threadIdx.x; e < rows * (HD / 4); e += blockDim.x) {  // V: 64 pieces of 16 bytes per key
+        const int pi = e / (HD / 4), c4 = e % (HD / 4);
+        cp16(sv + pi * HD + c4 * 4, A.vcache + (size_t)(c0 + pi) * rw + g * HD + c4 * 4, true);
+      }
+      // a row's probabilities are zero outside its range, which makes its FMAs there exact no-ops
+      // (a range's sum starts at +0 and never becomes -0, so adding 0 * v changes nothing)
+      for (int i = threadIdx.x; i < R * kPvRows; i += blockDim.x) {
+        const int row = i / kPvRows, pi = i % kPvRows, tt = row / G, h = row % G;
+        const uint32_t p = c0 + pi;
+        const bool ok = tt < tn && pi < rows && p >= s_a[tt] && p < s_b[tt];
+        cp4(sp + pi * R + row, scores + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride + (p - s_lo[tt]) : 0), ok);
+      }
+      cp_commit();
+      cp_wait<0>();
+      __syncthreads();
+      const float* pp = sp + 8 * w;
+      const float* vp = sv + 4 * lane;
+#pragma unroll 1
+      for (int k = 0; k < rows; ++k) {
+        const float4 pa = *(const float4*)(pp + k * R), pb = *(const float4*)(pp + k * R + 4);
+        const float4 va = *(const float4*)(vp + k * HD), vb = *(const float4*)(vp + k * HD + 128);
+        const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 q = make_float2(pr[i], pr[i]);
+          acc[i][0] = __ffma2_rn(q, make_float2(va.x, va.y), acc[i][0]);
+          acc[i][1] = __ffma2_rn(q, make_float2(va.z, va.w), acc[i][1]);
+          acc[i][2] = __ffma2_rn(q, make_float2(vb.x, vb.y), acc[i][2]);
+          acc[i][3] = __ffma2_rn(q, make_float2(vb.z, vb.w), acc[i][3]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = 8 * w + i, tt = row / G, h = row % G;
+      if (tt < tn) {
+        float* o = part + (((size_t)(t0 + tt) * A.nh + g * G + h) * threads + r) * HD + 4 * lane;
+        *(float4*)o = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
+        *(float4*)(o + 128) = make_float4(acc[i][2].x, acc[i][2].y, acc[i][3].x, acc[i][3].y);
+      }
+    }
+  }
+}
+
 // att[t][h][j] = partials summed in range order (from 0), then Act::quantize. One CTA per
 // (position, head), all partial loads in flight before the ordered adds.
 __global__ void k_seq_pv_combine(AttnArgs A, const float* part, int threads, int8_t* aq, float* as) {
@@ -656,59 +631,6 @@ __global__ void k_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t
       v = mul(mul(mul(0.5f, g), add(1.0f, k)), u);
     }
     quant_block_warp_x(v, lane, aq + (size_t)t * ff + b * 32, as + (size_t)t * nbk + b);
-  }
-}
-
-// ------------------------------------------------------------------------------------------------
-// Two-level class logits for every position: cl[t][c] = dot512(A[c], h[t]) + b[c]. A thread pair
-// holds one class's 16 lanes for 8 positions; CTA tile 32 classes x 32 positions, the positions'
-// hidden states staged in shared memory, class rows read from L2.
-// ------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256, 2) k_seq_class_logits(const float* A, const float* bias, int k, const float* h,
-                                                             int d, int T, float* cl) {
-  pdl_wait();
-  extern __shared__ __align__(16) float sh[];  // [32][d]
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane & 1;
-  const int tok0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-  for (int i = threadIdx.x; i < 32 * d / 4; i += blockDim.x) {
-    const int t = i / (d / 4), j = i % (d / 4);
-    const bool ok = tok0 + t < T;
-    cp16(sh + i * 4, h + (ok ? (size_t)(tok0 + t) * d + j * 4 : 0), ok);
-  }
-  cp_commit();
-  cp_wait<0>();
-  __syncthreads();
-  const int c = c0 + (warp & 1) * 16 + (lane >> 1);
-  const int tl = (warp >> 1) * 8;
-  const float* arow = A + (size_t)min(c, k - 1) * d + half * 8;
-  float2 acc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = make_float2(0.0f, 0.0f);
-  float4 a0 = __ldg((const float4*)arow), a1 = __ldg((const float4*)(arow + 4));
-  for (int ch = 0; ch < d / 16; ++ch) {
-    const float2 av[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
-    if (ch + 1 < d / 16) {  // the next chunk's class row while this one computes
-      a0 = __ldg((const float4*)(arow + (ch + 1) * 16));
-      a1 = __ldg((const float4*)(arow + (ch + 1) * 16 + 4));
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float* hv = sh + (size_t)(tl + u) * d + ch * 16 + half * 8;
-      const float4 b0 = *(const float4*)hv, b1 = *(const float4*)(hv + 4);
-      acc[u][0] = __ffma2_rn(av[0], make_float2(b0.x, b0.y), acc[u][0]);
-      acc[u][1] = __ffma2_rn(av[1], make_float2(b0.z, b0.w), acc[u][1]);
-      acc[u][2] = __ffma2_rn(av[2], make_float2(b1.x, b1.y), acc[u][2]);
-      acc[u][3] = __ffma2_rn(av[3], make_float2(b1.z, b1.w), acc[u][3]);
-    }
-  }
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const float a8[8] = {acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y, acc[u][2].x, acc[u][2].y, acc[u][3].x, acc[u][3].y};
-    const float z = reduce16_pair(a8);
-    const int t = tok0 + tl + u;
-    if (half == 0 && c < k && t < T) cl[(size_t)t * k + c] = add(z, bias[c]);
   }
 }
 
@@ -866,9 +788,11 @@ __device__ __forceinline__ void half_reduce16(float (&v)[64], int l) {
   }
 }
 
-// Full head over an F16 output matrix for T positions, exact: y[p][r] = dot16 (q8.rs:358-369) of row r,
-// each f16 weight converted to fp32, with the fp32 hidden state of position p -- lane i sums
-// w[16c+i] * x[16c+i] by FMA in order of c, then the halving reduction. A CTA takes kH16Rows rows x
+// Exact products of 16-lane dots for T positions: y[p][r] = dot16 (q8.rs:358-369) of row r of an F16
+// matrix (each weight converted to fp32) or dot512 (model.rs:106-120) of row r of an fp32 matrix, with
+// the fp32 hidden state of position p, plus bias[r] when given (the two-level class logits,
+// main.rs:101-107) -- lane i sums w[16c+i] * x[16c+i] by FMA in order of c, then the halving
+// reduction, then the bias. A CTA takes kH16Rows rows x
 // kH16Pos positions in stages of kH16Kc columns, double-buffered: the weights pass through registers
 // (converted once per CTA and stored as fp32 rows), the hidden states arrive by asynchronous copies.
 // Thread l of half h of warp w holds lane l of 8 rows (8 (w % 8) + r) x 8 positions
@@ -878,8 +802,9 @@ __device__ __forceinline__ void half_reduce16(float (&v)[64], int l) {
 constexpr int kH16Rows = 64, kH16Pos = 32, kH16Kc = 128, kH16Stride = kH16Kc + 16, kH16Threads = 512;
 constexpr size_t kH16Smem = (size_t)2 * (kH16Rows + kH16Pos) * kH16Stride * 4;
 
-__global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w, int rows, int d, const float* x, int T,
-                                                                  float* y, int ldy) {
+template <typename WT>
+__global__ void __launch_bounds__(kH16Threads, 1) k_seq_dot16_gemm(const WT* w, const float* bias, int rows, int d,
+                                                                    const float* x, int T, float* y, int ldy) {
   pdl_wait();
   extern __shared__ __align__(16) float sm[];
   float* sw = sm;                                // [2][kH16Rows][kH16Stride]
@@ -890,24 +815,35 @@ __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w
   // 4 (t % 16) .. + 4 and + 64 .. of position t / 16, of each stage
   const int sr = tid >> 4, sc = (tid & 15) * 8, xc = (tid & 15) * 4;
   const bool ok0 = r0 + sr < rows, ok1 = r0 + sr + 32 < rows, okx = p0 + sr < T;
-  const int4* w0 = (const int4*)(w + (size_t)(ok0 ? r0 + sr : 0) * d);
-  const int4* w1 = (const int4*)(w + (size_t)(ok1 ? r0 + sr + 32 : 0) * d);
+  const WT* w0 = w + (size_t)(ok0 ? r0 + sr : 0) * d;
+  const WT* w1 = w + (size_t)(ok1 ? r0 + sr + 32 : 0) * d;
   const float* xs = x + (size_t)(okx ? p0 + sr : 0) * d;
   int4 wv[2];
-  auto load_w = [&](int kc) {
-    const int c = kc * kH16Kc + sc;  // d is a multiple of 16: an 8-half piece is whole or outside
-    wv[0] = ok0 && c < d ? ldg_stream(w0 + c / 8) : make_int4(0, 0, 0, 0);
-    wv[1] = ok1 && c < d ? ldg_stream(w1 + c / 8) : make_int4(0, 0, 0, 0);
+  auto load_w = [&](int kc, int buf) {
+    const int c = kc * kH16Kc + sc;  // d is a multiple of 16: an 8-weight piece is whole or outside
+    if constexpr (std::is_same<WT, float>::value) {  // fp32 rows: straight into the stage
+      float* dst = sw + (buf * kH16Rows + sr) * kH16Stride + sc;
+      const float* src0 = (const float*)w0 + c, *src1 = (const float*)w1 + c;
+      cp16(dst, ok0 && c < d ? src0 : (const float*)w, ok0 && c < d);
+      cp16(dst + 4, ok0 && c < d ? src0 + 4 : (const float*)w, ok0 && c < d);
+      cp16(dst + 32 * kH16Stride, ok1 && c < d ? src1 : (const float*)w, ok1 && c < d);
+      cp16(dst + 32 * kH16Stride + 4, ok1 && c < d ? src1 + 4 : (const float*)w, ok1 && c < d);
+    } else {  // f16 rows: through registers, converted by store_w
+      wv[0] = ok0 && c < d ? ldg_stream((const int4*)w0 + c / 8) : make_int4(0, 0, 0, 0);
+      wv[1] = ok1 && c < d ? ldg_stream((const int4*)w1 + c / 8) : make_int4(0, 0, 0, 0);
+    }
   };
   auto store_w = [&](int buf) {
+    if constexpr (!std::is_same<WT, float>::value) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const __half2* h2 = (const __half2*)&wv[h];
-      const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]), f2 = __half22float2(h2[2]),
-                   f3 = __half22float2(h2[3]);
-      float* dst = sw + (buf * kH16Rows + sr + 32 * h) * kH16Stride + sc;
-      *(float4*)dst = make_float4(f0.x, f0.y, f1.x, f1.y);
-      *(float4*)(dst + 4) = make_float4(f2.x, f2.y, f3.x, f3.y);
+      for (int h = 0; h < 2; ++h) {
+        const __half2* h2 = (const __half2*)&wv[h];
+        const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]), f2 = __half22float2(h2[2]),
+                     f3 = __half22float2(h2[3]);
+        float* dst = sw + (buf * kH16Rows + sr + 32 * h) * kH16Stride + sc;
+        *(float4*)dst = make_float4(f0.x, f0.y, f1.x, f1.y);
+        *(float4*)(dst + 4) = make_float4(f2.x, f2.y, f3.x, f3.y);
+      }
     }
   };
   auto load_x = [&](int kc, int buf) {
@@ -919,7 +855,7 @@ __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w
       cp16(dst + 64 * h, xs + (ok ? c : 0), ok);
     }
   };
-  load_w(0);
+  load_w(0, 0);
   load_x(0, 0);
   cp_commit();
   store_w(0);
@@ -935,7 +871,7 @@ __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w
     cp_wait<0>();
     __syncthreads();  // stage kc is in place; every warp is done with stage kc - 1's buffers
     if (kc + 1 < nk) {
-      load_w(kc + 1);
+      load_w(kc + 1, buf ^ 1);
       load_x(kc + 1, buf ^ 1);
       cp_commit();
     }
@@ -965,10 +901,95 @@ __global__ void __launch_bounds__(kH16Threads, 1) k_seq_head_f16(const __half* w
   half_reduce16(v, l);
   const int row = r0 + tr + (l >> 1);  // sums 4l .. 4l + 3: row l / 2, positions 4 (l % 2) + i
   if (row < rows) {
+    const float b = bias ? bias[row] : 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int p = p0 + tp + 2 * (4 * (l & 1) + i);
-      if (p < T) y[(size_t)p * ldy + row] = v[i];
+      if (p < T) y[(size_t)p * ldy + row] = bias ? add(v[i], b) : v[i];
+    }
+  }
+}
+
+// Tiled scores, dot512 (model.rs:344-353) of each query row with each key of the tile: kAttnTQ
+// positions x G heads of kv group blockIdx.z against kScKC keys, both staged in shared memory, each
+// key row read once per tile. Thread l of half h of a warp holds dot512's lane l of 8 rows x 8 keys
+// (keys 16 kb + 2k + h), so 16 loaded values feed 64 FMAs; the halving reduction is the half-warp
+// reduce-scatter. Only keys in a row's window [lo, pos] are written. Rows are padded to hd + 16 floats: the
+// two halves' key rows (adjacent) fall in opposite halves of the banks and the query rows broadcast.
+template <int G>
+__global__ void __launch_bounds__(256, 2) k_seq_scores_tile8(AttnArgs A0, const float* qn, int L, uint32_t pos0,
+                                                             size_t kv_stride, uint32_t pbase, float* scores,
+                                                             int sstride) {
+  pdl_wait();
+  extern __shared__ __align__(16) float sm[];
+  constexpr int R = kAttnTQ * G;  // a multiple of 8
+  const int tps = (L + kAttnTQ - 1) / kAttnTQ, sq_i = blockIdx.x / tps;
+  const AttnArgs A = seq_kv(A0, sq_i, kv_stride);
+  const int hd = A.hd, g = blockIdx.z, rs = hd + 16;
+  const int t0 = (blockIdx.x % tps) * kAttnTQ, tn = min(kAttnTQ, L - t0);  // positions inside the sequence
+  qn += (size_t)sq_i * L * A.nh * hd;                                        // this sequence's rows
+  scores += (size_t)sq_i * L * A.nh * sstride;
+  const uint32_t p0 = pbase + blockIdx.y * kScKC;
+  const uint32_t need_lo = window_lo(pos0 + t0, A.window), need_hi = pos0 + t0 + tn - 1;
+  if (p0 > need_hi || p0 + kScKC <= need_lo) return;
+  float* sq = sm;           // [R][hd + 16]
+  float* sk = sm + R * rs;  // [kScKC][hd + 16]
+  const int rw = A.nkv * hd, h4 = hd / 4;
+  const int e = (int)threadIdx.x % h4, step = (int)blockDim.x / h4;
+  const bool whole = (int)blockDim.x % h4 == 0;
+  for (int i = threadIdx.x, row = (int)threadIdx.x / h4; i < R * h4; i += blockDim.x, row += step) {
+    const int rr = whole ? row : i / h4, ee = whole ? e : i % h4, tt = rr / G, h = rr % G;
+    const bool ok = tt < tn;
+    cp16(sq + rr * rs + ee * 4, qn + (ok ? ((size_t)(t0 + tt) * A.nh + g * G + h) * hd + ee * 4 : 0), ok);
+  }
+  for (int i = threadIdx.x, pr = (int)threadIdx.x / h4; i < kScKC * h4; i += blockDim.x, pr += step) {
+    const int rr = whole ? pr : i / h4, ee = whole ? e : i % h4;
+    const uint32_t p = p0 + rr;
+    const bool ok = p <= need_hi;
+    cp16(sk + rr * rs + ee * 4, A.kcache + (ok ? (size_t)p * rw + g * hd + ee * 4 : 0), ok);
+  }
+  cp_commit();
+  cp_wait<0>();
+  __syncthreads();
+  const int lane = threadIdx.x & 31, l = lane & 15, hh = lane >> 4;
+  constexpr int KB = kScKC / 16, NWT = (R / 8) * KB;  // warp tiles of 8 rows x 16 keys
+  for (int wt = (int)threadIdx.x >> 5; wt < NWT; wt += (int)blockDim.x >> 5) {
+    const int r0 = (wt / KB) * 8, k0 = (wt % KB) * 16 + hh;  // keys k0 + 2k
+    const float* qp = sq + r0 * rs + l;
+    const float* kp = sk + k0 * rs + l;
+    float2 acc[8][4];  // [row][key pair (2j, 2j + 1)], lane l
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[r][j] = make_float2(0.0f, 0.0f);
+#pragma unroll 2
+    for (int c = 0; c < hd / 16; ++c) {
+      float qv[8], kv[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) qv[r] = qp[r * rs + 16 * c];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) kv[k] = kp[2 * k * rs + 16 * c];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          acc[r][j] = __ffma2_rn(make_float2(qv[r], qv[r]), make_float2(kv[2 * j], kv[2 * j + 1]), acc[r][j]);
+    }
+    float v[64];  // sum o = 8 row + key
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[8 * r + 2 * j] = acc[r][j].x, v[8 * r + 2 * j + 1] = acc[r][j].y;
+    half_reduce16(v, l);
+    const int row = r0 + (l >> 1), tt = row / G, h = row % G;  // sums 4l .. 4l + 3: row l / 2, keys 4 (l % 2) + i
+    if (tt < tn) {
+      const uint32_t pos = pos0 + t0 + tt, lo = window_lo(pos, A.window);
+      float* out = scores + ((size_t)(t0 + tt) * A.nh + g * G + h) * sstride;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t p = p0 + k0 + 2 * (4 * (l & 1) + i);
+        if (p >= lo && p <= pos) out[p - lo] = v[i];
+      }
     }
   }
 }
@@ -1033,14 +1054,20 @@ bool seq_head_f16_supported(const MatView& w) {
          (w.rows + kH16Rows - 1) / kH16Rows <= 65535;
 }
 
-void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int ldy, cudaStream_t st) {
+template <typename WT>
+static void launch_dot16_gemm(const WT* w, const float* bias, int rows, int d, const float* x, int T, float* y, int ldy,
+                              cudaStream_t st) {
   static bool init = false;
   if (!init) {
-    cudaFuncSetAttribute(k_seq_head_f16, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kH16Smem);
+    cudaFuncSetAttribute(k_seq_dot16_gemm<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kH16Smem);
     init = true;
   }
-  const dim3 grid((T + kH16Pos - 1) / kH16Pos, (w.rows + kH16Rows - 1) / kH16Rows);  // position tiles fastest
-  launch_k(k_seq_head_f16, grid, dim3(kH16Threads), kH16Smem, st, (const __half*)w.q, w.rows, w.cols, x, T, y, ldy);
+  const dim3 grid((T + kH16Pos - 1) / kH16Pos, (rows + kH16Rows - 1) / kH16Rows);  // position tiles fastest
+  launch_k(k_seq_dot16_gemm<WT>, grid, dim3(kH16Threads), kH16Smem, st, w, bias, rows, d, x, T, y, ldy);
+}
+
+void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int ldy, cudaStream_t st) {
+  launch_dot16_gemm((const __half*)w.q, nullptr, w.rows, w.cols, x, T, y, ldy, st);
 }
 
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
@@ -1053,18 +1080,19 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
   const int nchunk = (int)((pos0 + L - pbase + kScKC - 1) / kScKC);
   const int tps = (L + kAttnTQ - 1) / kAttnTQ;
   const dim3 sgrid(tps * nseq, nchunk, A.nkv), pgrid(tps * nseq, threads);
-  const size_t ssm = ((size_t)kAttnTQ * G + kScKC) * (A.hd + 4) * 4;
+  const size_t ssm8 = ((size_t)kAttnTQ * G + kScKC) * (A.hd + 16) * 4;
   const size_t psm = ((size_t)kPvRows * A.hd + (size_t)kAttnTQ * G * kPvRows) * 4;
   const int pth = A.hd / 2;
 #define F(GG)                                                                                                        \
   do {                                                                                                               \
     static bool init = false;                                                                                        \
     if (!init) {                                                                                                     \
-      cudaFuncSetAttribute(k_seq_scores_tile<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);         \
+      cudaFuncSetAttribute(k_seq_scores_tile8<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);        \
       cudaFuncSetAttribute(k_seq_pv_tile<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);             \
+      cudaFuncSetAttribute(k_seq_pv_tile8<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);            \
       init = true;                                                                                                   \
     }                                                                                                                \
-    launch_k(k_seq_scores_tile<GG>, dim3(sgrid), dim3(256), ssm, st, A, qn, L, pos0, kv_stride, pbase, scores, sstride);               \
+    launch_k(k_seq_scores_tile8<GG>, dim3(sgrid), dim3(256), ssm8, st, A, qn, L, pos0, kv_stride, pbase, scores, sstride);          \
   } while (0)
   switch (G) {
     case 1: F(1); break;
@@ -1087,7 +1115,15 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
     const int nw = (int)std::max<size_t>(1, std::min<size_t>(8, (size_t)(200 * 1024) / (es * 4)));
     launch_k(k_seq_softmax, dim3((T * A.nh + nw - 1) / nw), dim3(nw * 32), (size_t)nw * es * 4, st, A, T, L, pos0, scores, sstride);
   }
-#define P(GG) launch_k(k_seq_pv_tile<GG>, dim3(pgrid), dim3(pth), psm, st, A, L, pos0, kv_stride, scores, sstride, threads, part)
+#define P(GG)                                                                                                    \
+  do {                                                                                                           \
+    if (A.hd == 256)                                                                                             \
+      launch_k(k_seq_pv_tile8<GG>, dim3(pgrid), dim3(32 * GG), psm, st, A, L, pos0, kv_stride, scores, sstride,  \
+               threads, part);                                                                                    \
+    else                                                                                                         \
+      launch_k(k_seq_pv_tile<GG>, dim3(pgrid), dim3(pth), psm, st, A, L, pos0, kv_stride, scores, sstride, threads, \
+               part);                                                                                             \
+  } while (0)
   switch (G) {
     case 1: P(1); break;
     case 2: P(2); break;
@@ -1126,13 +1162,7 @@ void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, 
 
 void launch_seq_class_logits(const float* A, const float* b, int k, const float* h, int d, int T, float* cl,
                              cudaStream_t st) {
-  static bool init = false;
-  if (!init) {
-    cudaFuncSetAttribute(k_seq_class_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    init = true;
-  }
-  dim3 grid((T + 31) / 32, (k + 31) / 32);
-  launch_k(k_seq_class_logits, dim3(grid), dim3(256), (size_t)32 * d * 4, st, A, b, k, h, d, T, cl);
+  launch_dot16_gemm(A, b, k, d, h, T, cl, k, st);
 }
 
 void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, float* lp, uint32_t* am, int* err,
