@@ -21,10 +21,29 @@ namespace gem {
 
 
 // ------------------------------------------------------------------------------------------------
-// GEMV, exact: a warp covers 16 rows per step (lane pair per row).
+// GEMV, exact, for one activation vector: a row's 16 lanes (lane i = pair i of every 32-block, one
+// FMA per block with scale ws*as, q8.rs:248-292; for F16 lane i = element i of every 16-chunk,
+// q8.rs:358-369) go to 8 threads with 2 lanes each, thread o holding lanes 2o and 2o + 1 (one
+// 4-byte word of weights per block), so that even 640-row matrices spread over the SMs. Each thread
+// issues kGemvU weight loads before its FMA chain consumes them. The halving reduction runs over the
+// 8 threads: lane i + lane i + 8 is partner o ^ 4, + 4 is o ^ 2, + 2 is o ^ 1, then the thread's own
+// two lanes.
 // ------------------------------------------------------------------------------------------------
+constexpr int kGemvThreads = 64, kGemvU = 16;
+
+template <int BITS>
+__device__ __forceinline__ int load_word(const MatView& w, size_t r, int b, int o) {
+  if constexpr (BITS == 8) {
+    return __ldg((const int*)((const int8_t*)w.q + r * w.cols + (size_t)b * 32) + o);
+  } else {  // dot4_avx512 (q8.rs:307-326): bytes 0..15 low nibbles (weights 0..15), high nibbles 16..31
+    const unsigned raw = (unsigned)__ldg((const int*)((const uint8_t*)w.q + r * (w.cols / 2) + (size_t)b * 16) + (o & 3));
+    return (int)__vsub4((raw >> (4 * (o >> 2))) & 0x0f0f0f0fu, 0x08080808u);
+  }
+}
+
 template <int BITS, typename ST>
-__global__ void k_gemv_exact(MatView w, const int8_t* aq, const float* as, const float* x, float* y) {
+__global__ void __launch_bounds__(kGemvThreads) k_gemv_exact(MatView w, const int8_t* aq, const float* as, const float* x,
+                                                             float* y) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int8_t* saq = (int8_t*)smem_raw;
   float* sas = (float*)(smem_raw + w.cols);
@@ -36,14 +55,57 @@ __global__ void k_gemv_exact(MatView w, const int8_t* aq, const float* as, const
     for (int j = threadIdx.x; j < w.cols / 32; j += blockDim.x) sas[j] = as[j];
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int half = lane & 1;
-  for (int base = (blockIdx.x * nw + warp) * 16; base < w.rows; base += gridDim.x * nw * 16) {
-    int r = base + (lane >> 1);
-    bool ok = r < w.rows;
-    float v = row_dot_exact<BITS, ST>(w, ok ? r : w.rows - 1, half, saq, sas, sx);
-    if (ok && half == 0) y[r] = v;
+  const int o = threadIdx.x & 7;
+  const int r = blockIdx.x * (kGemvThreads / 8) + (threadIdx.x >> 3);
+  const bool ok = r < w.rows;  // a row's 8 threads are consecutive lanes: the shuffles stay inside them
+  const size_t rr = ok ? r : w.rows - 1;
+  float a0 = 0.0f, a1 = 0.0f;  // lanes 2o, 2o + 1
+  if constexpr (BITS == 16) {
+    const __half2* row = (const __half2*)((const __half*)w.q + rr * w.cols);
+    const int nc = w.cols / 16;
+    for (int c0 = 0; c0 < nc; c0 += kGemvU) {
+      __half2 v[kGemvU];
+#pragma unroll
+      for (int u = 0; u < kGemvU; ++u)
+        if (c0 + u < nc) v[u] = __ldg(row + (size_t)(c0 + u) * 8 + o);
+#pragma unroll
+      for (int u = 0; u < kGemvU; ++u) {
+        if (c0 + u >= nc) break;
+        const float2 f = __half22float2(v[u]);
+        const float* xv = sx + (c0 + u) * 16 + 2 * o;
+        a0 = fmaf(f.x, xv[0], a0);
+        a1 = fmaf(f.y, xv[1], a1);
+      }
+    }
+  } else {
+    const int nb = w.cols / 32;
+    const ST* srow = (const ST*)w.s + rr * nb;
+    for (int b0 = 0; b0 < nb; b0 += kGemvU) {
+      int wv[kGemvU];
+      float sc[kGemvU];
+#pragma unroll
+      for (int u = 0; u < kGemvU; ++u)
+        if (b0 + u < nb) {
+          wv[u] = load_word<BITS>(w, rr, b0 + u, o);
+          sc[u] = ld_scale(srow, b0 + u);
+        }
+#pragma unroll
+      for (int u = 0; u < kGemvU; ++u) {
+        if (b0 + u >= nb) break;
+        const int av = ((const int*)saq)[(b0 + u) * 8 + o];
+        const float s = mul(sc[u], sas[b0 + u]);
+        a0 = fmaf(madd_lo(wv[u], av), s, a0);
+        a1 = fmaf(madd_hi(wv[u], av), s, a1);
+      }
+    }
   }
+  a0 = add(a0, __shfl_xor_sync(0xffffffffu, a0, 4));
+  a1 = add(a1, __shfl_xor_sync(0xffffffffu, a1, 4));
+  a0 = add(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
+  a1 = add(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+  a0 = add(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
+  a1 = add(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+  if (ok && o == 0) y[r] = add(a0, a1);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -489,15 +551,13 @@ static size_t act_smem_x(int cols, int bits) {
 
 void launch_gemv_exact(const MatView& w, const int8_t* aq, const float* as, const float* x, float* y, int sms,
                        cudaStream_t st) {
-  const int threads = 256, nw = threads / 32;
-  int blocks = (w.rows + nw * 16 - 1) / (nw * 16);
-  blocks = min(blocks, sms * 8);
+  const int blocks = (w.rows + kGemvThreads / 8 - 1) / (kGemvThreads / 8);  // 8 rows per CTA
   size_t sm = act_smem_x(w.cols, w.bits);
 #define F(B, S)                                                                                     \
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_gemv_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_gemv_exact<B, S><<<blocks, threads, sm, st>>>(w, aq, as, x, y);                               \
+    k_gemv_exact<B, S><<<blocks, kGemvThreads, sm, st>>>(w, aq, as, x, y);                          \
   } while (0)
   GEM_DISPATCH_X(w.bits, w.scale_f32, F);
 #undef F
