@@ -15,6 +15,7 @@ namespace gem {
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
 __global__ void k_embed(MatView head, const uint32_t* row_of, const StepCur* cur, float scale, float* x) {
+  pdl_wait();
   uint32_t tok = cur->tok;
   size_t row = row_of ? row_of[tok] : tok;
   for (int j = threadIdx.x; j < head.cols; j += blockDim.x) x[j] = mul(weight_at<BITS, ST>(head, row, j), scale);
@@ -50,6 +51,7 @@ __device__ __forceinline__ float rms_r(float ss, int n, float eps) {
 // is written when not null (the final-norm hidden state of model.rs:428).
 __global__ void k_residual_norm_quant(float* x, const float* delta, const float* w_post, const float* w_pre,
                                       float eps, int d, int8_t* aq, float* as, float* xn_out) {
+  pdl_wait();
   extern __shared__ float sm[];
   float* xs = sm;            // d
   float* red = sm + d;       // 32
@@ -153,6 +155,7 @@ __device__ __forceinline__ void stage_act(int cols, const int8_t* aq, const floa
 
 template <int BITS, typename ST>
 __global__ void k_gemv(MatView w, const int8_t* aq, const float* as, const float* x, float* y) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int8_t* saq = (int8_t*)smem_raw;
   float* sas = (float*)(smem_raw + w.cols);
@@ -189,6 +192,7 @@ __device__ __forceinline__ void rope_block(float* v, const float* sn, const floa
 }
 
 __global__ void k_attn_partial(AttnArgs A) {
+  pdl_wait();
   extern __shared__ __align__(16) float asm_[];
   const int hd = A.hd, G = A.nh / A.nkv, g = blockIdx.y, s = blockIdx.x;
   float* sq = asm_;                   // G * hd
@@ -294,6 +298,7 @@ __global__ void k_attn_partial(AttnArgs A) {
 // Merge the split partials of head h, normalise, and quantize the head's output blocks (the
 // Act::quantize of model.rs:384). One CTA per q head, hd threads.
 __global__ void k_attn_merge(AttnArgs A, int8_t* aq, float* as) {
+  pdl_wait();
   __shared__ float wsm[64];
   __shared__ float tot;
   const int hd = A.hd, G = A.nh / A.nkv, h = blockIdx.x, g = h / G, hh = h % G;
@@ -328,6 +333,7 @@ __global__ void k_attn_merge(AttnArgs A, int8_t* aq, float* as) {
 // Act::quantize (model.rs:417). SiLU for qwen2 (model.rs:400-407). gu holds [gate | up].
 // ------------------------------------------------------------------------------------------------
 __global__ void k_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float* as, float* gout) {
+  pdl_wait();
   int lane = threadIdx.x & 31;
   int warps = (blockDim.x >> 5) * gridDim.x;
   for (int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < ff / 32; b += warps) {
@@ -349,6 +355,7 @@ __global__ void k_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float
 // Step bookkeeping for the scoring loop: token, position and target of step `step`.
 // Token ids come from caller memory: ids >= vocab are recorded in *err and replaced by 0.
 __global__ void k_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, uint32_t vocab, StepCur* cur, int* err) {
+  pdl_wait();
   uint32_t i = *step;
   uint32_t t = toks[i], u = toks[i + 1];
   if (t >= vocab || u >= vocab) {
@@ -361,7 +368,7 @@ __global__ void k_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base
   cur->pos = base_pos + i;
   cur->slot = i;
 }
-__global__ void k_end_step(uint32_t* step) { *step += 1; }
+__global__ void k_end_step(uint32_t* step) { pdl_wait(); *step += 1; }
 
 // ------------------------------------------------------------------------------------------------
 // Full head (main.rs:20-38): logits = head . quantize(h); online (max, sum e^(z-max)), argmax and the
@@ -370,6 +377,7 @@ __global__ void k_end_step(uint32_t* step) { *step += 1; }
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
 __global__ void k_head_full(HeadArgs H) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
@@ -449,6 +457,7 @@ __global__ void k_head_full_merge(HeadArgs H, int nparts) {
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
 __global__ void k_tl_stage1(TwoLevelArgs T) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int bi = blockIdx.y;
   const int d = T.w.cols;
@@ -491,6 +500,7 @@ __global__ void k_tl_stage1(TwoLevelArgs T) {
 
 template <int BITS, typename ST>
 __global__ void k_tl_stage2(TwoLevelArgs T) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float red[32];
   __shared__ float red2[32];
@@ -676,7 +686,7 @@ static size_t act_smem(int cols, int bits) {
 }
 
 void launch_embed(const MatView& head, const uint32_t* row_of, const StepCur* cur, float scale, float* x, cudaStream_t st) {
-#define F(B, S) k_embed<B, S><<<1, 256, 0, st>>>(head, row_of, cur, scale, x)
+#define F(B, S) launch_k(k_embed<B, S>, dim3(1), dim3(256), 0, st, head, row_of, cur, scale, x)
   GEM_DISPATCH(head.bits, head.scale_f32, F);
 #undef F
 }
@@ -687,7 +697,7 @@ void launch_dequant_rows(const MatView& w, size_t r0, int nrows, float* out, cud
 }
 void launch_residual_norm_quant(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d,
                                 int8_t* aq, float* as, float* xn_out, cudaStream_t st) {
-  k_residual_norm_quant<<<1, 1024, (size_t)(d + 32) * 4, st>>>(x, delta, w_post, w_pre, eps, d, aq, as, xn_out);
+  launch_k(k_residual_norm_quant, dim3(1), dim3(1024), (size_t)(d + 32) * 4, st, x, delta, w_post, w_pre, eps, d, aq, as, xn_out);
 }
 void launch_quantize(const float* x, int n, int8_t* aq, float* as, cudaStream_t st) {
   int blocks = (n / 32 + 7) / 8;
@@ -702,7 +712,7 @@ void launch_gemv(const MatView& w, const int8_t* aq, const float* as, const floa
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_gemv<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_gemv<B, S><<<blocks, threads, sm, st>>>(w, aq, as, x, y);                                     \
+    launch_k(k_gemv<B, S>, dim3(blocks), dim3(threads), sm, st, w, aq, as, x, y);                   \
   } while (0)
   GEM_DISPATCH(w.bits, w.scale_f32, F);
 #undef F
@@ -711,18 +721,18 @@ void launch_attn(const AttnArgs& A, int8_t* aq, float* as, cudaStream_t st) {
   dim3 grid(A.nsplit, A.nkv);
   int G = A.nh / A.nkv;
   size_t sm = (size_t)(G * A.hd + 2 * A.hd + G * A.chunk + 32 + 2 * G) * 4;
-  k_attn_partial<<<grid, 256, sm, st>>>(A);
-  k_attn_merge<<<A.nh, A.hd, 0, st>>>(A, aq, as);
+  launch_k(k_attn_partial, grid, dim3(256), sm, st, A);
+  launch_k(k_attn_merge, dim3(A.nh), dim3(A.hd), 0, st, A, aq, as);
 }
 void launch_glu_quant(const float* gu, int ff, int silu, int8_t* aq, float* as, float* gout, cudaStream_t st) {
   int blocks = (ff / 32 + 7) / 8;
-  k_glu_quant<<<blocks, 256, 0, st>>>(gu, ff, silu, aq, as, gout);
+  launch_k(k_glu_quant, dim3(blocks), dim3(256), 0, st, gu, ff, silu, aq, as, gout);
 }
 void launch_begin_step(const uint32_t* toks, uint32_t* step, uint32_t base_pos, uint32_t vocab, StepCur* cur, int* err,
                        cudaStream_t st) {
-  k_begin_step<<<1, 1, 0, st>>>(toks, step, base_pos, vocab, cur, err);
+  launch_k(k_begin_step, dim3(1), dim3(1), 0, st, toks, step, base_pos, vocab, cur, err);
 }
-void launch_end_step(uint32_t* step, cudaStream_t st) { k_end_step<<<1, 1, 0, st>>>(step); }
+void launch_end_step(uint32_t* step, cudaStream_t st) { launch_k(k_end_step, dim3(1), dim3(1), 0, st, step); }
 
 int head_full_parts(int sms) { return sms * 2; }
 
@@ -734,7 +744,7 @@ void launch_head_full(const HeadArgs& H, int batch, int sms, cudaStream_t st) {
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_head_full<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_head_full<B, S><<<grid, 512, sm, st>>>(H);                                                    \
+    launch_k(k_head_full<B, S>, grid, dim3(512), sm, st, H);                                          \
   } while (0)
   GEM_DISPATCH(H.w.bits, H.w.scale_f32, F);
 #undef F
@@ -769,8 +779,8 @@ void launch_head_twolevel(const TwoLevelArgs& T, int batch, int sms, cudaStream_
       cudaFuncSetAttribute(k_tl_stage2<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
       init = true;                                                                                  \
     }                                                                                               \
-    k_tl_stage1<B, S><<<grid, 256, sm1, st>>>(t2);                                                  \
-    k_tl_stage2<B, S><<<batch, 256, sm2, st>>>(t2);                                                 \
+    launch_k(k_tl_stage1<B, S>, grid, dim3(256), sm1, st, t2);                                        \
+    launch_k(k_tl_stage2<B, S>, dim3(batch), dim3(256), sm2, st, t2);                                 \
   } while (0)
   GEM_DISPATCH(T.w.bits, T.w.scale_f32, F);
 #undef F

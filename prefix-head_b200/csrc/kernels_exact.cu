@@ -44,6 +44,7 @@ __device__ __forceinline__ int load_word(const MatView& w, size_t r, int b, int 
 template <int BITS, typename ST>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv_exact(MatView w, const int8_t* aq, const float* as, const float* x,
                                                              float* y) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int8_t* saq = (int8_t*)smem_raw;
   float* sas = (float*)(smem_raw + w.cols);
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_exact(MatView w, const in
 // ------------------------------------------------------------------------------------------------
 __global__ void k_residual_norm_quant_exact(float* x, const float* delta, const float* w_post, const float* w_pre,
                                             float eps, int d, int8_t* aq, float* as, float* xn_out) {
+  pdl_wait();
   extern __shared__ __align__(16) float smx[];
   float* xs = smx;       // d
   float* tv = smx + d;   // d
@@ -155,6 +157,7 @@ __global__ void k_residual_norm_quant_exact(float* x, const float* delta, const 
 // ------------------------------------------------------------------------------------------------
 // One CTA per kv group; writes normalised q to qn.
 __global__ void k_attn_prep_exact(AttnArgs A, float* qn) {
+  pdl_wait();
   extern __shared__ __align__(16) float smp[];
   __shared__ float s_r[17];
   attn_prep_token(A, A.qkv, A.cur->pos, blockIdx.x, qn, smp, s_r);
@@ -162,6 +165,7 @@ __global__ void k_attn_prep_exact(AttnArgs A, float* qn) {
 
 // scores[h][i] = dot512(q_h, k_(lo+i)) for every head and position (model.rs:344-353).
 __global__ void k_attn_scores_exact(AttnArgs A, const float* qn, float* scores, int sstride) {
+  pdl_wait();
   const int hd = A.hd, G = A.nh / A.nkv;
   const uint32_t pos = A.cur->pos;
   const uint32_t lo = (A.window > 0 && pos + 1 > (uint32_t)A.window) ? pos + 1 - A.window : 0;
@@ -183,6 +187,7 @@ __global__ void k_attn_scores_exact(AttnArgs A, const float* qn, float* scores, 
 // Softmax per head with the reference's order (model.rs:354-361): max, subtract, exp_fast,
 // sequential sum, multiply by 1/sum. One CTA per head.
 __global__ void k_attn_softmax_exact(AttnArgs A, float* scores, int sstride) {
+  pdl_wait();
   __shared__ float red[32];
   __shared__ float s_inv;
   const uint32_t pos = A.cur->pos;
@@ -208,6 +213,7 @@ __global__ void k_attn_softmax_exact(AttnArgs A, float* scores, int sstride) {
 // per = ceil(n_pos / threads); each range accumulates acc = fma(p, v, acc) in order; att = partials
 // summed in thread order. Then Act::quantize of the head's blocks. Grid (nh, hd / 32), block 32 * T.
 __global__ void k_attn_pv_exact(AttnArgs A, const float* scores, int sstride, int threads, int8_t* aq, float* as) {
+  pdl_wait();
   extern __shared__ float part[];  // [threads][32]
   const int hd = A.hd, G = A.nh / A.nkv, h = blockIdx.x, j0 = blockIdx.y * 32;
   const uint32_t pos = A.cur->pos;
@@ -238,6 +244,7 @@ __global__ void k_attn_pv_exact(AttnArgs A, const float* scores, int sstride, in
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
 __global__ void k_head_full_exact(HeadArgs H) {
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
@@ -557,7 +564,7 @@ void launch_gemv_exact(const MatView& w, const int8_t* aq, const float* as, cons
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_gemv_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_gemv_exact<B, S><<<blocks, kGemvThreads, sm, st>>>(w, aq, as, x, y);                          \
+    launch_k(k_gemv_exact<B, S>, dim3(blocks), dim3(kGemvThreads), sm, st, w, aq, as, x, y);        \
   } while (0)
   GEM_DISPATCH_X(w.bits, w.scale_f32, F);
 #undef F
@@ -565,20 +572,20 @@ void launch_gemv_exact(const MatView& w, const int8_t* aq, const float* as, cons
 
 void launch_residual_norm_quant_exact(float* x, const float* delta, const float* w_post, const float* w_pre, float eps,
                                       int d, int8_t* aq, float* as, float* xn_out, cudaStream_t st) {
-  k_residual_norm_quant_exact<<<1, 1024, (size_t)2 * d * 4, st>>>(x, delta, w_post, w_pre, eps, d, aq, as, xn_out);
+  launch_k(k_residual_norm_quant_exact, dim3(1), dim3(1024), (size_t)2 * d * 4, st, x, delta, w_post, w_pre, eps, d, aq, as, xn_out);
 }
 
 void launch_attn_exact(const AttnArgs& A, float* qn, float* scores, int sstride, int threads, int8_t* aq, float* as,
                        int sms, cudaStream_t st) {
   int G = A.nh / A.nkv;
-  k_attn_prep_exact<<<A.nkv, 256, (size_t)(G * A.hd + 2 * A.hd) * 4, st>>>(A, qn);
+  launch_k(k_attn_prep_exact, dim3(A.nkv), dim3(256), (size_t)(G * A.hd + 2 * A.hd) * 4, st, A, qn);
   int max_npos = A.window > 0 ? A.window : A.chunk * A.nsplit;
   int pairs = max_npos * A.nh;
   int blocks = min(sms * 4, max(1, (pairs * 2 + 255) / 256));
-  k_attn_scores_exact<<<blocks, 256, 0, st>>>(A, qn, scores, sstride);
-  k_attn_softmax_exact<<<A.nh, 256, 0, st>>>(A, scores, sstride);
+  launch_k(k_attn_scores_exact, dim3(blocks), dim3(256), 0, st, A, (const float*)qn, scores, sstride);
+  launch_k(k_attn_softmax_exact, dim3(A.nh), dim3(256), 0, st, A, scores, sstride);
   int tb = min(threads, 32) * 32;
-  k_attn_pv_exact<<<dim3(A.nh, A.hd / 32), tb, (size_t)threads * 32 * 4, st>>>(A, scores, sstride, threads, aq, as);
+  launch_k(k_attn_pv_exact, dim3(A.nh, A.hd / 32), dim3(tb), (size_t)threads * 32 * 4, st, A, (const float*)scores, sstride, threads, aq, as);
 }
 
 void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t st) {
@@ -589,7 +596,7 @@ void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t 
   do {                                                                                              \
     static bool init = false;                                                                       \
     if (!init) { cudaFuncSetAttribute(k_head_full_exact<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); init = true; } \
-    k_head_full_exact<B, S><<<grid, 512, sm, st>>>(H);                                              \
+    launch_k(k_head_full_exact<B, S>, grid, dim3(512), sm, st, H);                                    \
   } while (0)
   GEM_DISPATCH_X(H.w.bits, H.w.scale_f32, F);
 #undef F
