@@ -29,7 +29,7 @@ namespace gem {
 // 8 threads: lane i + lane i + 8 is partner o ^ 4, + 4 is o ^ 2, + 2 is o ^ 1, then the thread's own
 // two lanes.
 // ------------------------------------------------------------------------------------------------
-constexpr int kGemvThreads = 64, kGemvU = 16;
+constexpr int kGemvThreads = 64, kGemvU = 32;
 
 template <int BITS>
 __device__ __forceinline__ int load_word(const MatView& w, size_t r, int b, int o) {
