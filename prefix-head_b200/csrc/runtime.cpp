@@ -220,9 +220,33 @@ struct gem_model {
     }
   }
 
+  // Two-stream split of a single sequence's chunk (score_parallel): the second half of the positions
+  // runs on st2, one layer behind the first half. split_ev[l] marks the first half's layer-l
+  // attention (its K/V rows written); split_ev[nl] forks, split_ev[nl + 1] joins.
+  cudaStream_t st2 = nullptr;
+  std::vector<cudaEvent_t> split_ev;
+  void ensure_split() {
+    if (!st2) ck(cudaStreamCreateWithFlags(&st2, cudaStreamNonBlocking), "stream");
+    while ((int)split_ev.size() < nl + 2) {
+      cudaEvent_t e;
+      ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+      split_ev.push_back(e);
+    }
+  }
+  static bool split_on() {
+    static const bool on = [] {
+      const char* e = std::getenv("GEM_SPLIT");
+      return !(e && e[0] == '0');
+    }();
+    return on;
+  }
+
   ~gem_model() {
     if (st) cudaStreamSynchronize(st);
+    if (st2) cudaStreamSynchronize(st2);
     for (cudaEvent_t e : pev) cudaEventDestroy(e);
+    for (cudaEvent_t e : split_ev) cudaEventDestroy(e);
+    if (st2) cudaStreamDestroy(st2);
     if (comm) nccl().destroy(comm);
     for (auto& g : score_graph)
       if (g) cudaGraphExecDestroy(g);
@@ -544,32 +568,83 @@ struct gem_model {
         const int Lc = (int)std::min<size_t>(L, len - c0);
         T = Lc * ns;
         const uint32_t pos0 = base_pos + (uint32_t)c0;
-        launch_seq_gather_tokens(toks_d + (size_t)s0 * stride, stride, Lc, (int)c0, T, s_tin, s_tgt, st);
-        launch_seq_embed(E.v, s_tin, T, vocab, embed_scale, s_x, err, st);
+        // One sequence's chunk of 256 or more positions runs as two halves on two streams, the second
+        // half one layer behind: its layer-l attention waits for the first half's (which writes the
+        // K/V rows it reads); the first half reads no rows of the second. The halves' latency-bound
+        // kernels then overlap the other half's matrix products. Each position's arithmetic is the
+        // same. Buffers read and written at one width take row offsets; those used at several widths
+        // (s_y, s_aq, s_as) are split into two half-size slabs.
+        const bool split = ns == 1 && Lc >= 256 && Lc % 2 == 0 && !par_prof && split_on();
+        const int nh2 = split ? 2 : 1, Lh = Lc / nh2;
+        if (split) {
+          ensure_split();
+          ck(cudaEventRecord(split_ev[nl], st), "fork");
+          ck(cudaStreamWaitEvent(st2, split_ev[nl], 0), "fork");
+        }
+        const size_t ywide = std::max((size_t)qkv_rows, (size_t)d);
+        const size_t awide = std::max({(size_t)d, (size_t)nh * hd, (size_t)ff});
+        struct Half {
+          cudaStream_t s;
+          int r0, n;
+          float *x, *y, *gu, *dn, *qn, *sc, *part, *hx, *as, *has;
+          int8_t *aq, *haq;
+          uint32_t *tin, *tgt;
+        };
+        Half hv[2];
+        for (int k2 = 0; k2 < nh2; ++k2) {
+          Half& q = hv[k2];
+          const size_t r0 = (size_t)k2 * Lh;
+          q.s = k2 ? st2 : st, q.r0 = (int)r0, q.n = split ? Lh : T;
+          q.x = s_x + r0 * d, q.dn = s_dn + r0 * d, q.gu = s_gu + r0 * 2 * ff, q.qn = s_qn + r0 * nh * hd;
+          q.sc = s_scores + r0 * nh * seq_sstride, q.part = s_part + r0 * nh * ref_threads * hd;
+          q.hx = s_h + r0 * d, q.haq = s_haq + r0 * d, q.has = s_has + r0 * (d / 32);
+          q.tin = s_tin + r0, q.tgt = s_tgt + r0;
+          q.y = s_y + r0 * ywide, q.aq = s_aq + r0 * awide, q.as = s_as + r0 * (awide / 32);
+        }
+        for (int k2 = 0; k2 < nh2; ++k2) {
+          const Half& q = hv[k2];
+          const int Ln = split ? Lh : Lc;
+          launch_seq_gather_tokens(toks_d + (size_t)s0 * stride, stride, Ln, (int)c0 + q.r0, q.n, q.tin, q.tgt, q.s);
+          launch_seq_embed(E.v, q.tin, q.n, vocab, embed_scale, q.x, err, q.s);
+        }
         par_mark(PAR_EMBED);
         for (int l = 0; l < nl; ++l) {
           const Layer& Ly = layers[l];
           const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
-          launch_seq_norm(s_x, P ? s_dn : nullptr, P ? P->post_ffw : nullptr, Ly.attn_norm, eps, d, T, s_aq, s_as, nullptr, st);
-          par_mark(PAR_NORM);
-          launch_seq_gemm(Ly.qkv.v, s_aq, s_as, T, s_y, qkv_rows, sms, st);
-          par_mark(PAR_QKV);
-          launch_seq_attn(attn_args(l, 0), s_y, qkv_rows, Lc, ns, pos0, kv_stride, s_qn, s_scores, seq_sstride, ref_threads,
-                          s_part, s_aq, s_as, st);
-          par_mark(PAR_ATTN);
-          launch_seq_gemm(Ly.o.v, s_aq, s_as, T, s_y, d, sms, st);
-          par_mark(PAR_O);
-          launch_seq_norm(s_x, s_y, Ly.post_attn, Ly.ffn_norm, eps, d, T, s_aq, s_as, nullptr, st);
-          par_mark(PAR_NORM);
-          launch_seq_gemm(Ly.gu.v, s_aq, s_as, T, s_gu, 2 * ff, sms, st);
-          par_mark(PAR_GU);
-          launch_seq_glu_quant(s_gu, ff, T, silu ? 1 : 0, s_aq, s_as, sms, st);
-          par_mark(PAR_GLU);
-          launch_seq_gemm(Ly.down.v, s_aq, s_as, T, s_dn, d, sms, st);
-          par_mark(PAR_DOWN);
-          nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
+          for (int k2 = 0; k2 < nh2; ++k2) {
+            const Half& q = hv[k2];
+            const int Ln = split ? Lh : Lc;
+            launch_seq_norm(q.x, P ? q.dn : nullptr, P ? P->post_ffw : nullptr, Ly.attn_norm, eps, d, q.n, q.aq, q.as, nullptr,
+                            q.s);
+            par_mark(PAR_NORM);
+            launch_seq_gemm(Ly.qkv.v, q.aq, q.as, q.n, q.y, qkv_rows, sms, q.s);
+            par_mark(PAR_QKV);
+            if (k2 == 1) ck(cudaStreamWaitEvent(st2, split_ev[l], 0), "layer");
+            launch_seq_attn(attn_args(l, 0), q.y, qkv_rows, Ln, ns, pos0 + (uint32_t)q.r0, kv_stride, q.qn, q.sc,
+                            seq_sstride, ref_threads, q.part, q.aq, q.as, q.s);
+            if (split && k2 == 0) ck(cudaEventRecord(split_ev[l], st), "layer");
+            par_mark(PAR_ATTN);
+            launch_seq_gemm(Ly.o.v, q.aq, q.as, q.n, q.y, d, sms, q.s);
+            par_mark(PAR_O);
+            launch_seq_norm(q.x, q.y, Ly.post_attn, Ly.ffn_norm, eps, d, q.n, q.aq, q.as, nullptr, q.s);
+            par_mark(PAR_NORM);
+            launch_seq_gemm(Ly.gu.v, q.aq, q.as, q.n, q.gu, 2 * ff, sms, q.s);
+            par_mark(PAR_GU);
+            launch_seq_glu_quant(q.gu, ff, q.n, silu ? 1 : 0, q.aq, q.as, sms, q.s);
+            par_mark(PAR_GLU);
+            launch_seq_gemm(Ly.down.v, q.aq, q.as, q.n, q.dn, d, sms, q.s);
+            par_mark(PAR_DOWN);
+            nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
+          }
         }
-        launch_seq_norm(s_x, s_dn, layers[nl - 1].post_ffw, out_norm, eps, d, T, s_haq, s_has, s_h, st);
+        for (int k2 = 0; k2 < nh2; ++k2) {
+          const Half& q = hv[k2];
+          launch_seq_norm(q.x, q.dn, layers[nl - 1].post_ffw, out_norm, eps, d, q.n, q.haq, q.has, q.hx, q.s);
+        }
+        if (split) {  // the head reads both halves' final hidden states
+          ck(cudaEventRecord(split_ev[nl + 1], st2), "join");
+          ck(cudaStreamWaitEvent(st, split_ev[nl + 1], 0), "join");
+        }
         par_mark(PAR_NORM);
         if (which < 0) continue;  // prefill only: no head
         nk += 4 + seq_head(which, s_tgt, T, s_lp, s_am);
