@@ -424,13 +424,18 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
     roof = {"bound": "alu", "unit": "TOP/s", "achieved": round(achieved, 2), "peak": round(peak, 2),
             "peak_kind": f"derived: {sms} SMs x 128 lanes x {mhz:.0f} MHz / 3 instructions per int8 pair x 4 ops",
             "frac": round(achieved / peak, 4), "traffic": gemm_traffic(),
-            "kernel": "k_seq_gemm (4 launches per layer, 72 per step)", "ops_per_step": ops,
+            "kernel": "k_seq_gemm (4 launches per layer and sequence part)", "ops_per_step": ops,
+            "kernel_timing": "CUDA events around each launch group of a one-stream pass of the same step "
+                             "(profiling runs the sequence as one part; the timed step runs its parts' "
+                             "launches concurrently on their streams)",
             "kernel_ms_per_step": round(gemm_us / 1e3, 3), "share_of_step": round(gemm_us / 1e3 / ms_step, 3),
             "hbm_view": {"algorithmic_bytes_per_step": alg_bytes, "achieved_GB_s": round(alg_bytes / (ms_step * 1e-3) / 1e9, 1),
                          "peak": hbm, "peak_kind": hbm_kind},
             "tensor_view": {"bf16_peak_tflops": peaks().get("bf16_tflops"),
                             "note": "the reference's per-block fp32 FMA order cannot be reproduced by tensor-core accumulation"}}
-    sched = {"kind": "sequence-parallel (every position of the sequence through each layer together)",
+    sched = {"kind": "sequence-parallel (every position of the sequence through each layer together; the "
+                     "sequence in 4 parts of 128 positions on 4 streams, each part one layer behind the one "
+                     "before it)",
              "groups_us_per_step": prof}
     return roof, sched
 

@@ -220,33 +220,47 @@ struct gem_model {
     }
   }
 
-  // Two-stream split of a single sequence's chunk (score_parallel): the second half of the positions
-  // runs on st2, one layer behind the first half. split_ev[l] marks the first half's layer-l
-  // attention (its K/V rows written); split_ev[nl] forks, split_ev[nl + 1] joins.
-  cudaStream_t st2 = nullptr;
-  std::vector<cudaEvent_t> split_ev;
-  void ensure_split() {
-    if (!st2) ck(cudaStreamCreateWithFlags(&st2, cudaStreamNonBlocking), "stream");
-    while ((int)split_ev.size() < nl + 2) {
-      cudaEvent_t e;
-      ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
-      split_ev.push_back(e);
-    }
+  // Split of a single sequence's chunk into parts on their own streams (score_parallel): part k
+  // runs on split_st[k - 1] (part 0 on st), one layer behind part k - 1. split_ev[(k * nl) + l] marks
+  // part k's layer-l attention (its K/V rows written); fork_ev / join_ev[k] bracket the chunk.
+  static constexpr int kMaxParts = 8;
+  cudaStream_t split_st[kMaxParts - 1] = {};
+  std::vector<cudaEvent_t> split_ev, join_ev;
+  cudaEvent_t fork_ev = nullptr;
+  void ensure_split(int parts) {
+    for (int k = 0; k < parts - 1; ++k)
+      if (!split_st[k]) ck(cudaStreamCreateWithFlags(&split_st[k], cudaStreamNonBlocking), "stream");
+    auto more = [](std::vector<cudaEvent_t>& v, size_t n) {
+      while (v.size() < n) {
+        cudaEvent_t e;
+        ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+        v.push_back(e);
+      }
+    };
+    more(split_ev, (size_t)(parts - 1) * nl);
+    more(join_ev, (size_t)parts - 1);
+    if (!fork_ev) ck(cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming), "event");
   }
-  static bool split_on() {
-    static const bool on = [] {
+  // parts per single-sequence chunk (default 4): GEM_SPLIT=1 (or 0) runs one stream, 2..8 that many parts
+  static int split_parts() {
+    static const int n = [] {
       const char* e = std::getenv("GEM_SPLIT");
-      return !(e && e[0] == '0');
+      const int v = e ? std::atoi(e) : 4;
+      return std::max(1, std::min(kMaxParts, v));
     }();
-    return on;
+    return n;
   }
 
   ~gem_model() {
     if (st) cudaStreamSynchronize(st);
-    if (st2) cudaStreamSynchronize(st2);
+    for (cudaStream_t x : split_st)
+      if (x) cudaStreamSynchronize(x);
     for (cudaEvent_t e : pev) cudaEventDestroy(e);
     for (cudaEvent_t e : split_ev) cudaEventDestroy(e);
-    if (st2) cudaStreamDestroy(st2);
+    for (cudaEvent_t e : join_ev) cudaEventDestroy(e);
+    if (fork_ev) cudaEventDestroy(fork_ev);
+    for (cudaStream_t x : split_st)
+      if (x) cudaStreamDestroy(x);
     if (comm) nccl().destroy(comm);
     for (auto& g : score_graph)
       if (g) cudaGraphExecDestroy(g);
@@ -568,61 +582,60 @@ struct gem_model {
         const int Lc = (int)std::min<size_t>(L, len - c0);
         T = Lc * ns;
         const uint32_t pos0 = base_pos + (uint32_t)c0;
-        // One sequence's chunk of 256 or more positions runs as two halves on two streams, the second
-        // half one layer behind: its layer-l attention waits for the first half's (which writes the
-        // K/V rows it reads); the first half reads no rows of the second. The halves' latency-bound
-        // kernels then overlap the other half's matrix products. Each position's arithmetic is the
-        // same. Buffers read and written at one width take row offsets; those used at several widths
-        // (s_y, s_aq, s_as) are split into two half-size slabs.
-        const bool split = ns == 1 && Lc >= 256 && Lc % 2 == 0 && !par_prof && split_on();
-        const int nh2 = split ? 2 : 1, Lh = Lc / nh2;
-        if (split) {
-          ensure_split();
-          ck(cudaEventRecord(split_ev[nl], st), "fork");
-          ck(cudaStreamWaitEvent(st2, split_ev[nl], 0), "fork");
+        // One sequence's chunk runs as parts of at least 128 positions on their own streams, part k
+        // one layer behind part k - 1: its layer-l attention waits for part k - 1's (which writes the
+        // K/V rows it reads, after waiting for the parts before it); no part reads a later part's rows.
+        // The parts' latency-bound kernels then overlap the other parts' matrix products. Each
+        // position's arithmetic is the same. Buffers read and written at one width take row offsets;
+        // those used at several widths (s_y, s_aq, s_as) take offsets of whole rows of their widest use.
+        const int parts = (ns == 1 && !par_prof) ? std::max(1, std::min(split_parts(), Lc / 128)) : 1;
+        const int Lp = (Lc + parts - 1) / parts;
+        if (parts > 1) {
+          ensure_split(parts);
+          ck(cudaEventRecord(fork_ev, st), "fork");
+          for (int k = 0; k < parts - 1; ++k) ck(cudaStreamWaitEvent(split_st[k], fork_ev, 0), "fork");
         }
         const size_t ywide = std::max((size_t)qkv_rows, (size_t)d);
         const size_t awide = std::max({(size_t)d, (size_t)nh * hd, (size_t)ff});
-        struct Half {
+        struct Part {
           cudaStream_t s;
-          int r0, n;
+          int r0, n, L;
           float *x, *y, *gu, *dn, *qn, *sc, *part, *hx, *as, *has;
           int8_t *aq, *haq;
           uint32_t *tin, *tgt;
         };
-        Half hv[2];
-        for (int k2 = 0; k2 < nh2; ++k2) {
-          Half& q = hv[k2];
-          const size_t r0 = (size_t)k2 * Lh;
-          q.s = k2 ? st2 : st, q.r0 = (int)r0, q.n = split ? Lh : T;
+        Part hv[kMaxParts];
+        for (int k = 0; k < parts; ++k) {
+          Part& q = hv[k];
+          const size_t r0 = (size_t)k * Lp;
+          q.s = k ? split_st[k - 1] : st, q.r0 = (int)r0;
+          q.L = parts > 1 ? std::min(Lp, Lc - (int)r0) : Lc, q.n = parts > 1 ? q.L : T;
           q.x = s_x + r0 * d, q.dn = s_dn + r0 * d, q.gu = s_gu + r0 * 2 * ff, q.qn = s_qn + r0 * nh * hd;
           q.sc = s_scores + r0 * nh * seq_sstride, q.part = s_part + r0 * nh * ref_threads * hd;
           q.hx = s_h + r0 * d, q.haq = s_haq + r0 * d, q.has = s_has + r0 * (d / 32);
           q.tin = s_tin + r0, q.tgt = s_tgt + r0;
           q.y = s_y + r0 * ywide, q.aq = s_aq + r0 * awide, q.as = s_as + r0 * (awide / 32);
         }
-        for (int k2 = 0; k2 < nh2; ++k2) {
-          const Half& q = hv[k2];
-          const int Ln = split ? Lh : Lc;
-          launch_seq_gather_tokens(toks_d + (size_t)s0 * stride, stride, Ln, (int)c0 + q.r0, q.n, q.tin, q.tgt, q.s);
+        for (int k = 0; k < parts; ++k) {
+          const Part& q = hv[k];
+          launch_seq_gather_tokens(toks_d + (size_t)s0 * stride, stride, q.L, (int)c0 + q.r0, q.n, q.tin, q.tgt, q.s);
           launch_seq_embed(E.v, q.tin, q.n, vocab, embed_scale, q.x, err, q.s);
         }
         par_mark(PAR_EMBED);
         for (int l = 0; l < nl; ++l) {
           const Layer& Ly = layers[l];
           const Layer* P = l > 0 ? &layers[l - 1] : nullptr;
-          for (int k2 = 0; k2 < nh2; ++k2) {
-            const Half& q = hv[k2];
-            const int Ln = split ? Lh : Lc;
+          for (int k = 0; k < parts; ++k) {
+            const Part& q = hv[k];
             launch_seq_norm(q.x, P ? q.dn : nullptr, P ? P->post_ffw : nullptr, Ly.attn_norm, eps, d, q.n, q.aq, q.as, nullptr,
                             q.s);
             par_mark(PAR_NORM);
             launch_seq_gemm(Ly.qkv.v, q.aq, q.as, q.n, q.y, qkv_rows, sms, q.s);
             par_mark(PAR_QKV);
-            if (k2 == 1) ck(cudaStreamWaitEvent(st2, split_ev[l], 0), "layer");
-            launch_seq_attn(attn_args(l, 0), q.y, qkv_rows, Ln, ns, pos0 + (uint32_t)q.r0, kv_stride, q.qn, q.sc,
+            if (k > 0) ck(cudaStreamWaitEvent(q.s, split_ev[(size_t)(k - 1) * nl + l], 0), "layer");
+            launch_seq_attn(attn_args(l, 0), q.y, qkv_rows, q.L, ns, pos0 + (uint32_t)q.r0, kv_stride, q.qn, q.sc,
                             seq_sstride, ref_threads, q.part, q.aq, q.as, q.s);
-            if (split && k2 == 0) ck(cudaEventRecord(split_ev[l], st), "layer");
+            if (k + 1 < parts) ck(cudaEventRecord(split_ev[(size_t)k * nl + l], q.s), "layer");
             par_mark(PAR_ATTN);
             launch_seq_gemm(Ly.o.v, q.aq, q.as, q.n, q.y, d, sms, q.s);
             par_mark(PAR_O);
@@ -637,13 +650,13 @@ struct gem_model {
             nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
           }
         }
-        for (int k2 = 0; k2 < nh2; ++k2) {
-          const Half& q = hv[k2];
+        for (int k = 0; k < parts; ++k) {
+          const Part& q = hv[k];
           launch_seq_norm(q.x, q.dn, layers[nl - 1].post_ffw, out_norm, eps, d, q.n, q.haq, q.has, q.hx, q.s);
         }
-        if (split) {  // the head reads both halves' final hidden states
-          ck(cudaEventRecord(split_ev[nl + 1], st2), "join");
-          ck(cudaStreamWaitEvent(st, split_ev[nl + 1], 0), "join");
+        for (int k = 1; k < parts; ++k) {  // the head reads every part's final hidden states
+          ck(cudaEventRecord(join_ev[k - 1], split_st[k - 1]), "join");
+          ck(cudaStreamWaitEvent(st, join_ev[k - 1], 0), "join");
         }
         par_mark(PAR_NORM);
         if (which < 0) continue;  // prefill only: no head
