@@ -150,9 +150,10 @@ void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T,
 // x [T][cols], each the exact dot16; needs cols a multiple of 16 and a 16-byte aligned matrix.
 bool seq_head_f16_supported(const MatView& w);
 void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int ldy, cudaStream_t st);
+// `kv_written` (optional) is recorded on `st` once the chunk's K/V rows are in the cache.
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
                      float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
-                     cudaStream_t st);
+                     cudaStream_t st, cudaEvent_t kv_written = nullptr);
 void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
                                float* out, int* err, cudaStream_t st);
 void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st);

@@ -583,8 +583,8 @@ struct gem_model {
         T = Lc * ns;
         const uint32_t pos0 = base_pos + (uint32_t)c0;
         // One sequence's chunk runs as parts of at least 128 positions on their own streams, part k
-        // one layer behind part k - 1: its layer-l attention waits for part k - 1's (which writes the
-        // K/V rows it reads, after waiting for the parts before it); no part reads a later part's rows.
+        // behind part k - 1: its layer-l attention waits until part k - 1 has written its K/V rows of
+        // layer l (after waiting for the parts before it); no part reads a later part's rows.
         // The parts' latency-bound kernels then overlap the other parts' matrix products. Each
         // position's arithmetic is the same. Buffers read and written at one width take row offsets;
         // those used at several widths (s_y, s_aq, s_as) take offsets of whole rows of their widest use.
@@ -634,8 +634,8 @@ struct gem_model {
             par_mark(PAR_QKV);
             if (k > 0) ck(cudaStreamWaitEvent(q.s, split_ev[(size_t)(k - 1) * nl + l], 0), "layer");
             launch_seq_attn(attn_args(l, 0), q.y, qkv_rows, q.L, ns, pos0 + (uint32_t)q.r0, kv_stride, q.qn, q.sc,
-                            seq_sstride, ref_threads, q.part, q.aq, q.as, q.s);
-            if (k + 1 < parts) ck(cudaEventRecord(split_ev[(size_t)k * nl + l], q.s), "layer");
+                            seq_sstride, ref_threads, q.part, q.aq, q.as, q.s,
+                            k + 1 < parts ? split_ev[(size_t)k * nl + l] : nullptr);
             par_mark(PAR_ATTN);
             launch_seq_gemm(Ly.o.v, q.aq, q.as, q.n, q.y, d, sms, q.s);
             par_mark(PAR_O);

@@ -1072,10 +1072,11 @@ void launch_seq_head_f16(const MatView& w, const float* x, int T, float* y, int 
 
 void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int nseq, uint32_t pos0, size_t kv_stride,
                      float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
-                     cudaStream_t st) {
+                     cudaStream_t st, cudaEvent_t kv_written) {
   const int G = A.nh / A.nkv, T = L * nseq;
   if (G < 1 || G > 8) return;  // rejected by the caller before any launch
   launch_k(k_seq_attn_prep, dim3(dim3(T, A.nkv)), dim3(256), (size_t)(G + 2) * A.hd * 4, st, A, qkv, qkv_ld, L, pos0, kv_stride, qn);
+  if (kv_written) cudaEventRecord(kv_written, st);  // the chunk's K/V rows are in the cache
   const uint32_t pbase = window_lo(pos0, A.window);
   const int nchunk = (int)((pos0 + L - pbase + kScKC - 1) / kScKC);
   const int tps = (L + kAttnTQ - 1) / kAttnTQ;
