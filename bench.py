@@ -428,7 +428,8 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
             "kernel_timing": "CUDA events around each launch group of a one-stream pass of the same step "
                              "(profiling runs the sequence as one part; the timed step runs its parts' "
                              "launches concurrently on their streams)",
-            "kernel_ms_per_step": round(gemm_us / 1e3, 3), "share_of_step": round(gemm_us / 1e3 / ms_step, 3),
+            "kernel_ms_per_step": round(gemm_us / 1e3, 3),
+            "share_of_step": round(gemm_us / max(1e-9, sum(prof.values())), 3),  # of the one-part profiled step
             "hbm_view": {"algorithmic_bytes_per_step": alg_bytes, "achieved_GB_s": round(alg_bytes / (ms_step * 1e-3) / 1e9, 1),
                          "peak": hbm, "peak_kind": hbm_kind},
             "tensor_view": {"bf16_peak_tflops": peaks().get("bf16_tflops"),
