@@ -144,8 +144,9 @@ void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, 
 void launch_seq_norm(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d, int T,
                      int8_t* aq, float* as, float* xn_out, cudaStream_t st);
 bool seq_gemm_supported(const MatView& w);
+// `concurrent`: how many such products run at once on separate streams (tile choice).
 void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
-                     cudaStream_t st);
+                     cudaStream_t st, int concurrent = 1);
 // Full-head logits y[p][r] (p < T, row stride ldy) of an F16 output matrix against fp32 hidden states
 // x [T][cols], each the exact dot16; needs cols a multiple of 16 and a 16-byte aligned matrix.
 bool seq_head_f16_supported(const MatView& w);

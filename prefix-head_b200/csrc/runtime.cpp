@@ -630,22 +630,22 @@ struct gem_model {
             launch_seq_norm(q.x, P ? q.dn : nullptr, P ? P->post_ffw : nullptr, Ly.attn_norm, eps, d, q.n, q.aq, q.as, nullptr,
                             q.s);
             par_mark(PAR_NORM);
-            launch_seq_gemm(Ly.qkv.v, q.aq, q.as, q.n, q.y, qkv_rows, sms, q.s);
+            launch_seq_gemm(Ly.qkv.v, q.aq, q.as, q.n, q.y, qkv_rows, sms, q.s, parts);
             par_mark(PAR_QKV);
             if (k > 0) ck(cudaStreamWaitEvent(q.s, split_ev[(size_t)(k - 1) * nl + l], 0), "layer");
             launch_seq_attn(attn_args(l, 0), q.y, qkv_rows, q.L, ns, pos0 + (uint32_t)q.r0, kv_stride, q.qn, q.sc,
                             seq_sstride, ref_threads, q.part, q.aq, q.as, q.s,
                             k + 1 < parts ? split_ev[(size_t)k * nl + l] : nullptr);
             par_mark(PAR_ATTN);
-            launch_seq_gemm(Ly.o.v, q.aq, q.as, q.n, q.y, d, sms, q.s);
+            launch_seq_gemm(Ly.o.v, q.aq, q.as, q.n, q.y, d, sms, q.s, parts);
             par_mark(PAR_O);
             launch_seq_norm(q.x, q.y, Ly.post_attn, Ly.ffn_norm, eps, d, q.n, q.aq, q.as, nullptr, q.s);
             par_mark(PAR_NORM);
-            launch_seq_gemm(Ly.gu.v, q.aq, q.as, q.n, q.gu, 2 * ff, sms, q.s);
+            launch_seq_gemm(Ly.gu.v, q.aq, q.as, q.n, q.gu, 2 * ff, sms, q.s, parts);
             par_mark(PAR_GU);
             launch_seq_glu_quant(q.gu, ff, q.n, silu ? 1 : 0, q.aq, q.as, sms, q.s);
             par_mark(PAR_GLU);
-            launch_seq_gemm(Ly.down.v, q.aq, q.as, q.n, q.dn, d, sms, q.s);
+            launch_seq_gemm(Ly.down.v, q.aq, q.as, q.n, q.dn, d, sms, q.s, parts);
             par_mark(PAR_DOWN);
             nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
           }

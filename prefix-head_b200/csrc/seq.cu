@@ -1008,12 +1008,16 @@ bool seq_gemm_supported(const MatView& w) {
 // T positions: the fewest estimated wave-times, a wave of RN = 8 (2 CTAs per SM) taking 8 units and a
 // wave of RN = 4 or 6 (3 CTAs per SM) 1.55 units per position of RN (measured: the three shapes give
 // the same throughput per SM when their last wave is full).
-static int gemm_rn(int rows, int T, int sms) {
+// With `concurrent` products running at once (a chunk's parts on their streams), the other parts
+// fill the SMs a small grid leaves idle, so the most efficient tile per position (RN = 8) wins:
+// measured 102.5k against 101.7k tokens/s for the cost model's choice at 4 parts of 128 positions.
+static int gemm_rn(int rows, int T, int sms, int concurrent) {
   static const int forced = [] {  // tuning override: GEM_GEMM_RN=4, 6 or 8
     const char* e = std::getenv("GEM_GEMM_RN");
     return e ? std::atoi(e) : 0;
   }();
   if (forced == 4 || forced == 6 || forced == 8) return forced;
+  if (concurrent > 1) return 8;
   const long long rt = (rows + kGemmBM - 1) / kGemmBM;
   auto cost = [&](int rn, int occ, double unit) {
     const long long ctas = (long long)((T + 4 * rn - 1) / (4 * rn)) * rt;
@@ -1025,8 +1029,8 @@ static int gemm_rn(int rows, int T, int sms) {
 }
 
 void launch_seq_gemm(const MatView& w, const int8_t* aq, const float* as, int T, float* y, int ldy, int sms,
-                     cudaStream_t st) {
-  const int rn = gemm_rn(w.rows, T, sms);
+                     cudaStream_t st, int concurrent) {
+  const int rn = gemm_rn(w.rows, T, sms, concurrent);
 #define F2(B, S, RNV)                                                                                            \
   do {                                                                                                          \
     using GT = GemmTile<B, S, RNV>;                                                                             \
