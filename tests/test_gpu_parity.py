@@ -348,3 +348,70 @@ def test_head_full_f16_batches(torch, isa, threads, f16_head, batch):
         assert abs(lp[b] - want[0]) < 2e-5, (b, lp[b], want[0])
         assert am[b] == want[1], b
     g.close()
+
+
+@pytest.mark.parametrize("which", [-1, 0, 6])
+def test_matvec_q4_f16_bit_exact(torch, isa, f16_head, which):
+    """The per-token exact GEMV on a Q4_0 body matrix (11 blocks per row: f32 scales) and on an F16
+    output matrix (dot16), bit for bit against the oracle's AVX-512 rows."""
+    g = Gemma(f16_head, ctx=64)
+    name = "token_embd.weight" if which < 0 else f"blk.1.{NAMES[which]}.weight"
+    m = _gguf_mat(f16_head, name)
+    x = np.random.default_rng(140 + which).standard_normal(m.cols).astype(np.float32)
+    xd = torch.tensor(x, device="cuda")
+    yd = torch.empty(m.rows, device="cuda")
+    g.matvec_dev(1 if which >= 0 else -1, max(which, 0), xd.data_ptr(), yd.data_ptr())
+    assert np.array_equal(yd.cpu().numpy().view(np.uint32), m.matvec(x, "avx512", threads=1).view(np.uint32))
+    g.close()
+
+
+def test_sequential_q4_body_f16_head(torch, isa, f16_head):
+    """The per-token schedule on a Q4_0 body with an F16 output matrix, against the oracle."""
+    from gem_b200 import SEQUENTIAL
+    g = Gemma(f16_head, ctx=64)
+    g.set_schedule(SEQUENTIAL)
+    o = orc.Model(f16_head, ctx=64, threads=REF_THREADS, isa="avx512")
+    toks = synth.tokens(30, g.vocab, seed=150)
+    lp, am = g.score(toks, FULL)
+    lpo, amo, _, _ = o.score(toks, FULL)
+    assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo), np.abs(lp - lpo).max()
+    g.close()
+
+
+_PARTS_SCRIPT = """
+import sys, numpy as np
+from gem_b200 import FULL, TWO_LEVEL, Gemma, synth
+g = Gemma(sys.argv[1], ctx=600)
+g.load_twolevel(sys.argv[2])
+toks = synth.tokens(513, g.vocab, seed=160)
+lp, am = g.score(toks, TWO_LEVEL)
+lpf, amf = g.score(toks, FULL)
+np.savez(sys.argv[3], lp=lp, am=am, lpf=lpf, amf=amf)
+"""
+
+
+@pytest.mark.parametrize("parts", [1, 2, 3])
+def test_parallel_parts_agree(torch, small, tmp_path, parts):
+    """512 positions scored in 1, 2 or 3 parts (uneven: 171 + 171 + 170 positions) give bit-identical
+    log-probs and argmax ids to the default 4 parts of 128: the parts change only which stream runs
+    which positions. The part count is read once per process, so the other counts run in child
+    processes."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    out = tmp_path / f"parts{parts}.npz"
+    env = dict(os.environ, GEM_SPLIT=str(parts),
+               PYTHONPATH=os.pathsep.join([str(root / "prefix-head_b200"), str(root)]))
+    subprocess.run([sys.executable, "-c", _PARTS_SCRIPT, str(small.gguf), str(small.twolevel), str(out)], env=env,
+                   check=True, timeout=600)
+    got = np.load(out)
+    g = Gemma(small.gguf, ctx=600)
+    g.load_twolevel(small.twolevel)
+    toks = synth.tokens(513, g.vocab, seed=160)
+    lp, am = g.score(toks, TWO_LEVEL)
+    lpf, amf = g.score(toks, FULL)
+    assert np.array_equal(lp.view(np.uint32), got["lp"].view(np.uint32)) and np.array_equal(am, got["am"])
+    assert np.array_equal(lpf.view(np.uint32), got["lpf"].view(np.uint32)) and np.array_equal(amf, got["amf"])
+    g.close()
