@@ -418,35 +418,7 @@ __global__ void k_head_full(HeadArgs H) {
 
 __global__ void k_head_full_merge(HeadArgs H, int nparts) {
   pdl_wait();
-  __shared__ float red_m[32], red_s[32], red_v[32];
-  __shared__ uint32_t red_t[32];
-  const int bi = blockIdx.x;
-  Lse L{-INFINITY, 0.0f};
-  Best B{-INFINITY, 0xffffffffu};
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
-    float4 p = ((const float4*)H.part)[(size_t)bi * nparts + i];
-    L = lse_merge(L, Lse{p.x, p.y});
-    B = best_merge(B, Best{p.z, __float_as_uint(p.w)});
-  }
-  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int o = 16; o > 0; o >>= 1) {
-    Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
-    Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
-    L = lse_merge(L, l2);
-    B = best_merge(B, b2);
-  }
-  if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int i = 1; i < nw; ++i) {
-      L = lse_merge(L, Lse{red_m[i], red_s[i]});
-      B = best_merge(B, Best{red_v[i], red_t[i]});
-    }
-    float lse = L.m + logf(L.s);
-    uint32_t slot = H.targets ? (uint32_t)bi : H.cur->slot;
-    if (H.lp_out) H.lp_out[slot] = H.tlogit[bi] - lse;
-    if (H.am_out) H.am_out[slot] = B.tok;
-  }
+  head_merge(H, blockIdx.x, nparts);
 }
 
 // ------------------------------------------------------------------------------------------------

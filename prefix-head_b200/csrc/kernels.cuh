@@ -79,7 +79,45 @@ struct HeadArgs {
   float* lp_out;             // indexed by batch item, or cur->slot
   uint32_t* am_out;
   int* err;                  // device error word
+  int* cnt;                  // [batch] streamed-head CTAs done (zero between launches; the last CTA
+                             // merges the partials), or null for the separate merge kernel
 };
+
+#ifdef __CUDACC__
+// Log-sum-exp, argmax and log-prob of batch item bi from `nparts` per-CTA partials (max, sum of
+// exp, best logit, its token), merged by the calling CTA in a fixed order (strided per thread, then
+// the warp tree, then the warps in order), so the result does not depend on which CTA runs it.
+__device__ inline void head_merge(const HeadArgs& H, int bi, int nparts) {
+  __shared__ float red_m[32], red_s[32], red_v[32];
+  __shared__ uint32_t red_t[32];
+  Lse L{-INFINITY, 0.0f};
+  Best B{-INFINITY, 0xffffffffu};
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+    const float4 p = __ldcg((const float4*)H.part + (size_t)bi * nparts + i);
+    L = lse_merge(L, Lse{p.x, p.y});
+    B = best_merge(B, Best{p.z, __float_as_uint(p.w)});
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
+    Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
+    L = lse_merge(L, l2);
+    B = best_merge(B, b2);
+  }
+  if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < nw; ++i) {
+      L = lse_merge(L, Lse{red_m[i], red_s[i]});
+      B = best_merge(B, Best{red_v[i], red_t[i]});
+    }
+    const float lse = L.m + logf(L.s);
+    const uint32_t slot = H.targets ? (uint32_t)bi : H.cur->slot;
+    if (H.lp_out) H.lp_out[slot] = __ldcg(H.tlogit + bi) - lse;
+    if (H.am_out) H.am_out[slot] = B.tok;
+  }
+}
+#endif
 
 struct TwoLevelArgs {
   MatView w;                 // class-permuted output matrix: class c = rows [c*per, c*per + n_c)

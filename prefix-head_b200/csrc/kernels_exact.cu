@@ -374,8 +374,13 @@ __global__ void __launch_bounds__(G * 32) k_head_full_bulk(HeadArgs H, const uns
     for (int k = 0; k < NS; ++k)
       if ((int)(blockIdx.x + k * gridDim.x) < nst) issue(blockIdx.x + k * gridDim.x, k);
   pdl_wait();
-  for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)(H.aq + (size_t)bi * w.cols))[j];
-  for (int j = threadIdx.x; j < nb; j += blockDim.x) sas[j] = H.as[(size_t)bi * nb + j];
+  if (H.aq) {
+    for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)(H.aq + (size_t)bi * w.cols))[j];
+    for (int j = threadIdx.x; j < nb; j += blockDim.x) sas[j] = H.as[(size_t)bi * nb + j];
+  } else {  // Act::quantize of the fp32 hidden state here (q8.rs:187-246), a warp per 32-block
+    for (int b = warp; b < nb; b += G)
+      quant_block_warp_x(H.h[(size_t)bi * w.cols + b * 32 + lane], lane, saq + b * 32, sas + b);
+  }
   __syncthreads();
   uint32_t target = H.targets ? H.targets[bi] : H.cur->target;
   if (target >= (uint32_t)w.rows) {
@@ -424,7 +429,9 @@ __global__ void __launch_bounds__(G * 32) k_head_full_bulk(HeadArgs H, const uns
     B = best_merge(B, b2);
   }
   if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
+  if (H.cnt) __threadfence();  // this thread's target-logit store is visible before the CTA counts itself
   __syncthreads();
+  __shared__ int s_last;
   if (threadIdx.x == 0) {
     for (int j = 1; j < G; ++j) {
       L = lse_merge(L, Lse{red_m[j], red_s[j]});
@@ -432,6 +439,17 @@ __global__ void __launch_bounds__(G * 32) k_head_full_bulk(HeadArgs H, const uns
     }
     float4* p = (float4*)(H.part + ((size_t)bi * gridDim.x + blockIdx.x) * 4);
     *p = make_float4(L.m, L.s, B.v, __uint_as_float(B.tok));
+    s_last = 0;
+    if (H.cnt) {  // the partial before the count
+      __threadfence();
+      s_last = atomicAdd(H.cnt + bi, 1) == (int)gridDim.x - 1;
+    }
+  }
+  __syncthreads();
+  if (s_last) {  // every CTA's partial is written: merge them here instead of in a separate kernel
+    __threadfence();
+    head_merge(H, bi, gridDim.x);
+    if (threadIdx.x == 0) H.cnt[bi] = 0;  // ready for the next launch
   }
 }
 
@@ -463,7 +481,7 @@ void launch_head_full_bulk(const HeadArgs& H, const unsigned char* wq, const __h
     if (!init) { cudaFuncSetAttribute(k_head_full_bulk<4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024); init = true; }
     launch_k(k_head_full_bulk<4, 2>, grid, dim3(128), sm, st, H, wq, ws, ng);
   }
-  launch_head_full_merge(H, batch, ctas, st);
+  if (!H.cnt) launch_head_full_merge(H, batch, ctas, st);
 }
 
 // Two-level stage 1, exact: class logits dot512(A[c], h) + b[c] (main.rs:82-93) and the target

@@ -135,6 +135,7 @@ struct gem_model {
   // heads
   int hbatch = 0;
   float *head_part = nullptr, *tlogit = nullptr, *cl = nullptr, *inner = nullptr;
+  int* head_cnt = nullptr;  // the streamed full head's finished-CTA counters, one per batch item
   int8_t* hb_q = nullptr;  // batched head calls: quantized hidden states [batch][d] and their scales
   float* hb_s = nullptr;
   // two-level (main.rs:40-51)
@@ -288,6 +289,8 @@ struct gem_model {
     int parts = head_full_parts(sms);
     head_part = alloc<float>((size_t)batch * parts * 4);
     tlogit = alloc<float>(batch);
+    head_cnt = alloc<int>(batch);  // the streamed head's finished-CTA counters: zero between launches
+    ck(cudaMemsetAsync(head_cnt, 0, (size_t)batch * sizeof(int), st), "head counters");
     hb_q = alloc<int8_t>((size_t)batch * d);
     hb_s = alloc<float>((size_t)batch * d / 32);
     if (two) {
@@ -380,6 +383,7 @@ struct gem_model {
     if (which == 0) {
       HeadArgs H = head_args(qa, sa, hh, targets, lpo, amo);
       if (exact && head_bulk_q) {
+        H.cnt = head_cnt;  // the last CTA merges; with qa null each CTA quantizes hh itself
         launch_head_full_bulk(H, head_bulk_q, head_bulk_s, batch, sms, st);
       } else if (exact) {
         launch_head_full_exact(H, batch, sms, st);
@@ -1738,13 +1742,16 @@ static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_
   if (which == 1 && !m->two) throw Error(GEM_E_STATE, "two-level head not loaded");
   ck(cudaSetDevice(m->device), "cudaSetDevice");
   m->ensure_head_batch(batch);  // the quantized hidden states live in the model's head scratch
-  launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
   // from kHeadGemmMin hidden states on, the full head is cheaper as a matrix product (the output
   // matrix read once per 256 states) than as one streamed pass over it per state
-  if (which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && m->full_head_gemm_supported())
+  const bool product = which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && m->full_head_gemm_supported();
+  const bool streamed = which == 0 && m->exact && m->head_bulk_q && !product;  // quantizes in its own CTAs
+  if (!streamed) launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
+  if (product)
     m->full_head_gemm(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   else
-    m->run_head(which, m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
+    m->run_head(which, streamed ? nullptr : m->hb_q, streamed ? nullptr : m->hb_s, h_dev, targets_dev, batch, lp_dev,
+                am_dev);
   m->check_launch();
   API_END
 }
