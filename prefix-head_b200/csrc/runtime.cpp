@@ -332,7 +332,16 @@ struct gem_model {
   void enqueue_body(int seq) {
     const DevMat& E = untied ? emb : head;
     launch_embed(E.v, nullptr, cur, embed_scale, x, st);
-    auto norm = exact ? launch_residual_norm_quant_exact : launch_residual_norm_quant;
+    // exact numerics with d <= 1152 in 32-blocks: the parallel schedule's norm kernel for one position
+    // (one warp, the sequential sums fed by prefetched loads, quantization from registers), the same
+    // arithmetic as the single-CTA per-token kernel
+    const bool warp_norm = exact && d <= 1152 && d % 32 == 0;
+    auto norm = [&](float* xx, const float* delta, const float* w_post, const float* w_pre, float e, int n, int8_t* aq,
+                    float* as, float* xn_out, cudaStream_t s) {
+      if (warp_norm) launch_seq_norm(xx, delta, w_post, w_pre, e, n, 1, aq, as, xn_out, s);
+      else (exact ? launch_residual_norm_quant_exact : launch_residual_norm_quant)(xx, delta, w_post, w_pre, e, n, aq, as,
+                                                                                   xn_out, s);
+    };
     auto gemv = exact ? launch_gemv_exact : launch_gemv;
     for (int l = 0; l < nl; ++l) {
       const Layer& L = layers[l];
