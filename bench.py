@@ -179,7 +179,8 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
         "config": {"workload": "gemma3-270m Q8_0, two-level head 2048x128, batch 1, 512 random tokens per step",
-                   "model": "gemma3-270m geometry, random init N(0,0.02)", "global_batch": 1, "seq_len": SEQ_TOKENS,
+                   "geometry": "gemma3-270m (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "
+                               "random init N(0,0.02) quantized to Q8_0", "global_batch": 1, "seq_len": SEQ_TOKENS,
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "isa": m.isa, "sample": f"{args.steps} x {SEQ_TOKENS}-token sequences"},
@@ -252,7 +253,7 @@ def run_vocab_shard(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)",
             "data": "synthetic", "numerics": "exact",
             "config": {"workload": "gemma3-1b Q8_0, one 1024-position sequence per step, full head sharded by vocab rows",
-                       "model": "gemma3-1b geometry (d 1152, 26 layers, 4q/1kv heads, hd 256, ff 6912, vocab 262144), "
+                       "geometry": "gemma3-1b (d 1152, 26 layers, 4q/1kv heads, hd 256, ff 6912, vocab 262144), "
                                 "random init N(0,0.02) quantized to Q8_0",
                        "global_batch": 1, "seq_len": n, "parallelism": f"vocab shard x{world} (body replicated)",
                        "rows_per_rank": rows, "l2": "flushed (256 MiB write) before every step"},
@@ -367,7 +368,7 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
             "numerics": args.numerics,
             "config": {"workload": "gemma3-270m Q8_0, two-level head 2048x128, batch 1, 512 random tokens per step",
-                       "model": "gemma3-270m geometry (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "
+                       "geometry": "gemma3-270m (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "
                                 "random init N(0,0.02) quantized to Q8_0",
                        "global_batch": world, "seq_len": SEQ_TOKENS, "parallelism": f"dp{world} (one sequence per GPU)",
                        "l2": "flushed (256 MiB write) before every step"},

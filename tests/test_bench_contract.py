@@ -1,0 +1,38 @@
+"""bench.py's reference arm prints the JSON line a benchmark driver reads.
+
+The arm times the oracle (the CPU restatement of gem's scoring path) on the host cores, so this runs
+without a GPU: one bounded step of the 270M two-level workload in a child process, then checks the
+base keys, a cpu_baseline describing the run, and an e2e with no host-device copies."""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+BASE_KEYS = ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+             "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e")
+
+
+def test_reference_arm_json_line():
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([str(ROOT / "prefix-head_b200"), str(ROOT)]))
+    env.pop("RANK", None)
+    env.pop("WORLD_SIZE", None)
+    run = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "0"],
+                         cwd=ROOT, env=env, capture_output=True, text=True, timeout=900)
+    assert run.returncode == 0, run.stderr[-2000:]
+    lines = [ln for ln in run.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, run.stdout[-2000:]
+    d = json.loads(lines[0])
+    for k in BASE_KEYS:
+        assert k in d, k
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 0
+    assert d["config"]["workload"] and "model" not in d["config"]
+    cb = d["cpu_baseline"]
+    assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
+    assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
+    e = d["e2e"]
+    assert e["value"] == d["value"] and e["unit"] == d["unit"]
+    assert e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
