@@ -103,15 +103,16 @@ constexpr int kNormMaxV = 9;  // float4 per lane: d <= 1152
 __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const float* delta, const float* w_post,
                                                               const float* w_pre, float eps, int d, int T, int8_t* aq,
                                                               float* as, float* xn_out) {
-  pdl_wait();
   extern __shared__ __align__(16) float sn[];  // w_post [d], w_pre [d], then per warp [2 d] (sq in the second half)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, n4 = d / 4;
   float* swpost = sn;
   float* swpre = sn + d;
+  // the norm weights depend on no earlier kernel: they load while the previous kernel drains
   for (int i = threadIdx.x; i < n4; i += blockDim.x) {
     ((float4*)swpre)[i] = ((const float4*)w_pre)[i];
     if (w_post) ((float4*)swpost)[i] = ((const float4*)w_post)[i];
   }
+  pdl_wait();
   __syncthreads();
   const int t = blockIdx.x * kNormWarps + warp;
   if (t >= T) return;
