@@ -97,15 +97,15 @@ def small_qwen2(model_dir):
     return synth.ensure("small-qwen2", classes=64, directory=model_dir)
 
 
-def test_oracle_qwen2_forward_matches_transformers(small_qwen2, threads):
-    """The qwen2 branch (model.rs:160-161, 188-190, 311-315, 400-407: q/k/v biases, SiLU, untied output,
-    no embedding scale, every layer global) against transformers' Qwen2 on the same weights."""
+def qwen2_logprobs(files, toks):
+    """transformers' Qwen2ForCausalLM on the dequantized weights of a synthetic qwen2 GGUF: the log-prob
+    of toks[i + 1] after toks[:i + 1] for every i < len(toks) - 1."""
     torch = pytest.importorskip("torch")
     tr = pytest.importorskip("transformers")
     import gguf
     from gguf import quants
-    cfg = small_qwen2.cfg
-    r = gguf.GGUFReader(str(small_qwen2.gguf))
+    cfg = files.cfg
+    r = gguf.GGUFReader(str(files.gguf))
     T = {t.name: t for t in r.tensors}
 
     def deq(name):
@@ -133,12 +133,17 @@ def test_oracle_qwen2_forward_matches_transformers(small_qwen2, threads):
     m = tr.Qwen2ForCausalLM(c).float().eval()
     missing, unexpected = m.load_state_dict(sd, strict=False)
     assert not unexpected and all("rotary" in k for k in missing), (missing, unexpected)
-    n = 40
-    toks = synth.tokens(n + 1, cfg["vocab"], seed=9)
-    o = orc.Model(small_qwen2.gguf, ctx=128, threads=threads)
-    lp, _, _, _ = o.score(toks, 0)
+    n = len(toks) - 1
     with torch.no_grad():
         lg = m(torch.tensor(toks[None, :n].astype(np.int64))).logits[0].double()
-    want = torch.log_softmax(lg, -1)[torch.arange(n), torch.tensor(toks[1:n + 1].astype(np.int64))].numpy()
-    d = np.abs(lp - want)
+    return torch.log_softmax(lg, -1)[torch.arange(n), torch.tensor(toks[1:n + 1].astype(np.int64))].numpy()
+
+
+def test_oracle_qwen2_forward_matches_transformers(small_qwen2, threads):
+    """The qwen2 branch (model.rs:160-161, 188-190, 311-315, 400-407: q/k/v biases, SiLU, untied output,
+    no embedding scale, every layer global) against transformers' Qwen2 on the same weights."""
+    toks = synth.tokens(41, small_qwen2.cfg["vocab"], seed=9)
+    o = orc.Model(small_qwen2.gguf, ctx=128, threads=threads)
+    lp, _, _, _ = o.score(toks, 0)
+    d = np.abs(lp - qwen2_logprobs(small_qwen2, toks))
     assert d.max() < 0.05 and d.mean() < 0.015, (d.max(), d.mean())
