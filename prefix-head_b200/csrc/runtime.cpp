@@ -194,6 +194,43 @@ struct gem_model {
         cudaGraphExecDestroy(g);
         g = nullptr;
       }
+    drop_par_graph();
+    par_seen = false;
+  }
+  // The parallel schedule of one sequence as a CUDA graph (score_parallel): the arguments it was
+  // captured with, including the count of device allocations made before it (scratch that grows
+  // moves, and the graph holds its addresses).
+  struct ParKey {
+    const uint32_t* toks;
+    size_t stride, len;
+    int which, parts;
+    uint32_t base;
+    float* lp;
+    uint32_t* am;
+    int64_t gen;
+    bool operator==(const ParKey& o) const {
+      return toks == o.toks && stride == o.stride && len == o.len && which == o.which && parts == o.parts &&
+             base == o.base && lp == o.lp && am == o.am && gen == o.gen;
+    }
+  };
+  cudaGraphExec_t par_graph = nullptr;
+  ParKey par_key{};
+  bool par_seen = false;  // par_key holds the arguments of the last direct call
+  int64_t par_nk = 0;
+  int64_t alloc_gen = 0;
+  void drop_par_graph() {
+    if (par_graph) {
+      cudaGraphExecDestroy(par_graph);
+      par_graph = nullptr;
+    }
+  }
+  // GEM_PAR_GRAPH=0 launches every parallel-schedule call directly
+  static bool par_graph_enabled() {
+    static const bool on = [] {
+      const char* e = std::getenv("GEM_PAR_GRAPH");
+      return !(e && std::atoi(e) == 0);
+    }();
+    return on;
   }
   bool have_h = false;
   // generation-side heads (decode.cu): per-call scratch, grown on demand
@@ -265,6 +302,7 @@ struct gem_model {
     if (comm) nccl().destroy(comm);
     for (auto& g : score_graph)
       if (g) cudaGraphExecDestroy(g);
+    if (par_graph) cudaGraphExecDestroy(par_graph);
     for (void* p : owned) cudaFree(p);
     if (cur_host) cudaFreeHost(cur_host);
     if (st) cudaStreamDestroy(st);
@@ -274,12 +312,14 @@ struct gem_model {
   T* alloc(size_t n) {
     T* p = dev_alloc<T>(n);
     owned.push_back(p);
+    ++alloc_gen;
     return p;
   }
   template <typename T>
   T* upload(const std::vector<T>& v) {
     T* p = dev_upload(v);
     owned.push_back(p);
+    ++alloc_gen;
     return p;
   }
   float* upload_or_null(const std::vector<float>& v) { return v.empty() ? nullptr : upload(v); }
@@ -568,8 +608,62 @@ struct gem_model {
   // sequences of len + 1 ids, `stride` ids apart; sequence s's log-probs of ids 1..len go to
   // lp_d[s * len ..] (argmax likewise). A chunk holds up to kBatchRows positions of whole sequences
   // (each in its own KV slot) or kSeqChunk positions of one long sequence.
+  // One sequence's call repeated with the same arguments (the scoring loop of a benchmark or a
+  // service: same buffers, new token ids) replays a CUDA graph of its ~900 launches: the first call
+  // launches them directly, the second is captured and replayed, later ones replay. The graph reads
+  // the token ids and writes the outputs through the same device pointers, so only their contents
+  // may change between calls; profiling, batches and the vocab-sharded head launch directly.
   void score_parallel(const uint32_t* toks_d, size_t stride, int nseq, size_t len, int which, uint32_t base_pos,
                       float* lp_d, uint32_t* am_d) {
+    if (nseq != 1 || par_prof || comm || !par_graph_enabled()) {
+      drop_par_graph();
+      par_seen = false;
+      score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
+      return;
+    }
+    ParKey key{toks_d, stride, len, which, split_parts(), base_pos, lp_d, am_d, alloc_gen};
+    if (par_graph && key == par_key) {
+      ck(cudaGraphLaunch(par_graph, st), "graph launch");
+      last_launches = par_nk;
+      return;
+    }
+    const bool again = par_seen && key == par_key;
+    drop_par_graph();
+    par_seen = false;
+    if (!again) {  // scratch grows here, if it does: the key takes the allocation count after the call
+      score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
+      key.gen = alloc_gen;
+      par_key = key;
+      par_seen = true;
+      return;
+    }
+    cudaGraph_t g = nullptr;
+    ck(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
+    } catch (...) {
+      cudaStreamEndCapture(st, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    ck(cudaStreamEndCapture(st, &g), "end capture");
+    cudaGraphExec_t ge = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    ck(e, "graph instantiate");
+    if (alloc_gen != key.gen) {  // not expected: the direct call before sized the scratch
+      cudaGraphExecDestroy(ge);
+      throw Error(GEM_E_STATE, "scratch grew while the scoring graph was captured");
+    }
+    par_graph = ge;
+    par_key = key;
+    par_seen = true;
+    par_nk = last_launches;
+    ck(cudaGraphLaunch(par_graph, st), "graph launch");
+  }
+
+  void score_parallel_direct(const uint32_t* toks_d, size_t stride, int nseq, size_t len, int which,
+                             uint32_t base_pos, float* lp_d, uint32_t* am_d) {
     const int L = (int)std::min<size_t>(len, kSeqChunk);
     const int SC = std::max(1, std::min({nseq, max_seqs, kBatchRows / L}));
     const int cap = L * SC;
