@@ -137,7 +137,10 @@ int gem_twolevel_logprob(gem_model* m, uint32_t target, float* logprob, uint32_t
 /* gem bench / gem check's scoring loop (main.rs:270-289) on sequence 0: BOS forward when the model
  * has one, then for i < n: forward(toks[i], i + off), head logprob of toks[i + 1]. toks has n + 1
  * entries; logprob_out / argmax_out have n (argmax_out may be NULL). head: 0 full, 1 two-level.
- * Host buffers; the loop runs on the device under the schedule gem_set_schedule selects. */
+ * Host buffers; the loop runs on the device under the schedule gem_set_schedule selects. Under the
+ * parallel schedule a call repeated with the same n and head (and, for gem_score_dev, the same device
+ * pointers) replays a CUDA graph of the previous identical call's launches from its third repetition;
+ * the results are those of a direct call. */
 int gem_score(gem_model* m, const uint32_t* toks, size_t n, int head, float* logprob_out,
               uint32_t* argmax_out);
 /* Same loop on device buffers (toks_dev n + 1, outputs n), enqueued on the model's stream. */
