@@ -338,7 +338,8 @@ def main():
     am_h = am_d.cpu().numpy().astype(np.uint32)
     clocks = clk.summary()
     if kind == PARALLEL:
-        roofline, sched = parallel_roofline(g, torch, step, info, ms_max / args.steps, clocks, args)
+        roofline, sched = parallel_roofline(g, torch, step, info, ms_max / args.steps, clocks, args,
+                                            token_bytes(g, info, mf, am_h, toks_h))
     else:
         roofline, sched = token_roofline(g, info, mf, am_h, toks_h, ms_max / args.steps, args, kind)
     # ---- e2e: the host-buffer entry point (H2D token ids, D2H log-probs + argmax every step) ----
@@ -404,13 +405,29 @@ def gemm_traffic():
     return None
 
 
-def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
+def token_bytes(g, info, mf, am_h, toks_h):
+    """Algorithmic HBM bytes of one scored token (bytes_per_token), with the second class block counted
+    for the positions whose top class is not the target's."""
+    order = np.fromfile(str(mf.twolevel) + ".order", dtype="<u4")
+    cls_of = np.empty(g.vocab, np.int64)
+    cls_of[order] = np.arange(len(order)) // info["per"]
+    extra = float(np.mean(cls_of[am_h] != cls_of[toks_h[1:]]))
+    return bytes_per_token(info, n_pos_schedule(info, SEQ_TOKENS), extra)
+
+
+def parallel_roofline(g, torch, step, info, ms_step, clocks, args, bpt):
     """Roofline of the dominant kernel of parallel scoring, the exact int8 matrix product (k_seq_gemm).
 
-    It is bound by CUDA-core issue, not by HBM or tensor cores: the reference's rounding (one fp32 FMA
-    per 32-block per lane, q8.rs:248-292) leaves at least three instructions per int8 weight pair and
-    position (the pair dot, its exact conversion to fp32, the FMA). The peak is that floor at the SM
-    clock: SMs x 128 lanes x clock / 3 pairs per second, 2 multiply-adds per pair, 2 ops each."""
+    A dense contraction, so its roofline is the tensor-core one (the measured bf16 GEMM peak; int8 has
+    no measured figure here). The reference's rounding (one fp32 FMA per 32-block per lane,
+    q8.rs:248-292) keeps it on the CUDA cores: tensor-core variants are exact only with each lane pair
+    in its own accumulator column, which leaves that FMA on the CUDA cores and measured no faster. Its
+    own ceiling, `cuda_core_view`, is the instruction floor at the SM clock: at least three instructions
+    per int8 weight pair and position (the pair dot, its exact conversion to fp32, half a packed FMA
+    plus the scale), so SMs x 128 lanes x clock / 3 pairs per second, 2 multiply-adds per pair, 2 ops
+    each. `per_token_hbm_view` is the batch-1 HBM roofline of scoring (every token's bytes read once
+    per token, as a token-by-token schedule must): the parallel schedule reads the weights once per
+    step instead, so it can exceed it."""
     g.set_profiling(True)
     for _ in range(2):
         step()
@@ -425,10 +442,23 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
     peak = sms * 128 * mhz * 1e6 / 3 * 4 / 1e12
     hbm, hbm_kind = hbm_peak()
     alg_bytes = info["body_bytes"] + info["classes"] * info["d"] * 4
-    roof = {"bound": "alu", "unit": "TOP/s", "achieved": round(achieved, 2), "peak": round(peak, 2),
-            "peak_kind": f"derived: {sms} SMs x 128 lanes x {mhz:.0f} MHz / 3 instructions per int8 pair x 4 ops",
-            "frac": round(achieved / peak, 4), "traffic": gemm_traffic(),
+    tensor_peak = peaks().get("bf16_tflops")
+    tensor_kind = "measured bf16 dense (burst)"
+    if not tensor_peak:
+        tensor_peak, tensor_kind = 1590.0, "fallback bf16 dense"
+    tok_s = SEQ_TOKENS / (ms_step * 1e-3)
+    roof = {"bound": "tensor", "unit": "TFLOP/s", "achieved": round(achieved, 2), "peak": tensor_peak,
+            "peak_kind": tensor_kind, "frac": round(achieved / tensor_peak, 4), "traffic": gemm_traffic(),
             "kernel": "k_seq_gemm (4 launches per layer and sequence part)", "ops_per_step": ops,
+            "note": "exact int8 x int8 -> fp32 products on the CUDA cores (the reference's per-block fp32 "
+                    "rounding); the tensor-core peak is the dense-contraction bound, cuda_core_view this "
+                    "kernel's instruction ceiling",
+            "cuda_core_view": {"unit": "TOP/s", "achieved": round(achieved, 2), "peak": round(peak, 2),
+                               "peak_kind": f"derived: {sms} SMs x 128 lanes x {mhz:.0f} MHz / 3 instructions "
+                                            "per int8 pair x 4 ops", "frac": round(achieved / peak, 4)},
+            "per_token_hbm_view": {"algorithmic_bytes_per_token": int(bpt), "tokens_s": round(tok_s, 1),
+                                   "roofline_tokens_s": round(hbm * 1e9 / bpt, 1),
+                                   "frac": round(tok_s * bpt / (hbm * 1e9), 4), "peak": hbm, "peak_kind": hbm_kind},
             "kernel_timing": "CUDA events around each launch group of a one-stream pass of the same step "
                              "(profiling runs the sequence as one part; the timed step runs its parts' "
                              "launches concurrently on their streams)",
@@ -436,8 +466,7 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
             "share_of_step": round(gemm_us / max(1e-9, sum(prof.values())), 3),  # of the one-part profiled step
             "hbm_view": {"algorithmic_bytes_per_step": alg_bytes, "achieved_GB_s": round(alg_bytes / (ms_step * 1e-3) / 1e9, 1),
                          "peak": hbm, "peak_kind": hbm_kind},
-            "tensor_view": {"bf16_peak_tflops": peaks().get("bf16_tflops"),
-                            "note": "the reference's per-block fp32 FMA order cannot be reproduced by tensor-core accumulation"}}
+            }
     sched = {"kind": "sequence-parallel (every position of the sequence through each layer together; the "
                      "sequence in 4 parts of 128 positions on 4 streams, each part one layer behind the one "
                      "before it; a repeated call replays them as one CUDA graph)",
@@ -448,12 +477,7 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args):
 def token_roofline(g, info, mf, am_h, toks_h, ms_step, args, kind):
     """HBM roofline of per-token scoring: algorithmic bytes per token / time per token."""
     from gem_b200 import TWO_LEVEL
-    order = np.fromfile(str(mf.twolevel) + ".order", dtype="<u4")
-    per = info["per"]
-    cls_of = np.empty(g.vocab, np.int64)
-    cls_of[order] = np.arange(len(order)) // per
-    extra = float(np.mean(cls_of[am_h] != cls_of[toks_h[1:]]))
-    bpt = bytes_per_token(info, n_pos_schedule(info, SEQ_TOKENS), extra)
+    bpt = token_bytes(g, info, mf, am_h, toks_h)
     per_token_s = ms_step / 1e3 / SEQ_TOKENS
     peak, peak_kind = hbm_peak()
     achieved = bpt / per_token_s / 1e9
