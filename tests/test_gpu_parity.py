@@ -439,3 +439,31 @@ def test_parallel_graph_replay(torch, small, head):
         assert np.array_equal(lp.view(np.uint32), want[name][0].view(np.uint32)), name
         assert np.array_equal(am, want[name][1]), name
     g.close()
+
+
+def test_score_edge_inputs(torch, small):
+    """What the reference guards by panicking (an id >= vocab indexes past the embedding, a position
+    >= ctx past the KV cache) fails with GEM_E_RANGE before any device work, and the model stays
+    usable; an empty sequence scores nothing; the longest sequence ctx allows scores, and its first
+    positions equal a short prefix's bit for bit (a position's result depends on no later token)."""
+    from gem_b200 import GemError
+    ctx = 64
+    g = Gemma(small.gguf, ctx=ctx)
+    g.load_twolevel(small.twolevel)
+    lp, am = g.score(np.array([5], np.uint32), TWO_LEVEL)
+    assert lp.shape == (0,) and am.shape == (0,)
+    bad = synth.tokens(10, g.vocab, seed=180)
+    bad[4] = g.vocab
+    with pytest.raises(GemError) as e:
+        g.score(bad, FULL)
+    assert e.value.code == -7
+    with pytest.raises(GemError) as e:
+        g.score(synth.tokens(ctx + 2, g.vocab, seed=181), FULL)  # ctx + 1 scored positions
+    assert e.value.code == -7
+    toks = synth.tokens(ctx + 1, g.vocab, seed=182)  # ctx scored positions: the most ctx holds
+    for head in (FULL, TWO_LEVEL):
+        lp, am = g.score(toks, head)
+        assert lp.shape == (ctx,) and np.all(np.isfinite(lp)) and np.all(lp <= 0)
+        lp20, am20 = g.score(toks[:21], head)
+        assert np.array_equal(lp[:20].view(np.uint32), lp20.view(np.uint32)) and np.array_equal(am[:20], am20)
+    g.close()
