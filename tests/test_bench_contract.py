@@ -54,3 +54,27 @@ def test_reference_arm_under_torchrun_prints_one_line():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
     assert d["cpu_baseline"]["value"] == d["value"]
+
+
+def test_roofline_bytes_of_the_270m_geometry():
+    """The roofline's denominators from the geometry alone (d 640, 18 layers, 4 q / 1 kv heads of 256,
+    ff 2048, 2048 classes of 128): weights per step, and the algorithmic bytes of one scored token
+    itemised in canonical GGUF sizes (Q8_0: 34 bytes per 32 weights; fp32 class table, bias and KV)."""
+    import importlib
+    sys.path.insert(0, str(ROOT))
+    bench = importlib.import_module("bench")
+    info = {"d": 640, "layers": 18, "head_dim": 256, "n_kv_heads": 1, "n_heads": 4, "ffn": 2048, "classes": 2048,
+            "per": 128, "window": 512}
+    weights = bench.body_weights(info)
+    assert weights == 18 * (1024 * 640 + 2 * 256 * 640 + 640 * 1024 + 2 * 2048 * 640 + 640 * 2048) == 100_270_080
+    info["body_bytes"] = weights // 32 * 34
+    npos = bench.n_pos_schedule(info, 512)
+    assert abs(npos.mean() - 256.5) < 1e-9  # every layer's window (512) covers the whole sequence
+    body = 106_536_960
+    classes = 2048 * 640 * 4 + 2048 * 4
+    block = 128 * (640 + 20 * 2)            # one class block: 128 Q8_0 rows with f16 scales
+    kv = 18 * 256.5 * 256 * 4 * 2 + 18 * 256 * 4 * 2
+    vectors = 18 * (4 * 640 + 2 * 256 + 256) * 4 + 640 * 4
+    want = body + classes + block + kv + vectors
+    assert bench.bytes_per_token(info, npos, 0.0) == want == 121_609_728
+    assert bench.bytes_per_token(info, npos, 1.0) == want + block  # the top class's block too
