@@ -89,3 +89,11 @@ def test_null_arguments():
     assert L.gem_open(None, 64, 8, 0, 0, 1, None) == -1
     assert L.gem_forward(None, 0, 0, None) == -1
     assert L.gem_score(None, None, 0, 0, None, None) == -1
+
+
+def test_rust_binding_declares_every_entry_point():
+    """The reference-side binding a Rust host adds (the extern "C" blocks in INTEGRATION.md) names every
+    function include/gem.h declares."""
+    text = (ROOT / "INTEGRATION.md").read_text()
+    missing = [n for n in declared() if f"fn {n}(" not in text]
+    assert not missing, missing
