@@ -35,6 +35,16 @@ SEQ_TOKENS = 512
 CTX = 2048  # gem bench's context (main.rs:204)
 CLASSES = 2048
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+# The reference's published figure for this metric and workload: gem bench, Gemma 3 270M Q8_0, two-level
+# head 2048 x 128, 512 tokens, batch 1, AVX-512, 8 threads on a Ryzen 7 7700 (results/gem-bench.jsonl
+# rows 26, 28, 30: 310.2, 304.5, 311.1 tokens/s).
+PUBLISHED = {"value": round((310.2 + 304.5 + 311.1) / 3, 1), "unit": "tokens/s",
+             "source": "results/gem-bench.jsonl:26,28,30 (gem bench, 270M Q8_0, two-level 2048 x 128, "
+                       "AVX-512, 8 threads, Ryzen 7 7700; mean of 3)"}
+
+
+def vs_published(value):
+    return round(value / PUBLISHED["value"], 2)
 
 
 def parse():
@@ -177,7 +187,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": vs_published(value), "published_baseline": PUBLISHED,
+        "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
         "config": {"workload": "gemma3-270m Q8_0, two-level head 2048x128, batch 1, 512 random tokens per step",
                    "geometry": "gemma3-270m (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "
                                "random init N(0,0.02) quantized to Q8_0", "global_batch": 1, "seq_len": SEQ_TOKENS,
@@ -369,7 +380,8 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": vs_published(value), "published_baseline": PUBLISHED,
+            "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic",
             "numerics": args.numerics,
             "config": {"workload": "gemma3-270m Q8_0, two-level head 2048x128, batch 1, 512 random tokens per step",
                        "geometry": "gemma3-270m (d 640, 18 layers, 4q/1kv heads, hd 256, ff 2048, vocab 262144), "

@@ -30,6 +30,9 @@ def test_reference_arm_json_line():
     assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["higher_is_better"] is True
     assert d["value"] > 0 and d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 0
     assert d["config"]["workload"] and "model" not in d["config"]
+    pub = d["published_baseline"]  # the reference's own figure for this metric and workload
+    assert pub["value"] == 308.6 and pub["unit"] == d["unit"]
+    assert abs(d["vs_baseline"] - d["value"] / pub["value"]) < 0.01
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
