@@ -162,6 +162,25 @@ def n_pos_schedule(info, n_tokens):
     return tot / n_tokens
 
 
+def cpu_model():
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def gem_bench_fields(m, threads, seconds, body_s, head_s, steps):
+    """The oracle's run in the fields of gem bench's JSONL record (crates/gem/src/main.rs:295-310):
+    tokens/s, body and head microseconds per token, the head's share, threads, ISA; plus the CPU."""
+    n = SEQ_TOKENS * steps
+    return {"tok_per_s": round(n / seconds, 1), "body_us": round(body_s / n * 1e6, 1),
+            "head_us": round(head_s / n * 1e6, 1), "head_share": round(head_s / max(1e-12, body_s + head_s), 3),
+            "threads": threads, "isa": m.isa, "tokens": SEQ_TOKENS, "cpu": cpu_model()}
+
+
 def run_reference(args):
     """Times the oracle (the CPU restatement of the reference's scoring path) on all host cores."""
     from gem_b200 import synth
@@ -177,11 +196,12 @@ def run_reference(args):
     toks = synth.tokens(SEQ_TOKENS + 1, m.vocab, seed=1000)
     for _ in range(args.warmup):
         m.score(toks, 1)
-    times = []
+    times, body_s, head_s = [], 0.0, 0.0
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        m.score(toks, 1)
+        _, _, tb, th = m.score(toks, 1)
         times.append(time.perf_counter() - t0)
+        body_s, head_s = body_s + tb, head_s + th
     per_step = sum(times) / len(times)
     value = SEQ_TOKENS / per_step
     line = {
@@ -194,7 +214,8 @@ def run_reference(args):
                                "random init N(0,0.02) quantized to Q8_0", "global_batch": 1, "seq_len": SEQ_TOKENS,
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "isa": m.isa, "sample": f"{args.steps} x {SEQ_TOKENS}-token sequences"},
+                         "isa": m.isa, "sample": f"{args.steps} x {SEQ_TOKENS}-token sequences",
+                         "gem_bench": gem_bench_fields(m, threads, sum(times), body_s, head_s, args.steps)},
         "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -597,10 +618,11 @@ def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     m.load_twolevel(mf.twolevel)
     toks = synth.tokens(SEQ_TOKENS + 1, m.vocab, seed=1000)
     t0 = time.perf_counter()
-    m.score(toks, 1)
+    _, _, tb, th = m.score(toks, 1)
     dt = time.perf_counter() - t0
     out["cpu_baseline"] = {"value": round(SEQ_TOKENS / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
-                           "isa": m.isa, "sample": f"one {SEQ_TOKENS}-token sequence, two-level head, same workload"}
+                           "isa": m.isa, "sample": f"one {SEQ_TOKENS}-token sequence, two-level head, same workload",
+                           "gem_bench": gem_bench_fields(m, threads, dt, tb, th, 1)}
     m.close()
     return out
 

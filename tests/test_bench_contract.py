@@ -36,6 +36,9 @@ def test_reference_arm_json_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
     assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
+    gb = cb["gem_bench"]  # gem bench's JSONL fields (main.rs:295-310)
+    assert gb["threads"] == cb["cores"] and gb["tokens"] == 512 and gb["body_us"] > 0 and gb["head_us"] > 0
+    assert 0 < gb["head_share"] < 1 and abs(gb["tok_per_s"] - d["value"]) <= 0.02 * d["value"]
     e = d["e2e"]
     assert e["value"] == d["value"] and e["unit"] == d["unit"]
     assert e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
