@@ -216,6 +216,7 @@ struct gem_model {
   cudaGraphExec_t par_graph = nullptr;
   ParKey par_key{};
   bool par_seen = false;  // par_key holds the arguments of the last direct call
+  bool par_graph_failed = false;  // a capture failed on this model: launch directly from then on
   int64_t par_nk = 0;
   int64_t alloc_gen = 0;
   void drop_par_graph() {
@@ -615,7 +616,7 @@ struct gem_model {
   // may change between calls; profiling, batches and the vocab-sharded head launch directly.
   void score_parallel(const uint32_t* toks_d, size_t stride, int nseq, size_t len, int which, uint32_t base_pos,
                       float* lp_d, uint32_t* am_d) {
-    if (nseq != 1 || par_prof || comm || !par_graph_enabled()) {
+    if (nseq != 1 || par_prof || comm || par_graph_failed || !par_graph_enabled()) {
       drop_par_graph();
       par_seen = false;
       score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
@@ -637,23 +638,30 @@ struct gem_model {
       par_seen = true;
       return;
     }
+    // A capture or instantiation that fails (the caller's thread already capturing, a driver without
+    // the support) launches this call directly and turns the replay off for the model.
     cudaGraph_t g = nullptr;
-    ck(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "begin capture");
-    try {
-      score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
-    } catch (...) {
-      cudaStreamEndCapture(st, &g);
-      if (g) cudaGraphDestroy(g);
-      throw;
-    }
-    ck(cudaStreamEndCapture(st, &g), "end capture");
     cudaGraphExec_t ge = nullptr;
-    const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
-    cudaGraphDestroy(g);
-    ck(e, "graph instantiate");
-    if (alloc_gen != key.gen) {  // not expected: the direct call before sized the scratch
-      cudaGraphExecDestroy(ge);
-      throw Error(GEM_E_STATE, "scratch grew while the scoring graph was captured");
+    bool captured = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (captured) {
+      try {
+        score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
+      } catch (...) {
+        captured = false;
+      }
+      if (cudaStreamEndCapture(st, &g) != cudaSuccess) captured = false;
+      if (captured && g && cudaGraphInstantiate(&ge, g, 0) != cudaSuccess) {
+        ge = nullptr;
+        captured = false;
+      }
+      if (g) cudaGraphDestroy(g);
+    }
+    if (!captured || !ge || alloc_gen != key.gen) {  // scratch that grew under capture: not expected either
+      if (ge) cudaGraphExecDestroy(ge);
+      cudaGetLastError();  // a failed capture call leaves no sticky error; clear the last-error slot
+      par_graph_failed = true;
+      score_parallel_direct(toks_d, stride, nseq, len, which, base_pos, lp_d, am_d);
+      return;
     }
     par_graph = ge;
     par_key = key;
