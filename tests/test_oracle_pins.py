@@ -151,3 +151,55 @@ def test_greedy_top1_equals_two_level_argmax(small):
     for _ in range(8):
         h = rng.standard_normal(o.d).astype(np.float32)
         assert o.greedy(h, 1)[0] == o.twolevel(h, 0)[1]
+
+
+def test_heads_match_numpy_restatement(small):
+    """Full::logprob and TwoLevel::logprob (main.rs:20-38, 57-107) restated in float64 numpy on the same
+    weights: the head matrix from gguf-py's dequantization times the int8-quantized hidden state
+    (Act::quantize, q8.rs:187-246), log-sum-exp over the vocabulary; for the two-level head the class
+    files' mapping (per = ceil(V / k), class c holds order[c * per ..]), class logits A h + b on the
+    unquantized h, and the target class's block. Agreement within float32 summation noise, and the
+    oracle's argmax is a maximum of the restated logits."""
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+    r = gguf.GGUFReader(str(small.gguf))
+    t = next(t for t in r.tensors if t.name == "token_embd.weight")
+    W = np.asarray(quants.dequantize(t.data, t.tensor_type), np.float64).reshape(int(t.shape[1]), int(t.shape[0]))
+    V, d = W.shape
+    p = str(small.twolevel)
+    order = np.fromfile(p + ".order", "<u4").astype(np.int64)
+    k = len(np.fromfile(p + ".b", "<f4"))
+    A = np.fromfile(p + ".A", "<f4").astype(np.float64).reshape(k, d)
+    b = np.fromfile(p + ".b", "<f4").astype(np.float64)
+    per = -(-V // k)
+    cls_of, pos_of = np.empty(V, np.int64), np.empty(V, np.int64)
+    cls_of[order], pos_of[order] = np.arange(V) // per, np.arange(V) % per
+
+    def lse(v):
+        m = v.max()
+        return m + np.log(np.exp(v - m).sum())
+
+    o = orc.Model(small.gguf, ctx=16, threads=2)
+    o.load_twolevel(small.twolevel)
+    rng = np.random.default_rng(12)
+    for _ in range(6):
+        h = rng.standard_normal(d).astype(np.float32)
+        q, s = orc.quantize(h, o.isa)
+        hq = q.astype(np.float64) * np.repeat(s.astype(np.float64), 32)
+        z = W @ hq
+        tgt = int(rng.integers(0, V))
+        lp, am = o.full(h, tgt)
+        assert abs(lp - (z[tgt] - lse(z))) < 2e-4
+        assert z.max() - z[am] < 1e-4
+        cl = A @ h.astype(np.float64) + b
+        c = cls_of[tgt]
+        rows = order[c * per:(c + 1) * per]
+        inner = W[rows] @ hq
+        want = (cl[c] - lse(cl)) + (inner[pos_of[tgt]] - lse(inner))
+        lp2, am2 = o.twolevel(h, tgt)
+        assert abs(lp2 - want) < 2e-4
+        top = int(np.argmax(cl))  # screening with top = 1: the best class, then its best row
+        best = W[order[top * per:(top + 1) * per]] @ hq
+        assert cls_of[am2] == top or cl.max() - cl[cls_of[am2]] < 1e-4
+        if cls_of[am2] == top:
+            assert best.max() - best[pos_of[am2]] < 1e-4
