@@ -153,17 +153,22 @@ def test_greedy_top1_equals_two_level_argmax(small):
         assert o.greedy(h, 1)[0] == o.twolevel(h, 0)[1]
 
 
-def test_heads_match_numpy_restatement(small):
+@pytest.mark.parametrize("name", ["small", "small-qwen2"])
+def test_heads_match_numpy_restatement(name, model_dir):
     """Full::logprob and TwoLevel::logprob (main.rs:20-38, 57-107) restated in float64 numpy on the same
     weights: the head matrix from gguf-py's dequantization times the int8-quantized hidden state
     (Act::quantize, q8.rs:187-246), log-sum-exp over the vocabulary; for the two-level head the class
     files' mapping (per = ceil(V / k), class c holds order[c * per ..]), class logits A h + b on the
     unquantized h, and the target class's block. Agreement within float32 summation noise, and the
-    oracle's argmax is a maximum of the restated logits."""
+    oracle's argmax is a maximum of the restated logits. The qwen2 model's head is its own (untied)
+    output matrix."""
     gguf = pytest.importorskip("gguf")
     from gguf import quants
+    from gem_b200 import synth
+    small = synth.ensure(name, classes=64, directory=model_dir)
     r = gguf.GGUFReader(str(small.gguf))
-    t = next(t for t in r.tensors if t.name == "token_embd.weight")
+    names = {t.name: t for t in r.tensors}
+    t = names.get("output.weight", names["token_embd.weight"])
     W = np.asarray(quants.dequantize(t.data, t.tensor_type), np.float64).reshape(int(t.shape[1]), int(t.shape[0]))
     V, d = W.shape
     p = str(small.twolevel)
