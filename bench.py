@@ -8,9 +8,19 @@ One step scores one 512-token sequence (gem bench's loop, crates/gem/src/main.rs
 library's device-buffer entry point; `e2e` runs the same steps through the host-buffer entry point
 (token ids copied in, log-probs and argmax copied out, every step). Under torchrun each rank scores
 its own sequence on its own GPU (weak scaling, no collective on the data path); the timed region is
-bracketed by barriers and the time is the max over ranks. `--impl reference` times the oracle (the CPU
-restatement of gem's scoring path; the reference is Rust and no Rust toolchain exists here) on the
-host cores. Prints one JSON line from rank 0.
+bracketed by barriers and the time is the max over ranks. `parity` compares rank 0's last timed
+step with one untimed oracle pass of the same sequence.
+
+Secondary legs, at every N (all ranks take part, times are the max over ranks):
+  batched      256 sequences x 512 positions split over the ranks (strong scaling: fixed total)
+  vocab_shard  Gemma-3-1B geometry, 1024 positions, the full head's vocabulary sharded over the ranks
+               with an NCCL all-gather of per-shard statistics; checked on the box against the
+               unsharded head; time in the all-gather + merge reported beside the head shard's
+and at N = 1 only: the per-token schedules, the full head, the QAT layout (Q4_0 body, F16 head and
+its Q8_0 requantization), the head microbenchmark and the CPU baseline.
+
+`--impl reference` times the oracle (the CPU restatement of gem's scoring path; the reference is Rust
+and no Rust toolchain exists here) on the host cores. Prints one JSON line from rank 0.
 """
 from __future__ import annotations
 
@@ -32,6 +42,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "tokens/s scored (270M Q8_0, 2-level head) b1+batched; head GEMV HBM GB/s"
 SEQ_TOKENS = 512
+REF_THREADS = 8  # the pool size exact numerics reproduce (gem bench's default, main.rs:197)
+BATCH_SEQS = 256
+SHARD_TOKENS = 1024
 CTX = 2048  # gem bench's context (main.rs:204)
 CLASSES = 2048
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
@@ -222,78 +235,34 @@ def run_reference(args):
 
 
 def run_vocab_shard(args):
-    """Gemma-3-1B geometry, one 1024-position sequence per step, the full head's vocabulary sharded
-    over the ranks (one GPU each) with an NCCL merge of the per-shard statistics. Every rank scores the
-    same sequence (the body is replicated), so the total work is fixed: strong scaling. The unsharded
-    two-level head on the same model is timed beside it."""
+    """--workload 1b-vocab-shard: the C5 leg (run_vocab_shard_leg) alone, as the headline line."""
     import datetime
 
     import torch
     import torch.distributed as dist
-    from gem_b200 import FULL, TWO_LEVEL, Gemma, shard, synth
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
-    barrier = (lambda: dist.barrier()) if world > 1 else (lambda: None)
-    n = 1024
-    if rank == 0:
-        mf = synth.ensure("gemma3-1b", classes=2048)
-    barrier()
-    if rank != 0:
-        mf = synth.ensure("gemma3-1b", classes=2048)
-    g = Gemma(mf.gguf, ctx=2048, device=local)
-    g.load_twolevel(mf.twolevel)
-    if world > 1:
-        shard.init_vocab_shard(g)
-    stream = torch.cuda.ExternalStream(g.stream, device=local)
-    toks = torch.tensor(synth.tokens(n + 1, g.vocab, seed=3000).astype(np.int32), device="cuda")
-    lp = torch.empty(n, device="cuda")
-    am = torch.empty(n, dtype=torch.int32, device="cuda")
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
-
-    def timed(head, steps):
-        for _ in range(args.warmup):
-            g.score_dev(toks.data_ptr(), n, head, lp.data_ptr(), am.data_ptr())
-        torch.cuda.synchronize()
-        barrier()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-        for a, b in evs:
-            flush.zero_()
-            torch.cuda.synchronize()
-            a.record(stream)
-            g.score_dev(toks.data_ptr(), n, head, lp.data_ptr(), am.data_ptr())
-            b.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], device="cuda", dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item()) / steps
-
     with Clocks(local) as clk:
-        ms_full = timed(FULL, args.steps)
-    launches = g.last_launches()
-    ms_two = timed(TWO_LEVEL, args.steps)
+        r = run_vocab_shard_leg(torch, dist, world, rank, local, flush, args)
     if rank == 0:
-        first, rows = shard.row_range(g.vocab, world, rank)
         line = {
-            "metric": "tokens/s scored (1B Q8_0, full head vocab-sharded across GPUs)", "value": round(n / (ms_full / 1e3), 1),
-            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_full, 3),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x int8 -> f32 (Q8_0)",
-            "data": "synthetic", "numerics": "exact",
-            "config": {"workload": "gemma3-1b Q8_0, one 1024-position sequence per step, full head sharded by vocab rows",
-                       "geometry": "gemma3-1b (d 1152, 26 layers, 4q/1kv heads, hd 256, ff 6912, vocab 262144), "
-                                "random init N(0,0.02) quantized to Q8_0",
-                       "global_batch": 1, "seq_len": n, "parallelism": f"vocab shard x{world} (body replicated)",
-                       "rows_per_rank": rows, "l2": "flushed (256 MiB write) before every step"},
-            "two_level_unsharded": {"value": round(n / (ms_two / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_two, 3)},
-            "gpu_launches": int(launches * args.steps), "clocks": clk.summary(),
+            "metric": "tokens/s scored (1B Q8_0, full head vocab-sharded across GPUs)", "value": r["value"],
+            "unit": "tokens/s", "n_gpus": world, "steps": max(1, min(args.steps, 10)), "warmup": args.warmup,
+            "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8 x int8 -> f32 (Q8_0)", "data": "synthetic", "numerics": "exact",
+            "config": {"workload": r["workload"], "global_batch": 1, "seq_len": SHARD_TOKENS,
+                       "parallelism": f"vocab shard x{world} (body replicated)", "rows_per_rank": r["rows_per_rank"],
+                       "l2": r["l2"]},
+            "check_vs_unsharded": r["check_vs_unsharded"], "head_us_per_step": r["head_us_per_step"],
+            "two_level_unsharded": r["two_level_unsharded"],
+            "gpu_launches": int(r["gpu_launches_per_step"] * max(1, min(args.steps, 10))), "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
-    g.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -368,6 +337,7 @@ def main():
     kind, kind_why = g.schedule_kind(TWO_LEVEL)
     launches_per_step = g.last_launches()
     am_h = am_d.cpu().numpy().astype(np.uint32)
+    lp_h = lp_d.cpu().numpy()
     clocks = clk.summary()
     if kind == PARALLEL:
         roofline, sched = parallel_roofline(g, torch, step, info, ms_max / args.steps, clocks, args,
@@ -393,9 +363,16 @@ def main():
         dist.all_reduce(tw, op=dist.ReduceOp.MAX)
     e2e_value = tokens / float(tw.item())
 
+    # ---- parity: rank 0's last timed step against one untimed oracle pass of the same sequence ----
+    parity = oracle_parity(mf, toks_h, lp_h, am_h, TWO_LEVEL) if rank == 0 else None
+
     extras = {}
-    if not args.no_extras and world == 1:
-        extras = run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf)
+    if not args.no_extras:
+        # every rank takes part: C4 split over the ranks, C5 sharded over them
+        extras["batched"] = run_batched(torch, dist, world, rank, local, mf, flush, args)
+        extras["vocab_shard"] = run_vocab_shard_leg(torch, dist, world, rank, local, flush, args)
+        if world == 1:
+            extras.update(run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf))
 
     if rank == 0:
         line = {
@@ -415,6 +392,7 @@ def main():
                     "d2h_bytes_per_step": SEQ_TOKENS * 8},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks,
+            "parity": parity,
         }
         line.update(extras)
         print(json.dumps(line), flush=True)
@@ -482,6 +460,8 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args, bpt):
     tok_s = SEQ_TOKENS / (ms_step * 1e-3)
     roof = {"bound": "tensor", "unit": "TFLOP/s", "achieved": round(achieved, 2), "peak": tensor_peak,
             "peak_kind": tensor_kind, "frac": round(achieved / tensor_peak, 4), "traffic": gemm_traffic(),
+            "traffic_source": "the committed ncu capture's DRAM bytes per step (profiles/dram_traffic.txt), "
+                              "not measured in this run",
             "kernel": "k_seq_gemm (4 launches per layer and sequence part)", "ops_per_step": ops,
             "note": "exact int8 x int8 -> fp32 products on the CUDA cores (the reference's per-block fp32 "
                     "rounding); the tensor-core peak is the dense-contraction bound, cuda_core_view this "
@@ -542,6 +522,173 @@ def time_dev(torch, stream, fn, iters, flush):
     return sum(a.elapsed_time(b) for a, b in evs) / iters
 
 
+def oracle_parity(mf, toks_h, lp, am, head, ctx=CTX):
+    """Compares scored log-probs and argmax ids with one untimed oracle pass of the same sequence (the
+    oracle's AVX-512 path with the pool size exact numerics reproduce). Bar: identical argmax ids,
+    |d logprob| < 1e-3 nats (north-star); exact numerics give < 2e-5."""
+    from oracle import oracle as orc
+    isa = "avx512" if orc.detect_isa() == "avx512" else None
+    o = orc.Model(mf.gguf, ctx=ctx, threads=REF_THREADS, isa=isa)
+    if mf.twolevel is not None:
+        o.load_twolevel(mf.twolevel)
+    lpo, amo, _, _ = o.score(np.asarray(toks_h, np.uint32), head)
+    used = o.isa
+    o.close()
+    n = min(len(lpo), len(lp))
+    err = float(np.abs(np.asarray(lp[:n], np.float32) - lpo[:n]).max()) if n else 0.0
+    same = bool(np.array_equal(np.asarray(am[:n], np.uint32), amo[:n]))
+    return {"against": f"oracle ({used}, {REF_THREADS}-thread pool), one untimed pass of the same sequence",
+            "positions": int(n), "argmax_equal": same, "argmax_mismatches": int(np.sum(np.asarray(am[:n], np.uint32) != amo[:n])),
+            "max_abs_lp": err, "tolerance": 1e-3, "pass": bool(same and err < 1e-3)}
+
+
+def _max_over_ranks(torch, dist, world, v):
+    t = torch.tensor([float(v)], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_batched(torch, dist, world, rank, local, mf, flush, args):
+    """C4: 256 independent sequences x 512 positions, two-level head, split over the ranks by
+    shard.seq_range (strong scaling: the total is fixed); each rank scores its share in groups of 8
+    sequences (8 KV slots). Time = max over ranks of the device time of the rank's whole share."""
+    from gem_b200 import TWO_LEVEL, Gemma, shard, synth
+    first, count = shard.seq_range(BATCH_SEQS, world, rank)
+    gb = Gemma(mf.gguf, ctx=CTX, device=local, max_seqs=8)
+    gb.load_twolevel(mf.twolevel)
+    bstream = torch.cuda.ExternalStream(gb.stream, device=local)
+    btoks = np.stack([synth.tokens(SEQ_TOKENS + 1, gb.vocab, seed=2000 + s) for s in range(first, first + count)])
+    btd = torch.tensor(btoks.astype(np.int32), device="cuda")
+    blp = torch.empty((count, SEQ_TOKENS), device="cuda")
+    bam = torch.empty((count, SEQ_TOKENS), dtype=torch.int32, device="cuda")
+    bcall = lambda: gb.score_batch_dev(btd.data_ptr(), count, SEQ_TOKENS, TWO_LEVEL, blp.data_ptr(), bam.data_ptr())
+    bcall()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = time_dev(torch, bstream, bcall, 2, flush)
+    ms = _max_over_ranks(torch, dist, world, ms)
+    launches = gb.last_launches()
+    parity = None
+    if rank == 0:  # the rank's first sequence against the oracle
+        parity = oracle_parity(mf, btoks[0], blp[0].cpu().numpy(), bam[0].cpu().numpy().astype(np.uint32), TWO_LEVEL)
+        parity["sequence"] = int(first)
+    gb.close()
+    return {"value": round(BATCH_SEQS * SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+            "scaling": "strong", "n_gpus": world, "sequences_per_rank": count,
+            "workload": f"{BATCH_SEQS} sequences x {SEQ_TOKENS} positions, two-level head, split over {world} rank(s); "
+                        "one step = the whole batch; time = max over ranks",
+            "gpu_launches_per_step": launches, "parity": parity}
+
+
+def run_vocab_shard_leg(torch, dist, world, rank, local, flush, args):
+    """C5: Gemma-3-1B geometry, one 1024-position sequence per step, the full head's vocabulary sharded
+    over the ranks (one GPU each; at one rank, unsharded). The body is replicated, so the total work
+    is fixed (strong scaling). Before sharding every rank scores the sequence with the unsharded head;
+    the sharded results must equal it (argmax identical, log-probs within the log-sum-exp order
+    difference). A profiled pass splits the head's time into this rank's rows and the all-gather +
+    merge. The unsharded two-level head on the same model is timed beside it."""
+    from gem_b200 import FULL, TWO_LEVEL, Gemma, shard, synth
+    if rank == 0:
+        mf = synth.ensure("gemma3-1b", classes=2048)
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        mf = synth.ensure("gemma3-1b", classes=2048)
+    n = SHARD_TOKENS
+    g = Gemma(mf.gguf, ctx=CTX, device=local)
+    g.load_twolevel(mf.twolevel)
+    stream = torch.cuda.ExternalStream(g.stream, device=local)
+    toks = torch.tensor(synth.tokens(n + 1, g.vocab, seed=3000).astype(np.int32), device="cuda")
+    lp = torch.empty(n, device="cuda")
+    am = torch.empty(n, dtype=torch.int32, device="cuda")
+    call = lambda head: g.score_dev(toks.data_ptr(), n, head, lp.data_ptr(), am.data_ptr())
+    call(FULL)
+    g.sync()
+    want_lp, want_am = lp.cpu().numpy().copy(), am.cpu().numpy().copy()
+    rows = shard.row_range(g.vocab, 1, 0)
+    if world > 1:
+        rows = shard.init_vocab_shard(g)
+    steps = max(1, min(args.steps, 10))
+    for _ in range(args.warmup):
+        call(FULL)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_full = _max_over_ranks(torch, dist, world, time_dev(torch, stream, lambda: call(FULL), steps, flush))
+    launches = g.last_launches()
+    got_lp, got_am = lp.cpu().numpy(), am.cpu().numpy()
+    err = _max_over_ranks(torch, dist, world, float(np.abs(got_lp - want_lp).max()))
+    bad = _max_over_ranks(torch, dist, world, float(np.sum(got_am != want_am)))
+    g.set_profiling(True)
+    for _ in range(2):
+        call(FULL)
+    g.sync()
+    prof = g.parallel_profile()
+    g.set_profiling(False)
+    head_us = _max_over_ranks(torch, dist, world, prof["head"])
+    comb_us = _max_over_ranks(torch, dist, world, prof["combine"])
+    for _ in range(2):
+        call(TWO_LEVEL)
+    ms_two = _max_over_ranks(torch, dist, world, time_dev(torch, stream, lambda: call(TWO_LEVEL), steps, flush))
+    g.close()
+    return {"value": round(n / (ms_full / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_full, 3),
+            "scaling": "strong", "n_gpus": world,
+            "workload": f"gemma3-1b Q8_0 (d 1152, 26 layers, ff 6912), one {n}-position sequence per step, full head "
+                        f"{'sharded by vocab rows over ' + str(world) + ' ranks' if world > 1 else 'unsharded'}",
+            "rows_per_rank": rows[1], "gpu_launches_per_step": launches,
+            "check_vs_unsharded": {"max_abs_lp": err, "argmax_mismatches": int(bad), "pass": bool(bad == 0 and err < 2e-5)},
+            "head_us_per_step": {"this_rank_rows": round(head_us, 1), "all_gather_and_merge": round(comb_us, 1),
+                                 "note": "profiled pass (launched directly, events between launch groups), max over ranks"},
+            "two_level_unsharded": {"value": round(n / (ms_two / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms_two, 3)},
+            "l2": "flushed (256 MiB write) before every step"}
+
+
+def run_qat(torch, flush, args):
+    """C3: the 270M geometry in the QAT layout (Q4_0 body, F16 output matrix), full and two-level
+    heads, and the same model with the head requantized to Q8_0 at load (to_q8)."""
+    from gem_b200 import FULL, TWO_LEVEL, Gemma, synth
+    mf = synth.ensure("gemma3-270m", body="q4_0", head="f16", classes=CLASSES)
+    toks = synth.tokens(SEQ_TOKENS + 1, 262144, seed=1000)
+    out = {}
+    for head_bits, name in ((0, "f16_head"), (8, "q8_head")):
+        g = Gemma(mf.gguf, ctx=CTX, head_bits=head_bits)
+        g.load_twolevel(mf.twolevel)
+        stream = torch.cuda.ExternalStream(g.stream)
+        td = torch.tensor(toks.astype(np.int32), device="cuda")
+        lp = torch.empty(SEQ_TOKENS, device="cuda")
+        am = torch.empty(SEQ_TOKENS, dtype=torch.int32, device="cuda")
+        e = {}
+        for hname, head in (("two_level", TWO_LEVEL), ("full", FULL)):
+            call = lambda: g.score_dev(td.data_ptr(), SEQ_TOKENS, head, lp.data_ptr(), am.data_ptr())
+            for _ in range(2):
+                call()
+            ms = time_dev(torch, stream, call, 3, flush)
+            e[hname] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3)}
+        e["parity_two_level"] = oracle_parity_qat(mf, toks, g, td, lp, am, head_bits)
+        out[name] = e
+        g.close()
+    out["workload"] = "gemma3-270m, Q4_0 body, F16 262144x640 output matrix (f16_head) and the same requantized " \
+                      "to Q8_0 at load (q8_head); 512 random tokens per step, batch 1"
+    return out
+
+
+def oracle_parity_qat(mf, toks, g, td, lp, am, head_bits):
+    from gem_b200 import TWO_LEVEL
+    from oracle import oracle as orc
+    g.score_dev(td.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp.data_ptr(), am.data_ptr())
+    g.sync()
+    isa = "avx512" if orc.detect_isa() == "avx512" else None
+    o = orc.Model(mf.gguf, ctx=CTX, threads=REF_THREADS, isa=isa, head_bits=head_bits)
+    o.load_twolevel(mf.twolevel)
+    lpo, amo, _, _ = o.score(toks, TWO_LEVEL)
+    o.close()
+    a = am.cpu().numpy().astype(np.uint32)
+    err = float(np.abs(lp.cpu().numpy() - lpo).max())
+    return {"argmax_equal": bool(np.array_equal(a, amo)), "max_abs_lp": err, "positions": SEQ_TOKENS}
+
+
 def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     """Secondary figures: the full head end to end, the head microbenchmark (full 262144x640 GEMV with
     fused log-sum-exp vs the two-level head, batch 1 and 64) and the CPU baseline."""
@@ -569,22 +716,7 @@ def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     ms = time_dev(torch, stream, lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, FULL, lp_d.data_ptr(), am_d.data_ptr()),
                   2, flush)
     out["full_head"] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3)}
-    # batched scoring: 256 independent sequences x 512 positions (8 KV slots, groups of 8 sequences)
-    gb = Gemma(mf.gguf, ctx=CTX, device=torch.cuda.current_device(), max_seqs=8)
-    gb.load_twolevel(mf.twolevel)
-    bstream = torch.cuda.ExternalStream(gb.stream)
-    nseq = 256
-    btoks = np.stack([synth.tokens(SEQ_TOKENS + 1, gb.vocab, seed=2000 + s) for s in range(nseq)])
-    btd = torch.tensor(btoks.astype(np.int32), device="cuda")
-    blp = torch.empty((nseq, SEQ_TOKENS), device="cuda")
-    bam = torch.empty((nseq, SEQ_TOKENS), dtype=torch.int32, device="cuda")
-    bcall = lambda: gb.score_batch_dev(btd.data_ptr(), nseq, SEQ_TOKENS, TWO_LEVEL, blp.data_ptr(), bam.data_ptr())
-    bcall()
-    ms = time_dev(torch, bstream, bcall, 2, flush)
-    out["batched"] = {"value": round(nseq * SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
-                      "workload": f"{nseq} sequences x {SEQ_TOKENS} positions, two-level head, one step = the whole batch",
-                      "gpu_launches_per_step": gb.last_launches()}
-    gb.close()
+    out["qat"] = run_qat(torch, flush, args)
     # head microbenchmark: h ~ N(0, 1)
     peak, _ = hbm_peak()
     head_bytes = g.info["head_bytes"]

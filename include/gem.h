@@ -106,8 +106,10 @@ int gem_get_schedule_kind(gem_model* m, int head, int* kind);
 int gem_set_profiling(gem_model* m, int on);
 int gem_get_phase_profile(gem_model* m, double* layer_us, int n_layer, double* head_us, int n_head);
 /* Profile of parallel scoring (while profiling is on): mean device microseconds per scoring call in
- * each of 9 launch groups, timed with events between them - embedding, norms, q/k/v product,
- * attention, o product, gate/up product, gate, down product, head. No counterpart in the reference. */
+ * each of 10 launch groups, timed with events between them - embedding, norms, q/k/v product,
+ * attention, o product, gate/up product, gate, down product, head, and the vocab-sharded head's
+ * combine (the all-gather of the ranks' partial statistics and their merge; 0 unsharded). No
+ * counterpart in the reference. */
 int gem_get_parallel_profile(gem_model* m, double* us, int n);
 /* Kernels launched by the last scoring call (gem_score / gem_score_dev). */
 int gem_get_last_launches(gem_model* m, int64_t* n);

@@ -152,17 +152,22 @@ const GgufTensor& Gguf::info(const std::string& name) const {
 
 std::vector<uint8_t> Gguf::read(const std::string& name) const {  // gguf.rs:145-159
   const GgufTensor& t = info(name);
+  // element count and byte size in checked arithmetic: a crafted header cannot wrap them around
   uint64_t n = 1;
-  for (uint64_t d : t.dims) n *= d;
+  for (uint64_t d : t.dims)
+    if (__builtin_mul_overflow(n, d, &n)) throw Error(GEM_E_FORMAT, name + ": dimensions overflow");
   uint64_t bytes;
+  bool over = false;
   switch (t.type) {
-    case GGUF_F32: bytes = n * 4; break;
-    case GGUF_F16: bytes = n * 2; break;
-    case GGUF_Q8_0: bytes = n / 32 * 34; break;
-    case GGUF_Q4_0: bytes = n / 32 * 18; break;
+    case GGUF_F32: over = __builtin_mul_overflow(n, (uint64_t)4, &bytes); break;
+    case GGUF_F16: over = __builtin_mul_overflow(n, (uint64_t)2, &bytes); break;
+    case GGUF_Q8_0: over = __builtin_mul_overflow(n / 32, (uint64_t)34, &bytes); break;
+    case GGUF_Q4_0: over = __builtin_mul_overflow(n / 32, (uint64_t)18, &bytes); break;
     default: throw Error(GEM_E_FORMAT, name + ": unsupported tensor type " + std::to_string(t.type));
   }
-  if (base_ + t.offset + bytes > size_) throw Error(GEM_E_IO, name + ": tensor data past end of file");
+  if (over) throw Error(GEM_E_FORMAT, name + ": tensor size overflows");
+  if (base_ > size_ || t.offset > size_ - base_ || bytes > size_ - base_ - t.offset)
+    throw Error(GEM_E_IO, name + ": tensor data past end of file");
   std::vector<uint8_t> buf(bytes);
   size_t got = 0;
   while (got < bytes) {

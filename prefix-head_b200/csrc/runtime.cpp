@@ -177,7 +177,7 @@ struct gem_model {
   float *s_spart = nullptr, *s_sgath = nullptr;
   size_t spart_cap = 0;
   // per-category device time of parallel scoring (gem_set_profiling): events between launch groups
-  enum { PAR_EMBED, PAR_NORM, PAR_QKV, PAR_ATTN, PAR_O, PAR_GU, PAR_GLU, PAR_DOWN, PAR_HEAD, PAR_CATS };
+  enum { PAR_EMBED, PAR_NORM, PAR_QKV, PAR_ATTN, PAR_O, PAR_GU, PAR_GLU, PAR_DOWN, PAR_HEAD, PAR_COMBINE, PAR_CATS };
   bool par_prof = false;
   std::vector<cudaEvent_t> pev;
   std::vector<int> pcat;
@@ -599,9 +599,11 @@ struct gem_model {
                                 s_spart + (size_t)h0 * 5, err, st);
       launches += 2;
     }
+    par_mark(PAR_HEAD);  // this rank's rows: logits and partial statistics
     const ncclResult_t r = nccl().all_gather(s_spart, s_sgath, (size_t)T * 5, ncclFloat32, comm, st);
     if (r != ncclSuccess) throw Error(GEM_E_NCCL, std::string("ncclAllGather: ") + nccl().error_string(r));
     launch_seq_logit_combine(s_sgath, shard_n, T, lpo, amo, st);
+    par_mark(PAR_COMBINE);  // the all-gather over the ranks and the merge
     return launches + 1;
   }
 

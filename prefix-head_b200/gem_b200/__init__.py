@@ -248,12 +248,13 @@ class Gemma:
         _check(lib().gem_get_phase_profile(self._h, la, 16, ha, 6))
         return dict(zip(self.LAYER_PHASES, [round(v, 3) for v in la])), dict(zip(self.HEAD_PHASES, [round(v, 3) for v in ha]))
 
-    PARALLEL_GROUPS = ["embed", "norm", "qkv", "attention", "o", "gate_up", "gate", "down", "head"]
+    PARALLEL_GROUPS = ["embed", "norm", "qkv", "attention", "o", "gate_up", "gate", "down", "head", "combine"]
 
     def parallel_profile(self):
         """Mean device us per scoring call in each launch group of parallel scoring (profiling on)."""
-        a = (C.c_double * 9)()
-        _check(lib().gem_get_parallel_profile(self._h, a, 9))
+        n = len(self.PARALLEL_GROUPS)
+        a = (C.c_double * n)()
+        _check(lib().gem_get_parallel_profile(self._h, a, n))
         return dict(zip(self.PARALLEL_GROUPS, [round(v, 2) for v in a]))
 
     def last_launches(self) -> int:

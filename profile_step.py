@@ -1,6 +1,6 @@
 """Runs a few scoring calls of a synthetic workload, for profilers (ncu) to capture:
 
-  PYTHONPATH=prefix-head_b200 python -m gem_b200.profile_step [--model gemma3-270m] [--tokens 512]
+  python profile_step.py [--model gemma3-270m] [--tokens 512]
       [--calls 2] [--head two-level|full] [--schedule auto|sequential|pipelined|parallel] [--seqs 1]
       [--head-batch N]
 
@@ -10,10 +10,13 @@ N(0, 1) through gem_head_full_dev or gem_head_twolevel_dev, `calls` times."""
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
 
 import numpy as np
 
-from . import AUTO, FULL, PARALLEL, PIPELINED, SEQUENTIAL, TWO_LEVEL, Gemma, synth
+sys.path.insert(0, str(Path(__file__).resolve().parent / "prefix-head_b200"))
+from gem_b200 import AUTO, FULL, PARALLEL, PIPELINED, SEQUENTIAL, TWO_LEVEL, Gemma, synth  # noqa: E402
 
 
 def main(argv=None):

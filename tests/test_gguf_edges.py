@@ -77,3 +77,22 @@ def test_alignment_moves_tensor_data_not_results(small, tmp_path):
     a = orc.Model(small.gguf, ctx=32, threads=2).score(toks, 0)[0]
     b = orc.Model(p64, ctx=32, threads=2).score(toks, 0)[0]
     assert np.array_equal(a, b)  # same seed, same weights: only the data offsets differ
+
+
+@pytest.mark.gpu
+def test_tensor_offset_that_wraps_is_an_io_error(small, tmp_path):
+    """A crafted tensor offset chosen so that data start + offset wraps around 2^64 to the start of
+    the file: the bounds check works in checked arithmetic and rejects it (GEM_E_IO) instead of
+    reading the header's bytes as weights. Tensors are read after device setup, hence a GPU test."""
+    if not _has_gpu():
+        pytest.skip("no CUDA device")
+    import gguf
+    base = gguf.GGUFReader(str(small.gguf)).data_offset
+    b = bytearray(small.gguf.read_bytes())
+    name = b"token_embd.weight"
+    i = b.index(name) + len(name)
+    nd = struct.unpack_from("<I", b, i)[0]
+    struct.pack_into("<Q", b, i + 4 + 8 * nd + 4, (1 << 64) - base)
+    p = tmp_path / "wrap.gguf"
+    p.write_bytes(bytes(b))
+    assert _open_code(p) == GEM_E_IO
