@@ -689,6 +689,39 @@ def oracle_parity_qat(mf, toks, g, td, lp, am, head_bits):
     return {"argmax_equal": bool(np.array_equal(a, amo)), "max_abs_lp": err, "positions": SEQ_TOKENS}
 
 
+def run_tensor_cores(g, torch, stream, toks_d, lp_d, am_d, flush):
+    """The headline step with the body products on the tensor cores (tc_gemm.cu: tcgen05 MMAs form
+    each lane's exact int8 pair sums, the CUDA cores apply the reference's FMA per lane and block).
+    Its log-probs and argmax ids must equal the CUDA-core products' bit for bit; the products' device
+    time comes from the launch-group profile of a one-part pass, as for the headline's roofline."""
+    from gem_b200 import TWO_LEVEL
+    call = lambda: g.score_dev(toks_d.data_ptr(), SEQ_TOKENS, TWO_LEVEL, lp_d.data_ptr(), am_d.data_ptr())
+    call()
+    g.sync()
+    want_lp, want_am = lp_d.cpu().numpy().copy(), am_d.cpu().numpy().copy()
+    res = {}
+    for name, on in (("cuda_cores", False), ("tensor_cores", True)):
+        g.set_tensor_cores(on)
+        for _ in range(3):
+            call()
+        ms = time_dev(torch, stream, call, 5, flush)
+        same = bool(np.array_equal(lp_d.cpu().numpy().view(np.uint32), want_lp.view(np.uint32)) and
+                    np.array_equal(am_d.cpu().numpy(), want_am))
+        g.set_profiling(True)
+        for _ in range(2):
+            call()
+        torch.cuda.synchronize()
+        prof = g.parallel_profile()
+        g.set_profiling(False)
+        res[name] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
+                     "products_ms_per_step": round((prof["qkv"] + prof["o"] + prof["gate_up"] + prof["down"]) / 1e3, 3),
+                     "bit_identical_to_cuda_cores": same}
+    g.set_tensor_cores(False)
+    res["note"] = ("same workload and step as the headline; products_ms_per_step from the launch-group profile of a "
+                   "one-part pass; the headline runs the CUDA-core products")
+    return res
+
+
 def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
     """Secondary figures: the full head end to end, the head microbenchmark (full 262144x640 GEMV with
     fused log-sum-exp vs the two-level head, batch 1 and 64) and the CPU baseline."""
@@ -709,6 +742,7 @@ def run_extras(g, torch, stream, toks_d, lp_d, am_d, flush, args, mf):
         out[name] = {"value": round(SEQ_TOKENS / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 3),
                      "schedule": sched, "roofline": roof}
     g.set_schedule(AUTO)
+    out["tensor_cores"] = run_tensor_cores(g, torch, stream, toks_d, lp_d, am_d, flush)
     # full head, same sequence (two untimed calls: the first launches directly, the second is captured
     # as the CUDA graph the timed calls replay)
     for _ in range(2):

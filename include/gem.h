@@ -91,6 +91,13 @@ int gem_set_numerics(gem_model* m, int mode, int ref_threads);
  *   two-level head, else SEQUENTIAL. */
 enum { GEM_SCHEDULE_AUTO = 0, GEM_SCHEDULE_SEQUENTIAL = 1, GEM_SCHEDULE_PIPELINED = 2, GEM_SCHEDULE_PARALLEL = 3 };
 int gem_set_schedule(gem_model* m, int schedule);
+/* The parallel schedule's body products (q/k/v, o, gate/up, down) on the 5th-generation tensor cores
+ * (on != 0) or the CUDA cores (0, the default; GEM_TC=1 in the environment turns them on at gem_open).
+ * Both compute the reference's row dot bit for bit (q8.rs:257-270): the tensor cores form each lane's
+ * exact int8 pair sums (tcgen05.mma, f16 operands, f32 accumulators in tensor memory) and the CUDA
+ * cores apply the reference's one fp32 FMA per lane and block. Turning them on builds a tiled f16 copy
+ * of the body matrices (2.125 bytes per weight). No counterpart in the reference. */
+int gem_set_tensor_cores(gem_model* m, int on);
 /* Whether scoring with `head` (0 full, 1 two-level) runs pipelined; stages_ctas (nullable, 2 ints)
  * receives CTAs per layer stage and for the head stage. gem_last_error() then holds the reason. */
 int gem_get_schedule(gem_model* m, int head, int* pipelined, int* stages_ctas);

@@ -1,5 +1,6 @@
 // Kernel argument structs and launchers shared by the host runtime (runtime.cpp) and the kernels.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -22,6 +23,23 @@ struct MatView {
   const void* s = nullptr;
   int rows = 0, cols = 0, bits = 8, scale_f32 = 0;
 };
+
+// A Q8_0 / Q4_0 matrix tiled for the tensor-core product (tc_gemm.cu): per (row tile of 128, 32-block)
+// one 8704-byte chunk, the 128 x 32 weights as f16 in the MMA's K-major core-matrix order
+// ([8-row group][8-column group][8][8]) followed by the 128 scales as f32; rows past the last are zero.
+struct TcMat {
+  const unsigned char* tiles = nullptr;
+  int rows = 0, cols = 0;
+};
+bool tc_gemm_supported(const MatView& w);
+size_t tc_tiled_bytes(const MatView& w);
+// Builds the tiled copy of w into buf (tc_tiled_bytes), asynchronously on st.
+void tc_tile(const MatView& w, void* buf, TcMat* out, cudaStream_t st);
+// Y[t][r] (row stride ldy) = the exact row dot of W[r] and the quantized activation t (aq [T][cols],
+// as [T][cols/32]), bit-identical to launch_seq_gemm; err receives ERR_TIMEOUT if a bounded wait
+// gives up.
+void launch_tc_gemm(const TcMat& W, const int8_t* aq, const float* as, int T, float* y, int ldy, int* err, int sms,
+                    cudaStream_t st);
 
 #ifdef __CUDACC__
 // Mat::weight (q8.rs:112-126): the dequantized weight at row r, column j -- the bit-exact dequant
@@ -231,7 +249,8 @@ inline void launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at, cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k, args...);
+  // a refused launch is retried as a plain one, which records its error for cudaGetLastError
+  if (cudaLaunchKernelEx(&cfg, k, args...) != cudaSuccess) k<<<grid, block, smem, st>>>(args...);
 }
 #endif
 

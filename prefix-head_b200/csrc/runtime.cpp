@@ -99,6 +99,7 @@ struct Layer {
         *post_ffw = nullptr, *bqkv = nullptr;
   bool swa = false;
   DevMat q_only, k_only, v_only, gate_only, up_only;  // views into qkv / gu for gem_matvec_dev
+  TcMat tqkv, to, tgu, tdown;  // tiled copies for the tensor-core products (built by ensure_tc)
 };
 
 }  // namespace
@@ -146,6 +147,9 @@ struct gem_model {
   uint32_t *cls_of = nullptr, *pos_of = nullptr, *order = nullptr;
   // numerics: exact = bit-identical to the reference's AVX-512 path with a pool of ref_threads
   bool exact = true;
+  // the parallel schedule's body products on the tensor cores (tc_gemm.cu) instead of the CUDA cores;
+  // GEM_TC=1 in the environment turns them on at gem_open
+  bool tc = false, tc_ready = false;
   int ref_threads = 8;
   float *qn = nullptr, *scores = nullptr, *top_inner = nullptr;
   uint32_t* top_of = nullptr;
@@ -341,6 +345,28 @@ struct gem_model {
       top_of = alloc<uint32_t>(batch);
     }
     hbatch = batch;
+  }
+
+  // The tensor-core products' tiled copies of every layer's matrices (2.125 bytes per weight).
+  void ensure_tc() {
+    if (tc_ready) return;
+    for (Layer& L : layers)
+      for (auto [M, TM] : {std::pair<const DevMat*, TcMat*>{&L.qkv, &L.tqkv}, {&L.o, &L.to}, {&L.gu, &L.tgu}, {&L.down, &L.tdown}}) {
+        if (!tc_gemm_supported(M->v)) throw Error(GEM_E_STATE, "tensor-core products need Q8_0/Q4_0 body weights");
+        unsigned char* buf = alloc<unsigned char>(tc_tiled_bytes(M->v));
+        tc_tile(M->v, buf, TM, st);
+      }
+    ck(cudaGetLastError(), "tile for the tensor cores");
+    ck(cudaStreamSynchronize(st), "tile for the tensor cores");
+    tc_ready = true;
+  }
+  // One of a layer's exact int8 products, Y[t][r] for the chunk's n positions: on the tensor cores
+  // when they are on and the chunk fills a tile of positions, else on the CUDA cores. Both are
+  // bit-identical.
+  void product(const DevMat& M, const TcMat& TM, const int8_t* aq, const float* as, int n, float* y, int ldy,
+               cudaStream_t s, int parts) {
+    if (tc && tc_ready && n >= 16) launch_tc_gemm(TM, aq, as, n, y, ldy, err, sms, s);
+    else launch_seq_gemm(M.v, aq, as, n, y, ldy, sms, s, parts);
   }
 
   AttnArgs attn_args(int l, int seq) const {
@@ -747,22 +773,22 @@ struct gem_model {
             launch_seq_norm(q.x, P ? q.dn : nullptr, P ? P->post_ffw : nullptr, Ly.attn_norm, eps, d, q.n, q.aq, q.as, nullptr,
                             q.s);
             par_mark(PAR_NORM);
-            launch_seq_gemm(Ly.qkv.v, q.aq, q.as, q.n, q.y, qkv_rows, sms, q.s, parts);
+            product(Ly.qkv, Ly.tqkv, q.aq, q.as, q.n, q.y, qkv_rows, q.s, parts);
             par_mark(PAR_QKV);
             if (k > 0) ck(cudaStreamWaitEvent(q.s, split_ev[(size_t)(k - 1) * nl + l], 0), "layer");
             launch_seq_attn(attn_args(l, 0), q.y, qkv_rows, q.L, ns, pos0 + (uint32_t)q.r0, kv_stride, q.qn, q.sc,
                             seq_sstride, ref_threads, q.part, q.aq, q.as, q.s,
                             k + 1 < parts ? split_ev[(size_t)k * nl + l] : nullptr);
             par_mark(PAR_ATTN);
-            launch_seq_gemm(Ly.o.v, q.aq, q.as, q.n, q.y, d, sms, q.s, parts);
+            product(Ly.o, Ly.to, q.aq, q.as, q.n, q.y, d, q.s, parts);
             par_mark(PAR_O);
             launch_seq_norm(q.x, q.y, Ly.post_attn, Ly.ffn_norm, eps, d, q.n, q.aq, q.as, nullptr, q.s);
             par_mark(PAR_NORM);
-            launch_seq_gemm(Ly.gu.v, q.aq, q.as, q.n, q.gu, 2 * ff, sms, q.s, parts);
+            product(Ly.gu, Ly.tgu, q.aq, q.as, q.n, q.gu, 2 * ff, q.s, parts);
             par_mark(PAR_GU);
             launch_seq_glu_quant(q.gu, ff, q.n, silu ? 1 : 0, q.aq, q.as, sms, q.s);
             par_mark(PAR_GLU);
-            launch_seq_gemm(Ly.down.v, q.aq, q.as, q.n, q.dn, d, sms, q.s, parts);
+            product(Ly.down, Ly.tdown, q.aq, q.as, q.n, q.dn, d, q.s, parts);
             par_mark(PAR_DOWN);
             nk += 12;  // 2 norms, 4 matrix products, 5 attention kernels, the gate
           }
@@ -1253,6 +1279,10 @@ int gem_open(const char* gguf_path, int ctx, int body_bits, int head_bits, int d
   ck(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking), "stream");
   load_model(m.get(), g, body_bits, head_bits);
   ck(cudaDeviceSynchronize(), "load");
+  if (const char* e = std::getenv("GEM_TC"); e && std::atoi(e) == 1 && m->seq_supported()) {
+    m->ensure_tc();
+    m->tc = true;
+  }
   *out = m.release();
   API_END
 }
@@ -1364,6 +1394,17 @@ int gem_set_schedule(gem_model* m, int schedule) {
   if (!m) throw Error(GEM_E_ARG, "null argument");
   if (schedule < GEM_SCHEDULE_AUTO || schedule > GEM_SCHEDULE_PARALLEL) throw Error(GEM_E_ARG, "unknown schedule");
   m->schedule = schedule;
+  API_END
+}
+
+int gem_set_tensor_cores(gem_model* m, int on) {
+  API_BEGIN
+  if (!m) throw Error(GEM_E_ARG, "null argument");
+  ck(cudaSetDevice(m->device), "cudaSetDevice");
+  m->sync();
+  if (on) m->ensure_tc();
+  m->tc = on != 0;
+  m->drop_graphs();  // a replayed graph holds the other products' launches
   API_END
 }
 

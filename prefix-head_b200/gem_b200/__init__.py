@@ -16,7 +16,8 @@ import numpy as np
 
 PKG = Path(__file__).resolve().parents[1]          # prefix-head_b200/
 LIB = PKG / "_build" / "libgem_b200.so"
-SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "pipeline.cu", "noalloc.cu", "exact.cuh", "pipeline.cuh", "common.cuh", "kernels.cuh",
+SOURCES = [PKG / "csrc" / f for f in ("kernels.cu", "kernels_exact.cu", "pipeline.cu", "seq.cu", "decode.cu", "tc_gemm.cu",
+                                      "noalloc.cu", "exact.cuh", "pipeline.cuh", "common.cuh", "kernels.cuh",
                                       "internal.hpp", "host.cpp", "host.hpp", "runtime.cpp")]
 
 GEM_OK = 0
@@ -68,6 +69,7 @@ def lib():
     L.gem_sync.argtypes = [vp]
     L.gem_get_stream.argtypes = [vp, C.POINTER(vp)]
     L.gem_set_schedule.argtypes = [vp, C.c_int]
+    L.gem_set_tensor_cores.argtypes = [vp, C.c_int]
     L.gem_test_withhold_stage.argtypes = [vp, C.c_int, C.c_int]
     L.gem_set_profiling.argtypes = [vp, C.c_int]
     L.gem_get_phase_profile.argtypes = [vp, C.POINTER(C.c_double), C.c_int, C.POINTER(C.c_double), C.c_int]
@@ -175,6 +177,10 @@ class Gemma:
         """EXACT: bit-identical to the reference's AVX-512 path with a pool of ref_threads threads.
         FAST: tree reductions (within the reference's own cross-ISA spread)."""
         _check(lib().gem_set_numerics(self._h, mode, ref_threads))
+
+    def set_tensor_cores(self, on: bool = True):
+        """The parallel schedule's body products on the tensor cores (bit-identical to the CUDA cores)."""
+        _check(lib().gem_set_tensor_cores(self._h, 1 if on else 0))
 
     def set_schedule(self, schedule: int = AUTO):
         """SEQUENTIAL: a CUDA graph per token. PIPELINED: two-level scoring as one layer-pipelined kernel.
