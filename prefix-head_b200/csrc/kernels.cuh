@@ -192,6 +192,13 @@ void launch_attn_exact(const AttnArgs& A, float* qn, float* scores, int sstride,
 void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t st);
 void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, int block_ctas, cudaStream_t st);
 void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_of, float* top_inner, cudaStream_t st);
+// The whole exact two-level head in one launch (cnt: batch counters, zero between launches).
+// The exact two-level head in one launch: P = tl_parts(...) CTAs per hidden state, cnt[batch] zero
+// between launches, part[batch][tl_part_floats(k, per)] floats of per-CTA partials; false (nothing
+// launched) when its staging area does not fit in shared memory.
+int tl_parts(int k, int per, int batch, int sms);
+int tl_part_floats(int k, int per);
+bool launch_tl_fused(const TwoLevelArgs& T, int batch, int sms, int* cnt, float* part, cudaStream_t st);
 
 // Sequence-parallel scoring (seq.cu): every position of a chunk through one layer at a time, with the
 // exact per-position arithmetic above. Activations are [T][n] row-major, scales [T][n/32].

@@ -561,6 +561,396 @@ __global__ void k_tl_top_exact(TwoLevelArgs T, const uint32_t* top_of, float* to
 }
 
 // ------------------------------------------------------------------------------------------------
+// The two-level head in one launch (TwoLevel::logprob, main.rs:82-107, and the greedy token of
+// lean.rs:46-76 with top = 1). The tasks of one hidden state are its k class logits dot512(A[c], h) +
+// b[c] on the fp32 hidden state and the rows of the target class's block: the row dot on the
+// quantized hidden state (dot_avx512 / dot4_avx512) or on the fp32 one (dot16_avx512 for an F16
+// matrix). They spread over P CTAs in contiguous ranges; a CTA takes its range in rounds of 32 tasks,
+// one 16-thread group per task and one of the dot's 16 lanes per thread, in the reference's order.
+// A round's class rows and block rows are each one contiguous range of memory: one bulk copy each
+// into shared memory (the class rows of the first round are requested before the wait on the previous
+// kernel: they depend on nothing it writes), the block rows' scales by plain loads. Each CTA leaves its
+// partial class log-sum-exp and most likely class, and the target block's log-sum-exp; the last CTA
+// of a hidden state (a per-item counter, zero between launches) merges them, stages the most likely
+// class's block in one copy (unless it is the target's, whose logits are already written) and takes
+// its first maximum: the greedy token.
+// ------------------------------------------------------------------------------------------------
+constexpr int kTlThreads = 512, kTlGroups = kTlThreads / 16, kTlPart = 12;
+
+// Lane i of dot512 (model.rs:106-120) on a row in shared memory: the sum over chunks c of
+// a[16c + i] * x[16c + i], fused, in order.
+__device__ __forceinline__ float lane512_s(const float* a, const float* sx, int nc, int i) {
+  float acc = 0.0f;
+#pragma unroll 8
+  for (int c = 0; c < nc; ++c) acc = fmaf(a[16 * c + i], sx[16 * c + i], acc);
+  return acc;
+}
+
+// Lane i of the reference's row dot on a row in shared memory: Q8_0 / Q4_0 rows against the quantized
+// hidden state (lane i is the madd pair 2i, 2i + 1 of every 32-block, one FMA per block with scale
+// ws * as; sc holds the row's scales as fp32), F16 rows against the fp32 one (lane i sums w[16c + i] *
+// x[16c + i]).
+template <int BITS>
+__device__ __forceinline__ float lane_row_s(const unsigned char* q, const float* sc, int d, int i, const int8_t* saq,
+                                            const float* sas, const float* sx) {
+  float acc = 0.0f;
+  if constexpr (BITS == 16) {
+    const __half* row = (const __half*)q;
+#pragma unroll 8
+    for (int c = 0; c < d / 16; ++c) acc = fmaf(__half2float(row[16 * c + i]), sx[16 * c + i], acc);
+  } else {
+#pragma unroll 4
+    for (int b = 0; b < d / 32; ++b) {
+      int w0, w1;
+      if constexpr (BITS == 8) {
+        const uint16_t wp = *((const uint16_t*)(q + 32 * b) + i);
+        w0 = (int)(int8_t)(wp & 0xffu), w1 = (int)(int8_t)(wp >> 8);
+      } else {  // q8.rs:42-52: byte j holds weight j (low nibble) and j + 16 (high nibble), each + 8
+        const uint16_t wp = *((const uint16_t*)(q + 16 * b) + (i & 7));
+        const int sh = i < 8 ? 0 : 4;
+        w0 = (int)((wp >> sh) & 15u) - 8, w1 = (int)((wp >> (8 + sh)) & 15u) - 8;
+      }
+      const int p = w0 * (int)saq[32 * b + 2 * i] + w1 * (int)saq[32 * b + 2 * i + 1];
+      acc = fmaf((float)p, mul(sc[b], sas[b]), acc);
+    }
+  }
+  return acc;
+}
+
+// The halving reduction of the 16 lanes held by 16 consecutive threads of a half-warp (lane i in its
+// thread i): lanes i + 8 onto i, then 4, 2, 1 apart (_mm512_reduce_add_ps). The group's first thread
+// gets the result. The shuffles name only the group's 16 threads: the two halves of a warp run
+// separate tasks and may leave their loops at different times.
+__device__ __forceinline__ float reduce16_group(float v) {
+  const unsigned m = 0xffffu << (threadIdx.x & 16);
+  v = add(v, __shfl_down_sync(m, v, 8, 16));
+  v = add(v, __shfl_down_sync(m, v, 4, 16));
+  v = add(v, __shfl_down_sync(m, v, 2, 16));
+  return add(v, __shfl_down_sync(m, v, 1, 16));
+}
+
+// Bytes of one output-matrix row's weights (Q8_0: d, Q4_0: d / 2, F16: 2d).
+__host__ __device__ constexpr size_t tl_row_bytes(int bits, int d) {
+  return bits == 16 ? (size_t)d * 2 : bits == 8 ? (size_t)d : (size_t)d / 2;
+}
+// Shared memory of k_tl_fused: the hidden state (fp32, int8, block scales), then the staging area:
+// weights of max(32 class rows, rows_b block rows), the block rows' scales as fp32, the top block's
+// token ids.
+__host__ __device__ constexpr size_t tl_head_off(int d) { return ((size_t)d * 5 + (size_t)d / 8 + 127) & ~(size_t)127; }
+__host__ __device__ constexpr size_t tl_stage_q(int bits, int d, int rows_b) {
+  return (size_t)kTlGroups * 4 * d > (size_t)rows_b * tl_row_bytes(bits, d) ? (size_t)kTlGroups * 4 * d
+                                                                              : (size_t)rows_b * tl_row_bytes(bits, d);
+}
+__host__ __device__ constexpr size_t tl_smem(int bits, int d, int rows_b) {
+  return tl_head_off(d) + tl_stage_q(bits, d, rows_b) + (size_t)(rows_b > kTlGroups ? rows_b : kTlGroups) * (d / 32) * 4 +
+         (size_t)rows_b * 4;
+}
+
+// Lanes i of four rows of the reference's row dot (the 16-lane order of lane_row_s), rows q[u] in
+// shared memory: four independent FMA chains, each in order. For Q8_0 / Q4_0 rows sc[u][b] holds the
+// block's scale product RN(ws * as); the pair sum w0 a0 + w1 a1 is one dp4a (exact in int32; Q4_0's
+// nibbles carry +8, taken off as 8 (a0 + a1)).
+template <int BITS>
+__device__ __forceinline__ void lane_rows4_s(const unsigned char* const (&q)[4], const float* const (&sc)[4], int d, int i,
+                                             const int8_t* saq, const float* sx, float (&acc)[4]) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) acc[u] = 0.0f;
+  if constexpr (BITS == 16) {
+#pragma unroll 4
+    for (int c = 0; c < d / 16; ++c) {
+      const float x = sx[16 * c + i];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] = fmaf(__half2float(((const __half*)q[u])[16 * c + i]), x, acc[u]);
+    }
+  } else {
+    const int sh = i < 8 ? 0 : 4;
+#pragma unroll 2
+    for (int b = 0; b < d / 32; ++b) {
+      const int ap = *((const uint16_t*)(saq + 32 * b) + i);  // a0, a1 as signed bytes, upper bytes zero
+      const int off8 = BITS == 4 ? 8 * ((int)(int8_t)(ap & 0xff) + (int)(int8_t)(ap >> 8)) : 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        int p;
+        if constexpr (BITS == 8) {
+          p = __dp4a((int)*((const uint16_t*)(q[u] + 32 * b) + i), ap, 0);
+        } else {  // q8.rs:42-52: byte j holds weight j (low nibble) and j + 16 (high nibble), each + 8
+          const int wp = *((const uint16_t*)(q[u] + 16 * b) + (i & 7));
+          p = __dp4a((wp >> sh) & 0x0f0f, ap, 0) - off8;
+        }
+        acc[u] = fmaf((float)p, sc[u][b], acc[u]);
+      }
+    }
+  }
+}
+
+// Per-CTA partial of the two-level head: class log-sum-exp and most likely class, the target block's
+// log-sum-exp and first maximum, and the target's class logit and row logit where this CTA computed them.
+struct TlAcc {
+  Lse c;
+  Best bc;
+  Lse t;
+  Best bt;
+};
+__device__ __forceinline__ TlAcc tl_acc0() {
+  return TlAcc{Lse{-INFINITY, 0.0f}, Best{-INFINITY, 0xffffffffu}, Lse{-INFINITY, 0.0f}, Best{-INFINITY, 0xffffffffu}};
+}
+// Merges 32 lanes' partials: maxima first, then the sums rescaled to them (one exp per lane).
+__device__ __forceinline__ TlAcc tl_warp_merge(TlAcc v) {
+  float mc = v.c.m, mt = v.t.m;
+  for (int o = 16; o > 0; o >>= 1) {
+    mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+  }
+  float sc = v.c.m == -INFINITY ? 0.0f : v.c.s * expf(v.c.m - mc);
+  float st = v.t.m == -INFINITY ? 0.0f : v.t.s * expf(v.t.m - mt);
+  for (int o = 16; o > 0; o >>= 1) {
+    sc += __shfl_xor_sync(0xffffffffu, sc, o);
+    st += __shfl_xor_sync(0xffffffffu, st, o);
+    v.bc = best_merge(v.bc, Best{__shfl_xor_sync(0xffffffffu, v.bc.v, o), __shfl_xor_sync(0xffffffffu, v.bc.tok, o)});
+    v.bt = best_merge(v.bt, Best{__shfl_xor_sync(0xffffffffu, v.bt.v, o), __shfl_xor_sync(0xffffffffu, v.bt.tok, o)});
+  }
+  return TlAcc{Lse{mc, sc}, v.bc, Lse{mt, st}, v.bt};
+}
+
+// The target of hidden state bi (an id >= vocab is replaced by 0; the last CTA reports it), its class,
+// its place in the class and that class's rows [first, first + n) of the class-ordered matrix.
+struct TlTarget {
+  uint32_t tok, ct, pos, first;
+  int n;
+  bool bad;
+};
+__device__ __forceinline__ TlTarget tl_target(const TwoLevelArgs& T, int bi) {
+  uint32_t t = T.targets ? T.targets[bi] : T.cur->target;
+  const bool bad = t >= (uint32_t)T.vocab;
+  if (bad) t = 0;
+  const uint32_t c = T.cls_of[t], f = c * T.per;
+  return TlTarget{t, c, T.pos_of[t], f, (int)min((uint32_t)T.per, (uint32_t)T.w.rows - f), bad};
+}
+
+// n scales of whole rows' blocks (nb a row) as fp32 in shared memory, times the hidden state's block
+// scale (RN(ws * as), the factor of the row dot's FMA) when sas is given: eight independent loads in
+// flight per thread.
+template <typename ST>
+__device__ __forceinline__ void tl_stage_scales(float* dst, const ST* src, int n, int nb, const float* sas) {
+  for (int e0 = threadIdx.x; e0 < n; e0 += 8 * kTlThreads) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * kTlThreads;
+      v[u] = e < n ? ld_scale(src, e) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * kTlThreads;
+      if (e < n) dst[e] = sas ? mul(v[u], sas[e % nb]) : v[u];
+    }
+  }
+}
+
+template <int BITS, typename ST>
+__global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, int rows_b, int* cnt, float* part) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];  // bulk copies land on 16-byte boundaries
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ TlAcc red[kTlGroups];  // one partial per 16-thread group
+  __shared__ int s_last;
+  __shared__ float s_zcl, s_zin, s_lse_cl, s_lse_t;
+  __shared__ uint32_t s_top, s_jt;
+  const int bi = blockIdx.y, d = T.w.cols, nb = d / 32, nc = d / 16;
+  const int g = threadIdx.x >> 4, i = threadIdx.x & 15, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const size_t RB = tl_row_bytes(BITS, d);
+  float* sx = (float*)smem_raw;     // the fp32 hidden state [d]
+  int8_t* saq = (int8_t*)(sx + d);  // quantized [d]
+  float* sas = (float*)(saq + d);   // its block scales [d / 32]
+  unsigned char* stage = smem_raw + tl_head_off(d);
+  float* ssc = (float*)(stage + tl_stage_q(BITS, d, rows_b));                   // staged rows' scales
+  uint32_t* sorder = (uint32_t*)(ssc + (size_t)max(rows_b, kTlGroups) * nb);  // the top block's token ids
+  const int tasks_max = T.k + T.per, tpc = (tasks_max + P - 1) / P;
+  const int t_begin = blockIdx.x * tpc;
+  int t_end = min(tasks_max, t_begin + tpc);
+  const uint32_t abar = smem_u32(&bar);
+  // the first round's class rows: A depends on no earlier kernel, so its copy starts before the wait
+  const int c0_end = min(min(t_begin + kTlGroups, t_end), T.k);
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(abar));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (c0_end > t_begin) {
+      const uint32_t bytes = (uint32_t)(c0_end - t_begin) * 4u * d;
+      asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(abar), "r"(bytes) : "memory");
+      hb_issue(stage, T.A + (size_t)t_begin * d, bytes, &bar);
+    }
+    s_zcl = NAN, s_zin = NAN;
+  }
+  pdl_wait();
+  // the hidden state: fp32 (its first 1536 values requested before the target lookup's dependent loads),
+  // and Act::quantize, a warp per 32-block (q8.rs:187-246)
+  const float* hrow = T.h + (size_t)bi * d;
+  float hv[3];
+#pragma unroll
+  for (int u = 0; u < 3; ++u) hv[u] = threadIdx.x + u * kTlThreads < d ? hrow[threadIdx.x + u * kTlThreads] : 0.0f;
+  const TlTarget tg = tl_target(T, bi);
+#pragma unroll
+  for (int u = 0; u < 3; ++u)
+    if (threadIdx.x + u * kTlThreads < d) sx[threadIdx.x + u * kTlThreads] = hv[u];
+  for (int j = threadIdx.x + 3 * kTlThreads; j < d; j += kTlThreads) sx[j] = hrow[j];
+  __syncthreads();
+  for (int b = warp; b < nb; b += kTlThreads / 32) {
+    const float v = sx[32 * b + lane];
+    const float amax = warp_max(fabsf(v));
+    const float dd = div(amax, 127.0f);
+    const float inv = dd > 0.0f ? div(1.0f, dd) : 0.0f;
+    saq[32 * b + lane] = (int8_t)__float2int_rn(mul(v, inv));
+    if (lane == 0) sas[b] = dd;
+  }
+  t_end = min(t_end, T.k + tg.n);
+  TlAcc v = tl_acc0();
+  bool ok = true;
+  uint32_t parity = 0;
+  for (int t0 = t_begin, r = 0; t0 < t_end && ok; t0 += kTlGroups, ++r) {
+    const int n = min(kTlGroups, t_end - t0);
+    const int nca = max(0, min(t0 + n, T.k) - t0);         // the round's class rows [t0, t0 + nca)
+    const int ja = max(t0, T.k) - T.k, jb = t0 + n - T.k;  // and block rows [ja, jb) of the target class
+    const int t = t0 + g;
+    const float bias = g < nca && i == 0 ? T.b[t] : 0.0f;  // loads while the rows land
+    if (r > 0) __syncthreads();  // every group is done with the previous round's rows
+    if (threadIdx.x == 0) {      // round 0's class rows are on their way already
+      const uint32_t cbytes = r == 0 ? 0u : (uint32_t)nca * 4u * d;
+      const uint32_t bbytes = jb > ja ? (uint32_t)((jb - ja) * RB) : 0u;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(abar), "r"(cbytes + bbytes) : "memory");
+      if (cbytes) hb_issue(stage, T.A + (size_t)t0 * d, cbytes, &bar);
+      if (bbytes) hb_issue(stage + (size_t)nca * 4 * d, (const unsigned char*)T.w.q + (tg.first + ja) * RB, bbytes, &bar);
+    }
+    if constexpr (BITS != 16)
+      if (jb > ja) tl_stage_scales(ssc, (const ST*)T.w.s + (size_t)(tg.first + ja) * nb, (jb - ja) * nb, nb, (const float*)nullptr);
+    __syncthreads();  // the scales (and, in round 0, the hidden state) are in place
+    ok = __syncthreads_and(hb_wait(&bar, parity));  // one verdict for the whole CTA
+    parity ^= 1u;
+    if (!ok) {
+      if (threadIdx.x == 0) atomicExch(T.err, ERR_TIMEOUT);
+      break;
+    }
+    if (g < n) {
+      if (t < T.k) {
+        const float z = reduce16_group(lane512_s((const float*)stage + (size_t)g * d, sx, nc, i));
+        if (i == 0) {
+          const float zc = add(z, bias);
+          v.c = lse_add(v.c, zc);
+          v.bc = best_merge(v.bc, Best{zc, (uint32_t)t});
+          if ((uint32_t)t == tg.ct) s_zcl = zc;
+        }
+      } else {
+        const int jr = g - nca;  // this row's place among the round's block rows
+        const float z = reduce16_group(
+            lane_row_s<BITS>(stage + (size_t)nca * 4 * d + jr * RB, ssc + (size_t)jr * nb, d, i, saq, sas, sx));
+        if (i == 0) {
+          const uint32_t j = (uint32_t)(t - T.k);
+          v.t = lse_add(v.t, z);
+          v.bt = best_merge(v.bt, Best{z, j});
+          if (j == tg.pos) s_zin = z;
+        }
+      }
+    }
+  }
+  if (i == 0) red[g] = v;  // a group's partials sit in its first thread
+  __syncthreads();
+  if (warp == 0) v = tl_warp_merge(red[lane]);
+  if (threadIdx.x == 0) {
+    float4* p = (float4*)(part + ((size_t)bi * P + blockIdx.x) * kTlPart);
+    p[0] = make_float4(v.c.m, v.c.s, v.bc.v, __uint_as_float(v.bc.tok));
+    p[1] = make_float4(v.t.m, v.t.s, v.bt.v, __uint_as_float(v.bt.tok));
+    p[2] = make_float4(s_zcl, s_zin, 0.0f, 0.0f);
+    __threadfence();  // the partial before the count
+    s_last = atomicAdd(cnt + bi, 1) == P - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // ---- the last CTA: one warp merges the partials ----
+  if (warp == 0) {
+    v = tl_acc0();
+    for (int j = lane; j < P; j += 32) {
+      const float4* p = (const float4*)(part + ((size_t)bi * P + j) * kTlPart);
+      const float4 a = __ldcg(p), b = __ldcg(p + 1), c = __ldcg(p + 2);
+      v.c = lse_merge(v.c, Lse{a.x, a.y});
+      v.bc = best_merge(v.bc, Best{a.z, __float_as_uint(a.w)});
+      v.t = lse_merge(v.t, Lse{b.x, b.y});
+      v.bt = best_merge(v.bt, Best{b.z, __float_as_uint(b.w)});
+      if (!isnan(c.x)) s_zcl = c.x;  // exactly one CTA computed each
+      if (!isnan(c.y)) s_zin = c.y;
+    }
+    v = tl_warp_merge(v);
+    if (lane == 0) {
+      if (tg.bad) atomicExch(T.err, ERR_RANGE);
+      s_lse_cl = v.c.m + logf(v.c.s);
+      s_lse_t = v.t.m + logf(v.t.s);
+      s_top = v.bc.tok < (uint32_t)T.k ? v.bc.tok : 0;  // only NaN logits leave no candidate
+      s_jt = v.bt.tok;
+    }
+  }
+  __syncthreads();
+  const uint32_t top = s_top, first = top * T.per;
+  const int n = (int)min((uint32_t)T.per, (uint32_t)T.w.rows - first);
+  // the most likely class's block: its first maximum (the target block's, already merged, when they are
+  // the same class); its token ids load while its logits are computed
+  const bool ids_staged = n <= rows_b;
+  if (ids_staged)
+    for (int j = threadIdx.x; j < n; j += kTlThreads) sorder[j] = T.order[first + j];
+  Best bt{-INFINITY, 0xffffffffu};
+  if (top == tg.ct) {
+    if (threadIdx.x == 0) bt = Best{0.0f, s_jt};
+  } else if (ok) {
+    for (int j0 = 0; j0 < n && ok; j0 += rows_b) {
+      const int m = min(rows_b, n - j0);
+      __syncthreads();  // every group is done with the staging area
+      if (threadIdx.x == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(abar), "r"((uint32_t)(m * RB)) : "memory");
+        hb_issue(stage, (const unsigned char*)T.w.q + (first + j0) * RB, (uint32_t)(m * RB), &bar);
+      }
+      if constexpr (BITS != 16) tl_stage_scales(ssc, (const ST*)T.w.s + (size_t)(first + j0) * nb, m * nb, nb, sas);
+      __syncthreads();
+      ok = __syncthreads_and(hb_wait(&bar, parity));
+      parity ^= 1u;
+      if (!ok) {
+        if (threadIdx.x == 0) atomicExch(T.err, ERR_TIMEOUT);
+        break;
+      }
+      // four rows per group at once: j, j + 32, j + 64, j + 96 (a row past the end repeats row j)
+      for (int j = g; j < m; j += 4 * kTlGroups) {
+        const unsigned char* q4[4];
+        const float* s4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int ju = j + u * kTlGroups < m ? j + u * kTlGroups : j;
+          q4[u] = stage + ju * RB;
+          s4[u] = ssc + (size_t)ju * nb;
+        }
+        float acc[4];
+        lane_rows4_s<BITS>(q4, s4, d, i, saq, sx, acc);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float z = reduce16_group(acc[u]);
+          if (i == 0 && j + u * kTlGroups < m) bt = best_merge(bt, Best{z, (uint32_t)(j0 + j + u * kTlGroups)});
+        }
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1)
+    bt = best_merge(bt, Best{__shfl_xor_sync(0xffffffffu, bt.v, o), __shfl_xor_sync(0xffffffffu, bt.tok, o)});
+  __syncthreads();
+  if (lane == 0) red[warp].bt = bt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kTlThreads / 32; ++w) bt = best_merge(bt, red[w].bt);
+    const uint32_t slot = T.targets ? (uint32_t)bi : T.cur->slot;
+    const uint32_t jbest = bt.tok < (uint32_t)n ? bt.tok : 0;
+    if (T.lp_out) T.lp_out[slot] = s_zcl - s_lse_cl + s_zin - s_lse_t;
+    if (T.am_out) T.am_out[slot] = ids_staged ? sorder[jbest] : T.order[first + jbest];
+    cnt[bi] = 0;  // zero for the next launch
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 #define GEM_DISPATCH_X(bits, scale_f32, F)                    \
   do {                                                        \
     if ((bits) == 8 && !(scale_f32)) { F(8, __half); }        \
@@ -632,6 +1022,31 @@ void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, in
   } while (0)
   GEM_DISPATCH_X(T.w.bits, T.w.scale_f32, F);
 #undef F
+}
+
+int tl_parts(int k, int per, int batch, int sms) {
+  const int most = (k + per + 15) / 16;  // at least 16 tasks per CTA
+  return std::max(1, std::min(most, batch <= 1 ? sms : 2 * sms / batch));
+}
+int tl_part_floats(int k, int per) { return (k + per + 15) / 16 * kTlPart; }
+
+bool launch_tl_fused(const TwoLevelArgs& T, int batch, int sms, int* cnt, float* part, cudaStream_t st) {
+  constexpr size_t kMax = 200 * 1024;
+  const int d = T.w.cols;
+  int rows_b = T.per;  // the most likely class's block in one copy where it fits
+  while (rows_b > 16 && tl_smem(T.w.bits, d, rows_b) > kMax) rows_b -= 16;
+  if (d % 32 || tl_smem(T.w.bits, d, rows_b) > kMax) return false;
+  const int P = tl_parts(T.k, T.per, batch, sms);
+  const size_t sm = tl_smem(T.w.bits, d, rows_b);
+#define F(B, S)                                                                                     \
+  do {                                                                                              \
+    static bool init = false;                                                                       \
+    if (!init) { cudaFuncSetAttribute(k_tl_fused<B, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMax); init = true; } \
+    launch_k(k_tl_fused<B, S>, dim3(P, batch), dim3(kTlThreads), sm, st, T, P, rows_b, cnt, part);   \
+  } while (0)
+  GEM_DISPATCH_X(T.w.bits, T.w.scale_f32, F);
+#undef F
+  return true;
 }
 
 void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_of, float* top_inner, cudaStream_t st) {

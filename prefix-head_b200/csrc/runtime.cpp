@@ -137,6 +137,8 @@ struct gem_model {
   int hbatch = 0;
   float *head_part = nullptr, *tlogit = nullptr, *cl = nullptr, *inner = nullptr;
   int* head_cnt = nullptr;  // the streamed full head's finished-CTA counters, one per batch item
+  int* tl_cnt = nullptr;    // the fused two-level head's finished-CTA counters, one per batch item
+  float* tl_part = nullptr;  // and its per-CTA partials
   int8_t* hb_q = nullptr;  // batched head calls: quantized hidden states [batch][d] and their scales
   float* hb_s = nullptr;
   // two-level (main.rs:40-51)
@@ -336,6 +338,9 @@ struct gem_model {
     tlogit = alloc<float>(batch);
     head_cnt = alloc<int>(batch);  // the streamed head's finished-CTA counters: zero between launches
     ck(cudaMemsetAsync(head_cnt, 0, (size_t)batch * sizeof(int), st), "head counters");
+    tl_cnt = alloc<int>(batch);
+    ck(cudaMemsetAsync(tl_cnt, 0, (size_t)batch * sizeof(int), st), "head counters");
+    if (two) tl_part = alloc<float>((size_t)batch * tl_part_floats(k, per));
     hb_q = alloc<int8_t>((size_t)batch * d);
     hb_s = alloc<float>((size_t)batch * d / 32);
     if (two) {
@@ -473,10 +478,14 @@ struct gem_model {
       launch_head_twolevel(T, batch, sms, st);
       return;
     }
-    int class_ctas = std::max(1, std::min(sms, (k + 15) / 16));  // one 16-class task per CTA where possible
-    int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
-    T.class_ctas = class_ctas;
-    launch_tl_stage1_exact(T, batch, class_ctas, block_ctas, st);
+    if (launch_tl_fused(T, batch, sms, tl_cnt, tl_part, st)) return;  // quantizes hh itself
+    // a hidden size whose staging area does not fit in shared memory: four launches
+    if (!qa) {
+      launch_quantize(hh, batch * d, hb_q, hb_s, st);
+      T.aq = hb_q, T.as = hb_s;
+    }
+    T.class_ctas = std::max(1, std::min(sms, (k + 15) / 16));  // one 16-class task per CTA where possible
+    launch_tl_stage1_exact(T, batch, T.class_ctas, std::max(1, std::min(8, (per + 127) / 128)), st);
     launch_tl_select(T, batch, top_of, st);
     launch_tl_top_exact(T, batch, top_of, top_inner, st);
     launch_tl_argmax(T, batch, top_of, top_inner, st);
@@ -1899,13 +1908,14 @@ static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_
   // from kHeadGemmMin hidden states on, the full head is cheaper as a matrix product (the output
   // matrix read once per 256 states) than as one streamed pass over it per state
   const bool product = which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && m->full_head_gemm_supported();
-  const bool streamed = which == 0 && m->exact && m->head_bulk_q && !product;  // quantizes in its own CTAs
-  if (!streamed) launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
+  // the streamed full head and the exact two-level head quantize the hidden states in their own CTAs
+  const bool self_quant = (which == 0 && m->exact && m->head_bulk_q && !product) || (which == 1 && m->exact);
+  if (!self_quant) launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
   if (product)
     m->full_head_gemm(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   else
-    m->run_head(which, streamed ? nullptr : m->hb_q, streamed ? nullptr : m->hb_s, h_dev, targets_dev, batch, lp_dev,
-                am_dev);
+    m->run_head(which, self_quant ? nullptr : m->hb_q, self_quant ? nullptr : m->hb_s, h_dev, targets_dev, batch,
+                lp_dev, am_dev);
   m->check_launch();
   API_END
 }

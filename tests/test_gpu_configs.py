@@ -127,3 +127,35 @@ def test_f16_head_requantized_q8_small(torch, isa, tmp_path):
             _check(g, o, toks, head, f"f16->q8 schedule={schedule}")
         g.close()
     o.close()
+
+
+@pytest.mark.parametrize("head_bits", [0, 8, 4])
+def test_twolevel_head_row_formats(torch, isa, tmp_path, head_bits):
+    """The fused two-level head's block rows in every output-matrix format: F16 (dot16 on the fp32
+    hidden state), Q8_0 and Q4_0 (requantized at load, f32 scales), through the per-token schedule and
+    the batched entry point, against the oracle; 8 classes of 125 rows (the top class often differs
+    from the target's, so both block paths run)."""
+    from gem_b200 import SEQUENTIAL
+    cfg = dict(synth.SMALL, d=352, nh=4, nkv=1, hd=64, ff=512, vocab=1000, layers=2)
+    path = synth.write_model(tmp_path / "f16head.gguf", cfg, seed=11, body="q4_0", head="f16")
+    tl = synth.write_twolevel(tmp_path / "f16head-k8", cfg["vocab"], 8, cfg["d"], seed=12)
+    o = orc.Model(path, ctx=128, threads=REF_THREADS, isa="avx512", head_bits=head_bits)
+    o.load_twolevel(tl)
+    g = Gemma(path, ctx=128, head_bits=head_bits)
+    g.load_twolevel(tl)
+    g.set_schedule(SEQUENTIAL)
+    _check(g, o, synth.tokens(40, cfg["vocab"], seed=14 + head_bits), TWO_LEVEL, f"two-level head_bits={head_bits}")
+    rng = np.random.default_rng(15 + head_bits)
+    for batch in (1, 37):
+        H = rng.standard_normal((batch, g.d)).astype(np.float32)
+        Tg = rng.integers(0, g.vocab, batch).astype(np.uint32)
+        Hd, Td = torch.tensor(H, device="cuda"), torch.tensor(Tg.astype(np.int32), device="cuda")
+        lp = torch.empty(batch, device="cuda")
+        am = torch.empty(batch, dtype=torch.int32, device="cuda")
+        g.head_twolevel_dev(Hd.data_ptr(), Td.data_ptr(), batch, lp.data_ptr(), am.data_ptr())
+        lp, am = lp.cpu().numpy(), am.cpu().numpy().astype(np.uint32)
+        for b in range(batch):
+            want_lp, want_am = o.twolevel(H[b], int(Tg[b]))
+            assert abs(lp[b] - want_lp) < 2e-5 and am[b] == want_am, (batch, b, lp[b], want_lp, am[b], want_am)
+    g.close()
+    o.close()
