@@ -87,6 +87,44 @@ __device__ __forceinline__ Best best_merge(Best a, Best b) {
   return a;
 }
 
+// Argmax over the rows of an output matrix held in class order: a thread keeps its best row and reads
+// row_tok (row -> token; null: rows are tokens) only to break an exact tie by the lower token id, then
+// turns the row into its token before candidates of several threads merge by best_merge.
+__device__ __forceinline__ void best_row_add(Best& B, float v, uint32_t r, const uint32_t* row_tok) {
+  if (v > B.v || (v == B.v && (B.tok == 0xffffffffu || (row_tok ? row_tok[r] < row_tok[B.tok] : r < B.tok))))
+    B = Best{v, r};
+}
+__device__ __forceinline__ void best_row_to_token(Best& B, const uint32_t* row_tok) {
+  if (row_tok && B.tok != 0xffffffffu) B.tok = row_tok[B.tok];
+}
+
+// Warp-wide merge of log-sum-exp states and argmax candidates: the maximum first, then the sums
+// rescaled to it (one exp per lane instead of one per merge step); every lane gets the result.
+__device__ __forceinline__ void warp_lse_best(Lse& L, Best& B) {
+  float m = L.m;
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = L.m == -INFINITY ? 0.0f : L.s * expf(L.m - m);
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    B = best_merge(B, Best{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)});
+  }
+  L = Lse{m, s};
+}
+// The same over the block (every thread calls it; blockDim a multiple of 32): the result in every lane
+// of warp 0. red_* hold one entry per warp and are free when it is called.
+__device__ __forceinline__ void block_lse_best(Lse& L, Best& B, float* red_m, float* red_s, float* red_v,
+                                               uint32_t* red_t) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  warp_lse_best(L, B);
+  if (lane == 0) red_m[warp] = L.m, red_s[warp] = L.s, red_v[warp] = B.v, red_t[warp] = B.tok;
+  __syncthreads();
+  if (warp == 0) {
+    L = lane < nw ? Lse{red_m[lane], red_s[lane]} : Lse{-INFINITY, 0.0f};
+    B = lane < nw ? Best{red_v[lane], red_t[lane]} : Best{-INFINITY, 0xffffffffu};
+    warp_lse_best(L, B);
+  }
+}
+
 // ----- scale loads -----
 __device__ __forceinline__ float ld_scale(const __half* s, size_t i) { return __half2float(s[i]); }
 __device__ __forceinline__ float ld_scale(const float* s, size_t i) { return s[i]; }

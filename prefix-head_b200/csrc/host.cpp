@@ -332,26 +332,6 @@ HostMat concat_rows(const std::vector<const HostMat*>& parts) {
   return o;
 }
 
-HostMat gather_rows(const HostMat& m, const std::vector<uint32_t>& ids) {  // q8.rs:94-106
-  HostMat o;
-  o.bits = m.bits, o.rows = ids.size(), o.cols = m.cols;
-  size_t c = m.row_bytes(), b = m.cols / 32;
-  o.q.resize(ids.size() * c);
-  if (m.bits != 16) {
-    if (m.scale_f32()) o.s32.resize(ids.size() * b);
-    else o.s16.resize(ids.size() * b);
-  }
-  for (size_t k = 0; k < ids.size(); ++k) {
-    size_t r = ids[k];
-    std::memcpy(&o.q[k * c], &m.q[r * c], c);
-    if (m.bits != 16) {
-      if (m.scale_f32()) std::memcpy(&o.s32[k * b], &m.s32[r * b], b * 4);
-      else std::memcpy(&o.s16[k * b], &m.s16[r * b], b * 2);
-    }
-  }
-  return o;
-}
-
 size_t canonical_bytes(const HostMat& m) { return m.q.size() + m.s16.size() * 2 + m.s32.size() * 4; }
 
 }  // namespace gem

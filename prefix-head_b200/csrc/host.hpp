@@ -77,7 +77,6 @@ HostMat load_mat(const Gguf& g, const std::string& name);      // model.rs:71-79
 HostMat to_q8(const HostMat& m);                               // q8.rs:129-145
 HostMat to_q4(const HostMat& m);                               // q8.rs:148-165
 HostMat concat_rows(const std::vector<const HostMat*>& parts); // stacks matrices of one type
-HostMat gather_rows(const HostMat& m, const std::vector<uint32_t>& ids);  // q8.rs:94-106
 size_t canonical_bytes(const HostMat& m);                      // bytes of the planes as stored
 
 }  // namespace gem

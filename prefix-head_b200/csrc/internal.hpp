@@ -10,7 +10,9 @@ namespace gem {
 
 // What a kernel-level entry point needs to run the full head of a model.
 struct ModelHeadView {
-  MatView w;          // output matrix, rows in token order
+  MatView w;          // output matrix
+  const uint32_t* row_of = nullptr;   // token -> row when the rows are in class order (null: token order)
+  const uint32_t* row_tok = nullptr;  // row -> token, likewise
   bool exact = true;  // numerics mode
   cudaStream_t st = nullptr;
   int sms = 0, device = 0, d = 0;

@@ -21,6 +21,26 @@ __global__ void k_embed(MatView head, const uint32_t* row_of, const StepCur* cur
   for (int j = threadIdx.x; j < head.cols; j += blockDim.x) x[j] = mul(weight_at<BITS, ST>(head, row, j), scale);
 }
 
+// Output-matrix rows gathered into another matrix of the same shape: dst row i = src row src_row[i]
+// (weights as 16-byte pieces, a row being a multiple of 16 bytes; scales as 2-byte pieces).
+__global__ void k_gather_rows(MatView src, const uint32_t* src_row, MatView dst) {
+  const size_t rb = (size_t)src.cols * src.bits / 8;
+  const size_t sb = src.bits == 16 ? 0 : (size_t)(src.cols / 32) * (src.scale_f32 ? 4 : 2);
+  for (int i = blockIdx.x; i < dst.rows; i += gridDim.x) {
+    const size_t r = src_row[i];
+    const int4* a = (const int4*)((const unsigned char*)src.q + r * rb);
+    int4* b = (int4*)((unsigned char*)dst.q + (size_t)i * rb);
+    for (size_t j = threadIdx.x; j < rb / 16; j += blockDim.x) b[j] = a[j];
+    const uint16_t* c = (const uint16_t*)((const unsigned char*)src.s + r * sb);
+    uint16_t* e = (uint16_t*)((unsigned char*)dst.s + (size_t)i * sb);
+    for (size_t j = threadIdx.x; j < sb / 2; j += blockDim.x) e[j] = c[j];
+  }
+}
+__global__ void k_gather_f32(const float* x, const uint32_t* idx, int n, float* y) {
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = x[idx[i]];
+}
+
 // Dequantized rows (Mat::row_f32) for tests of the bit-exact dequant definition.
 template <int BITS, typename ST>
 __global__ void k_dequant_rows(MatView w, size_t r0, int nrows, float* out) {
@@ -399,11 +419,11 @@ __global__ void k_head_full(HeadArgs H) {
   Best B{-INFINITY, 0xffffffffu};
   for (int r = blockIdx.x * nw + warp; r < w.rows; r += gridDim.x * nw) {
     float z = row_dot<BITS, ST>(w, r, saq, sas, sx, lane);
-    uint32_t tok = H.row_tok ? H.row_tok[r] : (uint32_t)r;
     L = lse_add(L, z);
-    B = best_merge(B, Best{z, tok});
+    best_row_add(B, z, (uint32_t)r, H.row_tok);
     if ((uint32_t)r == trow && lane == 0) H.tlogit[bi] = z;
   }
+  best_row_to_token(B, H.row_tok);
   if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -661,6 +681,12 @@ void launch_embed(const MatView& head, const uint32_t* row_of, const StepCur* cu
 #define F(B, S) launch_k(k_embed<B, S>, dim3(1), dim3(256), 0, st, head, row_of, cur, scale, x)
   GEM_DISPATCH(head.bits, head.scale_f32, F);
 #undef F
+}
+void launch_gather_rows(const MatView& src, const uint32_t* src_row, const MatView& dst, cudaStream_t st) {
+  k_gather_rows<<<min(dst.rows, 4 * 1184), 128, 0, st>>>(src, src_row, dst);
+}
+void launch_gather_f32(const float* x, const uint32_t* idx, int n, float* y, cudaStream_t st) {
+  launch_k(k_gather_f32, dim3(min((n + 255) / 256, 4096)), dim3(256), 0, st, x, idx, n, y);
 }
 void launch_dequant_rows(const MatView& w, size_t r0, int nrows, float* out, cudaStream_t st) {
 #define F(B, S) k_dequant_rows<B, S><<<min(nrows, 1024), 256, 0, st>>>(w, r0, nrows, out)

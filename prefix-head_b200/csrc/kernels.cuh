@@ -103,8 +103,8 @@ struct HeadArgs {
 
 #ifdef __CUDACC__
 // Log-sum-exp, argmax and log-prob of batch item bi from `nparts` per-CTA partials (max, sum of
-// exp, best logit, its token), merged by the calling CTA in a fixed order (strided per thread, then
-// the warp tree, then the warps in order), so the result does not depend on which CTA runs it.
+// exp, best logit, its token), merged by the calling CTA in a fixed order (a thread per partial, then
+// block_lse_best), so the result does not depend on which CTA runs it.
 __device__ inline void head_merge(const HeadArgs& H, int bi, int nparts) {
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
@@ -115,20 +115,8 @@ __device__ inline void head_merge(const HeadArgs& H, int bi, int nparts) {
     L = lse_merge(L, Lse{p.x, p.y});
     B = best_merge(B, Best{p.z, __float_as_uint(p.w)});
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int o = 16; o > 0; o >>= 1) {
-    Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
-    Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
-    L = lse_merge(L, l2);
-    B = best_merge(B, b2);
-  }
-  if (lane == 0) { red_m[warp] = L.m; red_s[warp] = L.s; red_v[warp] = B.v; red_t[warp] = B.tok; }
-  __syncthreads();
+  block_lse_best(L, B, red_m, red_s, red_v, red_t);
   if (threadIdx.x == 0) {
-    for (int i = 1; i < nw; ++i) {
-      L = lse_merge(L, Lse{red_m[i], red_s[i]});
-      B = best_merge(B, Best{red_v[i], red_t[i]});
-    }
     const float lse = L.m + logf(L.s);
     const uint32_t slot = H.targets ? (uint32_t)bi : H.cur->slot;
     if (H.lp_out) H.lp_out[slot] = __ldcg(H.tlogit + bi) - lse;
@@ -202,8 +190,9 @@ bool launch_tl_fused(const TwoLevelArgs& T, int batch, int sms, int* cnt, float*
 
 // Sequence-parallel scoring (seq.cu): every position of a chunk through one layer at a time, with the
 // exact per-position arithmetic above. Activations are [T][n] row-major, scales [T][n/32].
-void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, float scale, float* x, int* err,
-                      cudaStream_t st);
+// row_of (token -> row; null: token order) for an output matrix held in class order.
+void launch_seq_embed(const MatView& E, const uint32_t* row_of, const uint32_t* toks, int T, int vocab, float scale,
+                      float* x, int* err, cudaStream_t st);
 void launch_seq_norm(float* x, const float* delta, const float* w_post, const float* w_pre, float eps, int d, int T,
                      int8_t* aq, float* as, float* xn_out, cudaStream_t st);
 bool seq_gemm_supported(const MatView& w);
@@ -219,7 +208,7 @@ void launch_seq_attn(const AttnArgs& A, const float* qkv, int qkv_ld, int L, int
                      float* qn, float* scores, int sstride, int threads, float* part, int8_t* aq, float* as,
                      cudaStream_t st, cudaEvent_t kv_written = nullptr);
 void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
-                               float* out, int* err, cudaStream_t st);
+                               const uint32_t* row_of, const uint32_t* row_tok, float* out, int* err, cudaStream_t st);
 void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st);
 // Generation-side heads (decode.cu).
 void launch_greedy_rank(const float* cl, int k, int top, float min_conf, int batch, uint32_t* sel, int* fallback,
@@ -238,8 +227,12 @@ void launch_seq_gather_tokens(const uint32_t* toks, size_t stride, int L, int c0
 void launch_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t* aq, float* as, int sms, cudaStream_t st);
 void launch_seq_class_logits(const float* A, const float* b, int k, const float* h, int d, int T, float* cl,
                              cudaStream_t st);
-void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, float* lp, uint32_t* am, int* err,
-                             cudaStream_t st);
+void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, const uint32_t* row_of,
+                             const uint32_t* row_tok, float* lp, uint32_t* am, int* err, cudaStream_t st);
+// Output-matrix rows gathered into another matrix of the same shape and format: dst row i = src row
+// src_row[i] (the class-ordered head, permute_head, model.rs:242-249); y[i] = x[idx[i]].
+void launch_gather_rows(const MatView& src, const uint32_t* src_row, const MatView& dst, cudaStream_t st);
+void launch_gather_f32(const float* x, const uint32_t* idx, int n, float* y, cudaStream_t st);
 
 #ifdef __CUDACC__
 // Launches `k` with programmatic stream serialization (see pdl_wait); GEM_PDL=0 turns it off.

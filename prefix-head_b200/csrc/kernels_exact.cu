@@ -274,12 +274,12 @@ __global__ void k_head_full_exact(HeadArgs H) {
     bool ok = r < w.rows;
     float z = row_dot_exact<BITS, ST>(w, ok ? r : w.rows - 1, half, saq, sas, sx);
     if (ok && half == 0) {
-      uint32_t tok = H.row_tok ? H.row_tok[r] : (uint32_t)r;
       L = lse_add(L, z);
-      B = best_merge(B, Best{z, tok});
+      best_row_add(B, z, (uint32_t)r, H.row_tok);
       if ((uint32_t)r == trow) H.tlogit[bi] = z;
     }
   }
+  best_row_to_token(B, H.row_tok);
   for (int o = 16; o > 0; o >>= 1) {
     Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
     Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
@@ -413,15 +413,15 @@ __global__ void __launch_bounds__(G * 32) k_head_full_bulk(HeadArgs H, const uns
       const float z = reduce16_pair(acc);
       const int r = g * 16 + (lane >> 1);
       if (r < w.rows && half == 0) {
-        const uint32_t tok = H.row_tok ? H.row_tok[r] : (uint32_t)r;
         L = lse_add(L, z);
-        B = best_merge(B, Best{z, tok});
+        best_row_add(B, z, (uint32_t)r, H.row_tok);
         if ((uint32_t)r == trow) H.tlogit[bi] = z;
       }
     }
     __syncthreads();  // every warp is done with buffer k
     if (threadIdx.x == 0 && s + NS * (int)gridDim.x < nst) issue(s + NS * gridDim.x, k);
   }
+  best_row_to_token(B, H.row_tok);
   for (int o = 16; o > 0; o >>= 1) {
     Lse l2{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)};
     Best b2{__shfl_xor_sync(0xffffffffu, B.v, o), __shfl_xor_sync(0xffffffffu, B.tok, o)};
@@ -646,12 +646,23 @@ __host__ __device__ constexpr size_t tl_smem(int bits, int d, int rows_b) {
          (size_t)rows_b * 4;
 }
 
-// Lanes i of four rows of the reference's row dot (the 16-lane order of lane_row_s), rows q[u] in
-// shared memory: four independent FMA chains, each in order. For Q8_0 / Q4_0 rows sc[u][b] holds the
-// block's scale product RN(ws * as); the pair sum w0 a0 + w1 a1 is one dp4a (exact in int32; Q4_0's
-// nibbles carry +8, taken off as 8 (a0 + a1)).
+__device__ __forceinline__ int lds_u16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return (int)v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+
+// Lanes i of four rows of the reference's row dot (the 16-lane order of lane_row_s), rows at shared
+// addresses q[u]: four independent FMA chains, each in order. For Q8_0 / Q4_0 rows the fp32 at sc[u] +
+// 4b holds block b's scale product RN(ws * as); the pair sum w0 a0 + w1 a1 is one dp4a (exact in int32;
+// Q4_0's nibbles carry +8, taken off as 8 (a0 + a1)).
 template <int BITS>
-__device__ __forceinline__ void lane_rows4_s(const unsigned char* const (&q)[4], const float* const (&sc)[4], int d, int i,
+__device__ __forceinline__ void lane_rows4_s(const uint32_t (&q)[4], const uint32_t (&sc)[4], int d, int i,
                                              const int8_t* saq, const float* sx, float (&acc)[4]) {
 #pragma unroll
   for (int u = 0; u < 4; ++u) acc[u] = 0.0f;
@@ -660,24 +671,25 @@ __device__ __forceinline__ void lane_rows4_s(const unsigned char* const (&q)[4],
     for (int c = 0; c < d / 16; ++c) {
       const float x = sx[16 * c + i];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) acc[u] = fmaf(__half2float(((const __half*)q[u])[16 * c + i]), x, acc[u]);
+      for (int u = 0; u < 4; ++u)
+        acc[u] = fmaf(__half2float(__ushort_as_half((unsigned short)lds_u16(q[u] + 2 * (16 * c + i)))), x, acc[u]);
     }
   } else {
     const int sh = i < 8 ? 0 : 4;
+    const uint32_t qa = (uint32_t)__cvta_generic_to_shared(saq) + 2 * i;
 #pragma unroll 2
     for (int b = 0; b < d / 32; ++b) {
-      const int ap = *((const uint16_t*)(saq + 32 * b) + i);  // a0, a1 as signed bytes, upper bytes zero
+      const int ap = lds_u16(qa + 32 * b);  // a0, a1 as signed bytes, upper bytes zero
       const int off8 = BITS == 4 ? 8 * ((int)(int8_t)(ap & 0xff) + (int)(int8_t)(ap >> 8)) : 0;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         int p;
         if constexpr (BITS == 8) {
-          p = __dp4a((int)*((const uint16_t*)(q[u] + 32 * b) + i), ap, 0);
+          p = __dp4a(lds_u16(q[u] + 32 * b + 2 * i), ap, 0);
         } else {  // q8.rs:42-52: byte j holds weight j (low nibble) and j + 16 (high nibble), each + 8
-          const int wp = *((const uint16_t*)(q[u] + 16 * b) + (i & 7));
-          p = __dp4a((wp >> sh) & 0x0f0f, ap, 0) - off8;
+          p = __dp4a((lds_u16(q[u] + 16 * b + 2 * (i & 7)) >> sh) & 0x0f0f, ap, 0) - off8;
         }
-        acc[u] = fmaf((float)p, sc[u][b], acc[u]);
+        acc[u] = fmaf((float)p, lds_f32(sc[u] + 4 * b), acc[u]);
       }
     }
   }
@@ -693,6 +705,9 @@ struct TlAcc {
 };
 __device__ __forceinline__ TlAcc tl_acc0() {
   return TlAcc{Lse{-INFINITY, 0.0f}, Best{-INFINITY, 0xffffffffu}, Lse{-INFINITY, 0.0f}, Best{-INFINITY, 0xffffffffu}};
+}
+__device__ __forceinline__ TlAcc tl_merge(TlAcc a, TlAcc b) {
+  return TlAcc{lse_merge(a.c, b.c), best_merge(a.bc, b.bc), lse_merge(a.t, b.t), best_merge(a.bt, b.bt)};
 }
 // Merges 32 lanes' partials: maxima first, then the sums rescaled to them (one exp per lane).
 __device__ __forceinline__ TlAcc tl_warp_merge(TlAcc v) {
@@ -725,6 +740,13 @@ __device__ __forceinline__ TlTarget tl_target(const TwoLevelArgs& T, int bi) {
   if (bad) t = 0;
   const uint32_t c = T.cls_of[t], f = c * T.per;
   return TlTarget{t, c, T.pos_of[t], f, (int)min((uint32_t)T.per, (uint32_t)T.w.rows - f), bad};
+}
+
+// A hint that [p, p + bytes) will be read soon: its 16-byte-aligned interior is prefetched into L2.
+__device__ __forceinline__ void tl_prefetch_l2(const void* p, size_t bytes) {
+  const uintptr_t a = ((uintptr_t)p + 15) & ~(uintptr_t)15, e = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
+  if (e > a)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
 }
 
 // n scales of whole rows' blocks (nb a row) as fp32 in shared memory, times the hidden state's block
@@ -861,24 +883,33 @@ __global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, 
     p[2] = make_float4(s_zcl, s_zin, 0.0f, 0.0f);
     __threadfence();  // the partial before the count
     s_last = atomicAdd(cnt + bi, 1) == P - 1;
+    if (!s_last && v.bc.tok < (uint32_t)T.k && v.bc.tok != tg.ct) {
+      // this CTA's most likely class may be the hidden state's: its block starts towards L2 while the
+      // other CTAs finish, for the last CTA's copy of the winner
+      const uint32_t f = v.bc.tok * T.per, nr = min((uint32_t)T.per, (uint32_t)T.w.rows - f);
+      tl_prefetch_l2((const unsigned char*)T.w.q + f * RB, nr * RB);
+      if constexpr (BITS != 16) tl_prefetch_l2((const ST*)T.w.s + (size_t)f * nb, (size_t)nr * nb * sizeof(ST));
+      tl_prefetch_l2(T.order + f, (size_t)nr * 4);
+    }
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // ---- the last CTA: one warp merges the partials ----
+  // ---- the last CTA: merge the partials (a thread each, then the warps' merges) ----
+  v = tl_acc0();
+  for (int j = threadIdx.x; j < P; j += kTlThreads) {
+    const float4* p = (const float4*)(part + ((size_t)bi * P + j) * kTlPart);
+    const float4 a = __ldcg(p), b = __ldcg(p + 1), c = __ldcg(p + 2);
+    v = tl_merge(v, TlAcc{Lse{a.x, a.y}, Best{a.z, __float_as_uint(a.w)}, Lse{b.x, b.y}, Best{b.z, __float_as_uint(b.w)}});
+    if (!isnan(c.x)) s_zcl = c.x;  // exactly one CTA computed each
+    if (!isnan(c.y)) s_zin = c.y;
+  }
+  v = tl_warp_merge(v);
+  __syncthreads();  // red is free
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
   if (warp == 0) {
-    v = tl_acc0();
-    for (int j = lane; j < P; j += 32) {
-      const float4* p = (const float4*)(part + ((size_t)bi * P + j) * kTlPart);
-      const float4 a = __ldcg(p), b = __ldcg(p + 1), c = __ldcg(p + 2);
-      v.c = lse_merge(v.c, Lse{a.x, a.y});
-      v.bc = best_merge(v.bc, Best{a.z, __float_as_uint(a.w)});
-      v.t = lse_merge(v.t, Lse{b.x, b.y});
-      v.bt = best_merge(v.bt, Best{b.z, __float_as_uint(b.w)});
-      if (!isnan(c.x)) s_zcl = c.x;  // exactly one CTA computed each
-      if (!isnan(c.y)) s_zin = c.y;
-    }
-    v = tl_warp_merge(v);
+    v = tl_warp_merge(lane < kTlThreads / 32 ? red[lane] : tl_acc0());
     if (lane == 0) {
       if (tg.bad) atomicExch(T.err, ERR_RANGE);
       s_lse_cl = v.c.m + logf(v.c.s);
@@ -916,14 +947,14 @@ __global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, 
         break;
       }
       // four rows per group at once: j, j + 32, j + 64, j + 96 (a row past the end repeats row j)
+      const uint32_t stage_a = (uint32_t)__cvta_generic_to_shared(stage), ssc_a = (uint32_t)__cvta_generic_to_shared(ssc);
       for (int j = g; j < m; j += 4 * kTlGroups) {
-        const unsigned char* q4[4];
-        const float* s4[4];
+        uint32_t q4[4], s4[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int ju = j + u * kTlGroups < m ? j + u * kTlGroups : j;
-          q4[u] = stage + ju * RB;
-          s4[u] = ssc + (size_t)ju * nb;
+          q4[u] = stage_a + (uint32_t)(ju * RB);
+          s4[u] = ssc_a + (uint32_t)(ju * nb * 4);
         }
         float acc[4];
         lane_rows4_s<BITS>(q4, s4, d, i, saq, sx, acc);

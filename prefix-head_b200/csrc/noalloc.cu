@@ -90,6 +90,7 @@ extern "C" int gem_head_full_noalloc(gem_model* m, const float* h_dev, const uin
   gem::launch_quantize(h_dev, batch * v.d, q, s, v.st);
   gem::HeadArgs H{};
   H.w = v.w;
+  H.row_of = v.row_of, H.row_tok = v.row_tok;
   H.aq = q, H.as = s, H.h = h_dev;
   H.targets = targets_dev;
   H.part = part;

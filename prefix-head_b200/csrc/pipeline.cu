@@ -516,7 +516,8 @@ __device__ bool layer_tokens(const PipeArgs& P, int l, int c, const Smem& S, WRi
         if (tid == 0) atomicCAS(P.err, 0, ERR_RANGE);
         tok = 0;
       }
-      for (int j = tid; j < d; j += nt) S.x[j] = mul(emb_weight<BH, SH>(P.emb, tok, j), P.embed_scale);
+      const uint32_t erow = P.emb_row ? P.emb_row[tok] : tok;
+      for (int j = tid; j < d; j += nt) S.x[j] = mul(emb_weight<BH, SH>(P.emb, erow, j), P.embed_scale);
     } else {
       if (tid == 0) *S.ok = wait_geq(P.ready + l * PIPE_RING + slot, (unsigned)t + 1, P.err, P.wait_ns);
       __syncthreads();

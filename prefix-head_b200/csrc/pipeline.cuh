@@ -24,7 +24,8 @@ struct PipeArgs {
   float eps, qscale, embed_scale;
   int silu;
   int layers_bits, layers_scale_f32;
-  MatView emb;  // embedding rows in token order (the tied output matrix)
+  MatView emb;              // embedding rows (the tied output matrix)
+  const uint32_t* emb_row;  // token -> row of emb when it is held in class order (null: token order)
   // two-level head
   MatView blocks;
   const float *A, *b, *out_norm;

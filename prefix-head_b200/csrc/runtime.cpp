@@ -117,6 +117,11 @@ struct gem_model {
   size_t body_bytes = 0;
   std::vector<Layer> layers;
   DevMat head, emb;  // emb used only when the file has a separate output matrix
+  // permute_head (model.rs:242-249): once a two-level class file covers the vocabulary, head's rows
+  // are in class order and row_of maps a token to its row (null: token order; row -> token is order)
+  uint32_t* row_of = nullptr;
+  std::vector<uint32_t> row_of_h;
+  const uint32_t* row_tok() const { return row_of ? order : nullptr; }
   unsigned char* head_bulk_q = nullptr;  // the output matrix's GEMV copy for the streamed full head, built on first use
   __half* head_bulk_s = nullptr;
   float* out_norm = nullptr;
@@ -322,6 +327,16 @@ struct gem_model {
     ++alloc_gen;
     return p;
   }
+  // Frees a buffer from alloc / upload (the graphs that used it must be dropped).
+  void release(const void* p) {
+    for (size_t i = 0; i < owned.size(); ++i)
+      if (owned[i] == p) {
+        cudaFree(owned[i]);
+        owned.erase(owned.begin() + (long)i);
+        ++alloc_gen;
+        return;
+      }
+  }
   template <typename T>
   T* upload(const std::vector<T>& v) {
     T* p = dev_upload(v);
@@ -403,7 +418,7 @@ struct gem_model {
   // hidden state in h and its quantization in (haq, has).
   void enqueue_body(int seq) {
     const DevMat& E = untied ? emb : head;
-    launch_embed(E.v, nullptr, cur, embed_scale, x, st);
+    launch_embed(E.v, untied ? nullptr : row_of, cur, embed_scale, x, st);
     // exact numerics with d <= 1152 in 32-blocks: the parallel schedule's norm kernel for one position
     // (one warp, the sequential sums fed by prefetched loads, quantization from registers), the same
     // arithmetic as the single-CTA per-token kernel
@@ -435,6 +450,7 @@ struct gem_model {
   HeadArgs head_args(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, float* lpo, uint32_t* amo) {
     HeadArgs H{};
     H.w = head.v;
+    H.row_of = row_of, H.row_tok = row_tok();
     H.aq = qa, H.as = sa, H.h = hh;
     H.targets = targets;
     H.cur = cur;
@@ -576,7 +592,8 @@ struct gem_model {
         launch_seq_head_f16(head.v, h + (size_t)h0 * d, n, s_logits, vocab, st);
       else
         launch_seq_gemm(head.v, q + (size_t)h0 * d, s + (size_t)h0 * d / 32, n, s_logits, vocab, sms, st);
-      launch_seq_logit_reduce(s_logits, vocab, n, targets + h0, lpo + h0, amo ? amo + h0 : nullptr, err, st);
+      launch_seq_logit_reduce(s_logits, vocab, n, targets + h0, row_of, row_tok(), lpo + h0, amo ? amo + h0 : nullptr,
+                              err, st);
       launches += 2;
     }
     return launches;
@@ -630,8 +647,8 @@ struct gem_model {
     for (int h0 = 0; h0 < T; h0 += hc) {
       const int n = std::min(hc, T - h0);
       launch_seq_gemm(w, s_haq + (size_t)h0 * d, s_has + (size_t)h0 * d / 32, n, s_logits, shard_rows, sms, st);
-      launch_seq_logit_partials(s_logits, shard_rows, (uint32_t)shard_row0, n, targets + h0, (uint32_t)vocab,
-                                s_spart + (size_t)h0 * 5, err, st);
+      launch_seq_logit_partials(s_logits, shard_rows, (uint32_t)shard_row0, n, targets + h0, (uint32_t)vocab, row_of,
+                                row_tok(), s_spart + (size_t)h0 * 5, err, st);
       launches += 2;
     }
     par_mark(PAR_HEAD);  // this rank's rows: logits and partial statistics
@@ -771,7 +788,7 @@ struct gem_model {
         for (int k = 0; k < parts; ++k) {
           const Part& q = hv[k];
           launch_seq_gather_tokens(toks_d + (size_t)s0 * stride, stride, q.L, (int)c0 + q.r0, q.n, q.tin, q.tgt, q.s);
-          launch_seq_embed(E.v, q.tin, q.n, vocab, embed_scale, q.x, err, q.s);
+          launch_seq_embed(E.v, untied ? nullptr : row_of, q.tin, q.n, vocab, embed_scale, q.x, err, q.s);
         }
         par_mark(PAR_EMBED);
         for (int l = 0; l < nl; ++l) {
@@ -878,7 +895,7 @@ struct gem_model {
       }
       if (!seq_gemm_supported(blocks.v)) throw Error(GEM_E_STATE, "the fallback needs a Q8_0/Q4_0 output matrix");
       launch_seq_gemm(blocks.v, gs.q, gs.s, batch, gs.logits, vocab, sms, st);
-      launch_seq_logit_reduce(gs.logits, vocab, batch, gs.zeros, gs.lp, gs.fb_row, err, st);
+      launch_seq_logit_reduce(gs.logits, vocab, batch, gs.zeros, nullptr, nullptr, gs.lp, gs.fb_row, err, st);
     }
     launch_greedy_pick(gs.z, gs.rows, top, per, n_always, gs.fallback, fb ? gs.fb_row : nullptr, order, batch, tok_dev, st);
     if (fallback_dev) ck(cudaMemcpyAsync(fallback_dev, gs.fallback, (size_t)batch * 4, cudaMemcpyDeviceToDevice, st), "fb");
@@ -946,6 +963,7 @@ struct gem_model {
     P.eps = eps, P.qscale = 1.0f / std::sqrt((float)hd), P.embed_scale = embed_scale, P.silu = silu ? 1 : 0;
     P.layers_bits = layers[0].qkv.v.bits, P.layers_scale_f32 = layers[0].qkv.v.scale_f32;
     P.emb = head.v;
+    P.emb_row = row_of;
     P.blocks = blocks.v;
     P.A = A, P.b = b, P.out_norm = out_norm, P.cls_of = cls_of, P.pos_of = pos_of, P.order = order;
     P.k = k, P.per = per;
@@ -1052,6 +1070,7 @@ namespace gem {
 bool model_head_view(const gem_model* m, ModelHeadView* out) {
   if (!m || !out) return false;
   out->w = m->head.v;
+  out->row_of = m->row_of, out->row_tok = m->row_tok();
   out->exact = m->exact;
   out->st = m->st;
   out->sms = m->sms;
@@ -1321,23 +1340,54 @@ int gem_open_twolevel(gem_model* m, const char* prefix) {
     cls_of[order[i]] = (uint32_t)(i / per);
     pos_of[order[i]] = (uint32_t)(i % per);
   }
-  // Gather the class blocks (main.rs:74) from the device head into a class-ordered copy.
-  HostMat hm;
-  hm.bits = m->head.v.bits, hm.rows = (size_t)m->head.v.rows, hm.cols = (size_t)m->head.v.cols;
-  hm.q.resize(hm.rows * hm.row_bytes());
-  ck(cudaMemcpy(hm.q.data(), m->head.v.q, hm.q.size(), cudaMemcpyDeviceToHost), "download head");
-  if (hm.bits != 16) {
-    size_t ns = hm.rows * hm.cols / 32;
-    if (m->head.v.scale_f32) {
-      hm.s32.resize(ns);
-      ck(cudaMemcpy(hm.s32.data(), m->head.v.s, ns * 4, cudaMemcpyDeviceToHost), "download scales");
-    } else {
-      hm.s16.resize(ns);
-      ck(cudaMemcpy(hm.s16.data(), m->head.v.s, ns * 2, cudaMemcpyDeviceToHost), "download scales");
+  // TwoLevel::load gathers the class blocks (main.rs:74); permute_head (model.rs:242-249, q8.rs:65-91)
+  // then keeps the output matrix once, in class order. Here, when the class file covers every token
+  // once, the rows are gathered on the device into class order (from the current order, if an earlier
+  // class file permuted them) and the previous rows released: a second copy exists only during the
+  // gather, and the class blocks are views into the one matrix. Otherwise the blocks are a copy.
+  m->drop_graphs();
+  const bool old_blocks_copy = m->two && m->blocks.v.q && m->blocks.v.q != m->head.v.q;
+  const DevMat old_blocks = m->blocks;
+  std::vector<uint32_t> src(order.size()), new_row_of(m->vocab, 0xffffffffu);
+  bool perm = order.size() == (size_t)m->vocab;
+  for (size_t i = 0; i < order.size(); ++i) {
+    src[i] = m->row_of_h.empty() ? order[i] : m->row_of_h[order[i]];
+    if (perm && new_row_of[order[i]] != 0xffffffffu) perm = false;  // a token in two classes
+    if (perm) new_row_of[order[i]] = (uint32_t)i;
+  }
+  const MatView& hv = m->head.v;
+  const size_t rb = (size_t)hv.cols * hv.bits / 8, sb = hv.bits == 16 ? 0 : (size_t)(hv.cols / 32) * (hv.scale_f32 ? 4 : 2);
+  uint32_t* d_src = m->upload(src);
+  DevMat gathered;
+  gathered.v = hv;
+  gathered.v.rows = (int)order.size();
+  gathered.v.q = m->alloc<unsigned char>(order.size() * rb);
+  gathered.v.s = sb ? m->alloc<unsigned char>(order.size() * sb) : nullptr;
+  gathered.bytes = order.size() * (rb + sb);
+  launch_gather_rows(hv, d_src, gathered.v, m->st);
+  ck(cudaGetLastError(), "gather class blocks");
+  ck(cudaStreamSynchronize(m->st), "gather class blocks");
+  m->release(d_src);
+  if (old_blocks_copy) {  // an earlier class file's blocks
+    m->release(old_blocks.v.q);
+    if (old_blocks.v.s) m->release(old_blocks.v.s);
+  }
+  if (perm) {
+    m->release(m->head.v.q);
+    if (m->head.v.s) m->release(m->head.v.s);
+    if (m->row_of) m->release(m->row_of);
+    m->head = gathered;
+    m->row_of = m->upload(new_row_of);
+    m->row_of_h = std::move(new_row_of);
+    if (m->head_bulk_q) {  // the streamed full head's copy follows the rows' new order
+      launch_head_bulk_layout(m->head.v, m->head_bulk_q, m->head_bulk_s, m->st);
+      ck(cudaStreamSynchronize(m->st), "head layout");
     }
   }
-  HostMat blocks = gather_rows(hm, order);
-  m->blocks = upload_mat(blocks, m->owned);
+  m->blocks = gathered;
+  for (const void* p : {(const void*)m->A, (const void*)m->b, (const void*)m->cls_of, (const void*)m->pos_of,
+                        (const void*)m->order})
+    if (p) m->release(p);
   m->A = m->upload(A);
   m->b = m->upload(b);
   m->cls_of = m->upload(cls_of);
@@ -1886,14 +1936,16 @@ int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float
   int cols = M->v.cols;
   int8_t* q = m->alloc<int8_t>(cols);
   float* s = m->alloc<float>(cols / 32);
+  // the output matrix in class order: its rows' values back in token order, y[t] = row row_of[t]
+  float* y_rows = layer == -1 && m->row_of ? m->alloc<float>(M->v.rows) : nullptr;
   launch_quantize(x_dev, cols, q, s, m->st);
-  (m->exact ? launch_gemv_exact : launch_gemv)(M->v, q, s, x_dev, y_dev, m->sms, m->st);
+  (m->exact ? launch_gemv_exact : launch_gemv)(M->v, q, s, x_dev, y_rows ? y_rows : y_dev, m->sms, m->st);
+  if (y_rows) launch_gather_f32(y_rows, m->row_of, M->v.rows, y_dev, m->st);
   m->check_launch();
   m->sync();
-  m->owned.pop_back();
-  m->owned.pop_back();
-  cudaFree(q);
-  cudaFree(s);
+  m->release(q);
+  m->release(s);
+  if (y_rows) m->release(y_rows);
   API_END
 }
 

@@ -55,10 +55,12 @@ __host__ __device__ __forceinline__ uint32_t window_lo(uint32_t pos, int window)
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------
-// Embedding: one CTA per position. Ids >= vocab are recorded in *err and replaced by 0.
+// Embedding: one CTA per position. Ids >= vocab are recorded in *err and replaced by 0. row_of maps a
+// token to its row when the matrix is held in class order (null: token order).
 // ------------------------------------------------------------------------------------------------
 template <int BITS, typename ST>
-__global__ void k_seq_embed(MatView E, const uint32_t* toks, int vocab, float scale, float* x, int* err) {
+__global__ void k_seq_embed(MatView E, const uint32_t* row_of, const uint32_t* toks, int vocab, float scale, float* x,
+                            int* err) {
   pdl_wait();
   const int t = blockIdx.x;
   uint32_t tok = toks[t];
@@ -66,7 +68,8 @@ __global__ void k_seq_embed(MatView E, const uint32_t* toks, int vocab, float sc
     if (threadIdx.x == 0) atomicExch(err, ERR_RANGE);
     tok = 0;
   }
-  for (int j = threadIdx.x; j < E.cols; j += blockDim.x) x[(size_t)t * E.cols + j] = mul(weight_at<BITS, ST>(E, tok, j), scale);
+  const size_t row = row_of ? row_of[tok] : tok;
+  for (int j = threadIdx.x; j < E.cols; j += blockDim.x) x[(size_t)t * E.cols + j] = mul(weight_at<BITS, ST>(E, row, j), scale);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -637,10 +640,12 @@ __global__ void k_seq_glu_quant(const float* gu, int ff, int T, int silu, int8_t
 
 // ------------------------------------------------------------------------------------------------
 // Full head from a logits matrix [T][V]: online log-sum-exp, argmax (first maximum) and the target's
-// logit per position; logprob = logit[target] - lse. One CTA per position.
+// logit per position; logprob = logit[target] - lse. One CTA per position. With the matrix in class
+// order, row_tok maps a row to its token and row_of a token to its row (both null: token order); a
+// thread keeps its best row (best_row_add), reading tokens only to break exact ties.
 // ------------------------------------------------------------------------------------------------
-__global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* targets, float* lp, uint32_t* am,
-                                   int* err) {
+__global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* targets, const uint32_t* row_of,
+                                   const uint32_t* row_tok, float* lp, uint32_t* am, int* err) {
   pdl_wait();
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
@@ -651,8 +656,9 @@ __global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* t
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float v = z[i];
     L = lse_add(L, v);
-    B = best_merge(B, Best{v, (uint32_t)i});
+    best_row_add(B, v, (uint32_t)i, row_tok);
   }
+  best_row_to_token(B, row_tok);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int o = 16; o > 0; o >>= 1) {
     L = lse_merge(L, Lse{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)});
@@ -670,7 +676,7 @@ __global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* t
       atomicExch(err, ERR_RANGE);
       tg = 0;
     }
-    lp[t] = z[tg] - (L.m + logf(L.s));
+    lp[t] = z[row_of ? row_of[tg] : tg] - (L.m + logf(L.s));
     if (am) am[t] = B.tok;
   }
 }
@@ -679,7 +685,7 @@ __global__ void k_seq_logit_reduce(const float* logits, int V, const uint32_t* t
 // the partial log-sum-exp state, the best logit with its token id and the target's logit (NaN when
 // the target is another rank's). out[t] = {m, s, best, best id bits, target logit}.
 __global__ void k_seq_logit_partials(const float* logits, int V, uint32_t row0, const uint32_t* targets, uint32_t vocab,
-                                     float* out, int* err) {
+                                     const uint32_t* row_of, const uint32_t* row_tok, float* out, int* err) {
   pdl_wait();
   __shared__ float red_m[32], red_s[32], red_v[32];
   __shared__ uint32_t red_t[32];
@@ -690,8 +696,9 @@ __global__ void k_seq_logit_partials(const float* logits, int V, uint32_t row0, 
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float v = z[i];
     L = lse_add(L, v);
-    B = best_merge(B, Best{v, row0 + (uint32_t)i});
+    best_row_add(B, v, row0 + (uint32_t)i, row_tok);
   }
+  best_row_to_token(B, row_tok);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int o = 16; o > 0; o >>= 1) {
     L = lse_merge(L, Lse{__shfl_xor_sync(0xffffffffu, L.m, o), __shfl_xor_sync(0xffffffffu, L.s, o)});
@@ -709,7 +716,8 @@ __global__ void k_seq_logit_partials(const float* logits, int V, uint32_t row0, 
       atomicExch(err, ERR_RANGE);
       tg = 0;
     }
-    const float tl = tg >= row0 && tg < row0 + (uint32_t)V ? z[tg - row0] : __int_as_float(0x7fffffff);
+    const uint32_t tr = row_of ? row_of[tg] : tg;
+    const float tl = tr >= row0 && tr < row0 + (uint32_t)V ? z[tr - row0] : __int_as_float(0x7fffffff);
     float* o = out + (size_t)t * 5;
     o[0] = L.m, o[1] = L.s, o[2] = B.v, o[3] = __uint_as_float(B.tok), o[4] = tl;
   }
@@ -753,9 +761,9 @@ bool pdl_on() {
   return on;
 }
 
-void launch_seq_embed(const MatView& E, const uint32_t* toks, int T, int vocab, float scale, float* x, int* err,
-                      cudaStream_t st) {
-#define F(B, S) launch_k(k_seq_embed<B, S>, dim3(T), dim3(256), 0, st, E, toks, vocab, scale, x, err)
+void launch_seq_embed(const MatView& E, const uint32_t* row_of, const uint32_t* toks, int T, int vocab, float scale,
+                      float* x, int* err, cudaStream_t st) {
+#define F(B, S) launch_k(k_seq_embed<B, S>, dim3(T), dim3(256), 0, st, E, row_of, toks, vocab, scale, x, err)
   if (E.bits == 16) F(16, __half);
   else GEM_DISPATCH_Q(E.bits, E.scale_f32, F);
 #undef F
@@ -1171,17 +1179,17 @@ void launch_seq_class_logits(const float* A, const float* b, int k, const float*
   launch_dot16_gemm(A, b, k, d, h, T, cl, k, st);
 }
 
-void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, float* lp, uint32_t* am, int* err,
-                             cudaStream_t st) {
-  launch_k(k_seq_logit_reduce, dim3(T), dim3(1024), 0, st, logits, V, targets, lp, am, err);
+void launch_seq_logit_reduce(const float* logits, int V, int T, const uint32_t* targets, const uint32_t* row_of,
+                             const uint32_t* row_tok, float* lp, uint32_t* am, int* err, cudaStream_t st) {
+  launch_k(k_seq_logit_reduce, dim3(T), dim3(1024), 0, st, logits, V, targets, row_of, row_tok, lp, am, err);
 }
 
 }  // namespace gem
 
 namespace gem {
 void launch_seq_logit_partials(const float* logits, int V, uint32_t row0, int T, const uint32_t* targets, uint32_t vocab,
-                               float* out, int* err, cudaStream_t st) {
-  launch_k(k_seq_logit_partials, dim3(T), dim3(1024), 0, st, logits, V, row0, targets, vocab, out, err);
+                               const uint32_t* row_of, const uint32_t* row_tok, float* out, int* err, cudaStream_t st) {
+  launch_k(k_seq_logit_partials, dim3(T), dim3(1024), 0, st, logits, V, row0, targets, vocab, row_of, row_tok, out, err);
 }
 void launch_seq_logit_combine(const float* parts, int nranks, int T, float* lp, uint32_t* am, cudaStream_t st) {
   launch_k(k_seq_logit_combine, dim3((T + 127) / 128), dim3(128), 0, st, parts, nranks, T, lp, am);
