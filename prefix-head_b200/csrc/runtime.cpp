@@ -551,19 +551,24 @@ struct gem_model {
   }
 
   // Head over T final hidden states (s_h, s_haq, s_has) with targets[0..T); returns the kernels launched.
+  // The exact two-level head over T hidden states (fp32 hh, quantized qa / sa) as the class logits'
+  // tile product (every class row read once for all T) and the block kernels: target block, top
+  // class, top block, argmax. Returns the kernels launched.
+  int twolevel_product(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, int T, float* lpo,
+                       uint32_t* amo) {
+    ensure_head_batch(T);
+    launch_seq_class_logits(A, b, k, hh, d, T, cl, st);
+    TwoLevelArgs TL = tl_args(qa, sa, hh, targets, lpo, amo);
+    TL.class_ctas = 0;
+    const int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
+    launch_tl_stage1_exact(TL, T, 0, block_ctas, st);
+    launch_tl_select(TL, T, top_of, st);
+    launch_tl_top_exact(TL, T, top_of, top_inner, st);
+    launch_tl_argmax(TL, T, top_of, top_inner, st);
+    return 5;
+  }
   int seq_head(int which, const uint32_t* targets, int T, float* lpo, uint32_t* amo) {
-    if (which == 1) {
-      ensure_head_batch(T);
-      launch_seq_class_logits(A, b, k, s_h, d, T, cl, st);
-      TwoLevelArgs TL = tl_args(s_haq, s_has, s_h, targets, lpo, amo);
-      TL.class_ctas = 0;
-      const int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
-      launch_tl_stage1_exact(TL, T, 0, block_ctas, st);
-      launch_tl_select(TL, T, top_of, st);
-      launch_tl_top_exact(TL, T, top_of, top_inner, st);
-      launch_tl_argmax(TL, T, top_of, top_inner, st);
-      return 5;
-    }
+    if (which == 1) return twolevel_product(s_haq, s_has, s_h, targets, T, lpo, amo);
     if (comm) return seq_head_sharded(targets, T, lpo, amo);
     if (!full_head_gemm_supported()) {  // the per-position exact head kernels
       run_head(0, s_haq, s_has, s_h, targets, T, lpo, amo);
@@ -1950,6 +1955,15 @@ int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float
 }
 
 constexpr int kHeadGemmMin = 12;  // ~30 us per streamed state vs ~0.37 ms per 32-state product tile
+// from this many hidden states on, the two-level head's class logits are one tile product (every class
+// row read once) instead of the one-launch kernel's per-state passes
+static int two_level_product_min() {
+  static const int v = [] {
+    const char* e = std::getenv("GEM_TL_PRODUCT_MIN");
+    return e ? std::max(1, std::atoi(e)) : 48;
+  }();
+  return v;
+}
 static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_t* targets_dev, int batch, float* lp_dev,
                       uint32_t* am_dev) {
   API_BEGIN
@@ -1960,11 +1974,14 @@ static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_
   // from kHeadGemmMin hidden states on, the full head is cheaper as a matrix product (the output
   // matrix read once per 256 states) than as one streamed pass over it per state
   const bool product = which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && m->full_head_gemm_supported();
-  // the streamed full head and the exact two-level head quantize the hidden states in their own CTAs
-  const bool self_quant = (which == 0 && m->exact && m->head_bulk_q && !product) || (which == 1 && m->exact);
+  const bool tl_product = which == 1 && m->exact && batch >= two_level_product_min();
+  // the streamed full head and the one-launch two-level head quantize the hidden states in their CTAs
+  const bool self_quant = (which == 0 && m->exact && m->head_bulk_q && !product) || (which == 1 && m->exact && !tl_product);
   if (!self_quant) launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
   if (product)
     m->full_head_gemm(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
+  else if (tl_product)
+    m->twolevel_product(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   else
     m->run_head(which, self_quant ? nullptr : m->hb_q, self_quant ? nullptr : m->hb_s, h_dev, targets_dev, batch,
                 lp_dev, am_dev);

@@ -133,7 +133,7 @@ def test_f16_head_requantized_q8_small(torch, isa, tmp_path):
 def test_twolevel_head_row_formats(torch, isa, tmp_path, head_bits):
     """The fused two-level head's block rows in every output-matrix format: F16 (dot16 on the fp32
     hidden state), Q8_0 and Q4_0 (requantized at load, f32 scales), through the per-token schedule and
-    the batched entry point, against the oracle; 8 classes of 125 rows (the top class often differs
+    the batched entry point (batch 64: the class-logit product), against the oracle; 8 classes of 125 rows (the top class often differs
     from the target's, so both block paths run)."""
     from gem_b200 import SEQUENTIAL
     cfg = dict(synth.SMALL, d=352, nh=4, nkv=1, hd=64, ff=512, vocab=1000, layers=2)
@@ -146,7 +146,7 @@ def test_twolevel_head_row_formats(torch, isa, tmp_path, head_bits):
     g.set_schedule(SEQUENTIAL)
     _check(g, o, synth.tokens(40, cfg["vocab"], seed=14 + head_bits), TWO_LEVEL, f"two-level head_bits={head_bits}")
     rng = np.random.default_rng(15 + head_bits)
-    for batch in (1, 37):
+    for batch in (1, 5, 64):  # one round per CTA, two rounds (one launch), the class-logit product
         H = rng.standard_normal((batch, g.d)).astype(np.float32)
         Tg = rng.integers(0, g.vocab, batch).astype(np.uint32)
         Hd, Td = torch.tensor(H, device="cuda"), torch.tensor(Tg.astype(np.int32), device="cuda")
