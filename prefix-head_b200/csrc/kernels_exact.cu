@@ -742,13 +742,6 @@ __device__ __forceinline__ TlTarget tl_target(const TwoLevelArgs& T, int bi) {
   return TlTarget{t, c, T.pos_of[t], f, (int)min((uint32_t)T.per, (uint32_t)T.w.rows - f), bad};
 }
 
-// A hint that [p, p + bytes) will be read soon: its 16-byte-aligned interior is prefetched into L2.
-__device__ __forceinline__ void tl_prefetch_l2(const void* p, size_t bytes) {
-  const uintptr_t a = ((uintptr_t)p + 15) & ~(uintptr_t)15, e = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
-  if (e > a)
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(e - a)) : "memory");
-}
-
 // n scales of whole rows' blocks (nb a row) as fp32 in shared memory, times the hidden state's block
 // scale (RN(ws * as), the factor of the row dot's FMA) when sas is given: eight independent loads in
 // flight per thread.
@@ -883,14 +876,6 @@ __global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, 
     p[2] = make_float4(s_zcl, s_zin, 0.0f, 0.0f);
     __threadfence();  // the partial before the count
     s_last = atomicAdd(cnt + bi, 1) == P - 1;
-    if (!s_last && v.bc.tok < (uint32_t)T.k && v.bc.tok != tg.ct) {
-      // this CTA's most likely class may be the hidden state's: its block starts towards L2 while the
-      // other CTAs finish, for the last CTA's copy of the winner
-      const uint32_t f = v.bc.tok * T.per, nr = min((uint32_t)T.per, (uint32_t)T.w.rows - f);
-      tl_prefetch_l2((const unsigned char*)T.w.q + f * RB, nr * RB);
-      if constexpr (BITS != 16) tl_prefetch_l2((const ST*)T.w.s + (size_t)f * nb, (size_t)nr * nb * sizeof(ST));
-      tl_prefetch_l2(T.order + f, (size_t)nr * 4);
-    }
   }
   __syncthreads();
   if (!s_last) return;
