@@ -44,31 +44,37 @@ __device__ __forceinline__ int load_word(const MatView& w, size_t r, int b, int 
 template <int BITS, typename ST>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv_exact(MatView w, const int8_t* aq, const float* as, const float* x,
                                                              float* y) {
-  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int8_t* saq = (int8_t*)smem_raw;
   float* sas = (float*)(smem_raw + w.cols);
   float* sx = (float*)smem_raw;
-  if (BITS == 16) {
-    for (int j = threadIdx.x; j < w.cols; j += blockDim.x) sx[j] = x[j];
-  } else {
-    for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)aq)[j];
-    for (int j = threadIdx.x; j < w.cols / 32; j += blockDim.x) sas[j] = as[j];
-  }
-  __syncthreads();
   const int o = threadIdx.x & 7;
   const int r = blockIdx.x * (kGemvThreads / 8) + (threadIdx.x >> 3);
   const bool ok = r < w.rows;  // a row's 8 threads are consecutive lanes: the shuffles stay inside them
   const size_t rr = ok ? r : w.rows - 1;
+  // The weights depend on no earlier kernel: the first kGemvU blocks are requested before the wait for
+  // the previous kernel (programmatic dependent launch), so their latency passes while it finishes.
+  // The activation vector is its output, staged after the wait.
+  auto stage_act = [&]() {
+    pdl_wait();
+    if (BITS == 16) {
+      for (int j = threadIdx.x; j < w.cols; j += blockDim.x) sx[j] = x[j];
+    } else {
+      for (int j = threadIdx.x; j < w.cols / 16; j += blockDim.x) ((int4*)saq)[j] = ((const int4*)aq)[j];
+      for (int j = threadIdx.x; j < w.cols / 32; j += blockDim.x) sas[j] = as[j];
+    }
+    __syncthreads();
+  };
   float a0 = 0.0f, a1 = 0.0f;  // lanes 2o, 2o + 1
   if constexpr (BITS == 16) {
     const __half2* row = (const __half2*)((const __half*)w.q + rr * w.cols);
     const int nc = w.cols / 16;
+    __half2 v[kGemvU];
     for (int c0 = 0; c0 < nc; c0 += kGemvU) {
-      __half2 v[kGemvU];
 #pragma unroll
       for (int u = 0; u < kGemvU; ++u)
         if (c0 + u < nc) v[u] = __ldg(row + (size_t)(c0 + u) * 8 + o);
+      if (c0 == 0) stage_act();
 #pragma unroll
       for (int u = 0; u < kGemvU; ++u) {
         if (c0 + u >= nc) break;
@@ -81,15 +87,16 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_exact(MatView w, const in
   } else {
     const int nb = w.cols / 32;
     const ST* srow = (const ST*)w.s + rr * nb;
+    int wv[kGemvU];
+    float sc[kGemvU];
     for (int b0 = 0; b0 < nb; b0 += kGemvU) {
-      int wv[kGemvU];
-      float sc[kGemvU];
 #pragma unroll
       for (int u = 0; u < kGemvU; ++u)
         if (b0 + u < nb) {
           wv[u] = load_word<BITS>(w, rr, b0 + u, o);
           sc[u] = ld_scale(srow, b0 + u);
         }
+      if (b0 == 0) stage_act();
 #pragma unroll
       for (int u = 0; u < kGemvU; ++u) {
         if (b0 + u >= nb) break;
