@@ -159,3 +159,35 @@ def test_twolevel_head_row_formats(torch, isa, tmp_path, head_bits):
             assert abs(lp[b] - want_lp) < 2e-5 and am[b] == want_am, (batch, b, lp[b], want_lp, am[b], want_am)
     g.close()
     o.close()
+
+
+@pytest.mark.parametrize("head_bits", [0, 8, 4])
+def test_twolevel_head_large_classes(torch, isa, tmp_path, head_bits):
+    """Classes of 300 rows: with the F16 output matrix the most likely class's block does not fit in
+    shared memory at once (300 rows of 704 bytes), so the last CTA copies and scores it in two rounds;
+    at batch 32 (one launch, 9 CTAs a hidden state) each CTA takes its 35 tasks in two rounds. The
+    per-token schedule and the batched entry point at batch 1 and 32."""
+    from gem_b200 import SEQUENTIAL
+    cfg = dict(synth.SMALL, d=352, nh=4, nkv=1, hd=64, ff=512, vocab=2400, layers=2)
+    path = synth.write_model(tmp_path / "bigclass.gguf", cfg, seed=21, body="q4_0", head="f16")
+    tl = synth.write_twolevel(tmp_path / "bigclass-k8", cfg["vocab"], 8, cfg["d"], seed=22)
+    o = orc.Model(path, ctx=128, threads=REF_THREADS, isa="avx512", head_bits=head_bits)
+    o.load_twolevel(tl)
+    g = Gemma(path, ctx=128, head_bits=head_bits)
+    g.load_twolevel(tl)
+    g.set_schedule(SEQUENTIAL)
+    _check(g, o, synth.tokens(30, cfg["vocab"], seed=23 + head_bits), TWO_LEVEL, f"large classes head_bits={head_bits}")
+    rng = np.random.default_rng(24 + head_bits)
+    for batch in (1, 32):
+        H = rng.standard_normal((batch, g.d)).astype(np.float32)
+        Tg = rng.integers(0, g.vocab, batch).astype(np.uint32)
+        Hd, Td = torch.tensor(H, device="cuda"), torch.tensor(Tg.astype(np.int32), device="cuda")
+        lp = torch.empty(batch, device="cuda")
+        am = torch.empty(batch, dtype=torch.int32, device="cuda")
+        g.head_twolevel_dev(Hd.data_ptr(), Td.data_ptr(), batch, lp.data_ptr(), am.data_ptr())
+        lp, am = lp.cpu().numpy(), am.cpu().numpy().astype(np.uint32)
+        for b in range(batch):
+            want_lp, want_am = o.twolevel(H[b], int(Tg[b]))
+            assert abs(lp[b] - want_lp) < 2e-5 and am[b] == want_am, (batch, b, lp[b], want_lp, am[b], want_am)
+    g.close()
+    o.close()
