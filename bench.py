@@ -525,7 +525,7 @@ def time_dev(torch, stream, fn, iters, flush):
 def oracle_parity(mf, toks_h, lp, am, head, ctx=CTX):
     """Compares scored log-probs and argmax ids with one untimed oracle pass of the same sequence (the
     oracle's AVX-512 path with the pool size exact numerics reproduce). Bar: identical argmax ids,
-    |d logprob| < 1e-3 nats (north-star); exact numerics give < 2e-5."""
+    |d logprob| < 1e-3 nats, the contract tolerance; exact numerics give < 2e-5."""
     from oracle import oracle as orc
     isa = "avx512" if orc.detect_isa() == "avx512" else None
     o = orc.Model(mf.gguf, ctx=ctx, threads=REF_THREADS, isa=isa)

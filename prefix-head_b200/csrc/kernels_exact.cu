@@ -845,7 +845,7 @@ __global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, 
     if constexpr (BITS != 16)
       if (jb > ja) tl_stage_scales(ssc, (const ST*)T.w.s + (size_t)(tg.first + ja) * nb, (jb - ja) * nb, nb, (const float*)nullptr);
     __syncthreads();  // the scales (and, in round 0, the hidden state) are in place
-    ok = __syncthreads_and(hb_wait(&bar, parity));  // one verdict for the whole CTA
+    ok = __syncthreads_and(hb_wait(&bar, parity));  // one answer for the whole CTA
     parity ^= 1u;
     if (!ok) {
       if (threadIdx.x == 0) atomicExch(T.err, ERR_TIMEOUT);

@@ -14,7 +14,7 @@ from oracle import oracle as orc
 
 pytestmark = pytest.mark.gpu
 
-LP_TOL = 1e-3      # north-star per-token log-prob tolerance (absolute, nats)
+LP_TOL = 1e-3      # per-token log-prob tolerance of the contract (absolute, nats)
 REF_THREADS = 8    # gem bench's default pool size (crates/gem/src/main.rs:197)
 
 
