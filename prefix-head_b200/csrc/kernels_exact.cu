@@ -583,6 +583,7 @@ __global__ void k_tl_top_exact(TwoLevelArgs T, const uint32_t* top_of, float* to
 // its first maximum: the greedy token.
 // ------------------------------------------------------------------------------------------------
 constexpr int kTlThreads = 512, kTlGroups = kTlThreads / 16, kTlPart = 12;
+static_assert(kTlGroups == 32, "k_tl_fused merges its groups' partials with one warp: one group per lane");
 
 // Lane i of dot512 (model.rs:106-120) on a row in shared memory: the sum over chunks c of
 // a[16c + i] * x[16c + i], fused, in order.
