@@ -460,8 +460,9 @@ def parallel_roofline(g, torch, step, info, ms_step, clocks, args, bpt):
     tok_s = SEQ_TOKENS / (ms_step * 1e-3)
     roof = {"bound": "tensor", "unit": "TFLOP/s", "achieved": round(achieved, 2), "peak": tensor_peak,
             "peak_kind": tensor_kind, "frac": round(achieved / tensor_peak, 4), "traffic": gemm_traffic(),
-            "traffic_source": "the committed ncu capture's DRAM bytes per step (profiles/dram_traffic.txt), "
-                              "not measured in this run",
+            "traffic_source": "the committed ncu capture's DRAM bytes per step (profiles/dram_traffic.txt: one "
+                              "layer's launches with L2 as the live step leaves it, x layers), not measured "
+                              "in this run",
             "kernel": "k_seq_gemm (4 launches per layer and sequence part)", "ops_per_step": ops,
             "note": "exact int8 x int8 -> fp32 products on the CUDA cores (the reference's per-block fp32 "
                     "rounding); the tensor-core peak is the dense-contraction bound, cuda_core_view this "
