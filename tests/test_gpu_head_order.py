@@ -92,3 +92,33 @@ def test_head_matvec_in_token_order_after_permutation(torch, isa, small):
     g.matvec_dev(-1, 0, xd.data_ptr(), after.data_ptr())
     assert np.array_equal(before.cpu().numpy().view(np.uint32), after.cpu().numpy().view(np.uint32))
     g.close()
+
+
+def test_partial_class_file_keeps_token_order(torch, isa, small, tmp_path):
+    """A class file that covers only part of the vocabulary (the reference gives the other tokens class
+    0, position 0: main.rs:66-73) leaves the output matrix in token order and gathers the class blocks
+    as a copy; results match the oracle. A covering class file loaded afterwards permutes the matrix and
+    releases that copy: bit-identical to a fresh model that loaded only the covering file."""
+    import numpy as np
+    prefix = tmp_path / "partial"
+    rng = np.random.default_rng(41)
+    rng.permutation(8000).astype("<u4").tofile(str(prefix) + ".order")
+    (rng.standard_normal((64, 256)) * 0.02).astype("<f4").tofile(str(prefix) + ".A")
+    np.zeros(64, "<f4").tofile(str(prefix) + ".b")
+    g = Gemma(small.gguf, ctx=128)
+    g.load_twolevel(prefix)
+    o = orc.Model(small.gguf, ctx=128, threads=REF_THREADS, isa="avx512")
+    o.load_twolevel(prefix)
+    toks = synth.tokens(50, g.vocab, seed=42)
+    for head in (TWO_LEVEL, FULL):
+        lp, am = g.score(toks, head)
+        lpo, amo, _, _ = o.score(toks, head)
+        assert np.abs(lp - lpo).max() < 2e-5 and np.array_equal(am, amo), head
+    o.close()
+    g.load_twolevel(small.twolevel)
+    fresh = Gemma(small.gguf, ctx=128)
+    fresh.load_twolevel(small.twolevel)
+    for (lp, am), (lpf, amf) in zip(_scores(g, toks), _scores(fresh, toks)):
+        assert np.array_equal(lp.view(np.uint32), lpf.view(np.uint32)) and np.array_equal(am, amf)
+    fresh.close()
+    g.close()
