@@ -172,15 +172,24 @@ __global__ void k_attn_prep_exact(AttnArgs A, float* qn) {
 
 // scores[h][i] = dot512(q_h, k_(lo+i)) for every head and position (model.rs:344-353).
 __global__ void k_attn_scores_exact(AttnArgs A, const float* qn, float* scores, int sstride) {
-  pdl_wait();
   const int hd = A.hd, G = A.nh / A.nkv;
-  const uint32_t pos = A.cur->pos;
+  const uint32_t pos = A.cur->pos;  // set when the token began, several kernels back
   const uint32_t lo = (A.window > 0 && pos + 1 > (uint32_t)A.window) ? pos + 1 - A.window : 0;
   const uint32_t n_pos = pos + 1 - lo;
   const int rw = A.nkv * hd;
   const int lane = threadIdx.x & 31, half = lane & 1;
   const int pairs = (blockDim.x * gridDim.x) / 2;
   const uint32_t total = n_pos * A.nh;
+  // The K rows of earlier positions were written by earlier tokens' kernels: their lines come into L1
+  // while the previous kernel (which writes this position's row and the queries) finishes.
+  for (uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) / 2; t < total; t += pairs) {
+    const uint32_t i = t / A.nh, h = t % A.nh;
+    if (lo + i < pos) {
+      const float* k = A.kcache + (size_t)(lo + i) * rw + (h / G) * hd;
+      for (int c = half; c < hd / 32; c += 2) asm volatile("prefetch.global.L1 [%0];" ::"l"(k + 32 * c));
+    }
+  }
+  pdl_wait();
   for (uint32_t t = (blockIdx.x * blockDim.x + threadIdx.x) / 2; t < ((total + 15) / 16) * 16; t += pairs) {
     bool ok = t < total;
     uint32_t tt = ok ? t : 0;
@@ -220,10 +229,9 @@ __global__ void k_attn_softmax_exact(AttnArgs A, float* scores, int sstride) {
 // per = ceil(n_pos / threads); each range accumulates acc = fma(p, v, acc) in order; att = partials
 // summed in thread order. Then Act::quantize of the head's blocks. Grid (nh, hd / 32), block 32 * T.
 __global__ void k_attn_pv_exact(AttnArgs A, const float* scores, int sstride, int threads, int8_t* aq, float* as) {
-  pdl_wait();
   extern __shared__ float part[];  // [threads][32]
   const int hd = A.hd, G = A.nh / A.nkv, h = blockIdx.x, j0 = blockIdx.y * 32;
-  const uint32_t pos = A.cur->pos;
+  const uint32_t pos = A.cur->pos;  // set when the token began, several kernels back
   const uint32_t lo = (A.window > 0 && pos + 1 > (uint32_t)A.window) ? pos + 1 - A.window : 0;
   const int n_pos = (int)(pos + 1 - lo);
   const int per = (n_pos + threads - 1) / threads;
@@ -231,6 +239,14 @@ __global__ void k_attn_pv_exact(AttnArgs A, const float* scores, int sstride, in
   const int lane = threadIdx.x & 31, t = threadIdx.x >> 5;
   const float* p = scores + (size_t)h * sstride;
   const float* vc = A.vcache + (h / G) * hd + j0 + lane;
+  // The V rows were all written by kernels that finished before the previous one (the softmax)
+  // started: this warp's rows come into L1 (one 128-byte line per row) while the softmax runs.
+  for (int tt = t; tt < threads; tt += blockDim.x >> 5) {
+    const int i0 = min(tt * per, n_pos), i1 = min((tt + 1) * per, n_pos);
+    for (int i = i0 + lane; i < i1; i += 32)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(A.vcache + (size_t)(lo + i) * rw + (h / G) * hd + j0));
+  }
+  pdl_wait();
   for (int tt = t; tt < threads; tt += blockDim.x >> 5) {
     float acc = 0.0f;
     int i0 = min(tt * per, n_pos), i1 = min((tt + 1) * per, n_pos);
