@@ -164,6 +164,25 @@ __global__ void k_residual_norm_quant_exact(float* x, const float* delta, const 
 // ------------------------------------------------------------------------------------------------
 // One CTA per kv group; writes normalised q to qn.
 __global__ void k_attn_prep_exact(AttnArgs A, float* qn) {
+  // the norm weights, this position's RoPE rows and the biases depend on no earlier kernel: their
+  // lines come into L1 while the previous kernel (the q/k/v GEMV) finishes
+  {
+    const int hd = A.hd, G = A.nh / A.nkv, g = blockIdx.x;
+    const uint32_t pos = A.cur->pos;  // set when the token began, several kernels back
+    auto pf = [](const float* p, int n) {
+      if (p)
+        for (int j = threadIdx.x * 32; j < n; j += blockDim.x * 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(p + j));
+    };
+    pf(A.q_norm, hd);
+    pf(A.k_norm, hd);
+    pf(A.rope_sin + (size_t)pos * (hd / 2), hd / 2);
+    pf(A.rope_cos + (size_t)pos * (hd / 2), hd / 2);
+    if (A.bqkv) {
+      pf(A.bqkv + (size_t)g * G * hd, G * hd);
+      pf(A.bqkv + (size_t)A.nh * hd + g * hd, hd);
+      pf(A.bqkv + (size_t)A.nh * hd + A.nkv * hd + g * hd, hd);
+    }
+  }
   pdl_wait();
   extern __shared__ __align__(16) float smp[];
   __shared__ float s_r[17];

@@ -115,19 +115,26 @@ __global__ void __launch_bounds__(kNormWarps * 32) k_seq_norm(float* x, const fl
     ((float4*)swpre)[i] = ((const float4*)w_pre)[i];
     if (w_post) ((float4*)swpost)[i] = ((const float4*)w_post)[i];
   }
-  pdl_wait();
-  __syncthreads();
   const int t = blockIdx.x * kNormWarps + warp;
-  if (t >= T) return;
-  float* sq = sn + 2 * d + (size_t)warp * 2 * d + d;
   float4* xt = (float4*)(x + (size_t)t * d);
   float4 xv[kNormMaxV], dv[kNormMaxV];
+  // With a delta the residual stream x was last written by a norm at least three kernels back (the
+  // previous kernel writes only delta), so it loads before the wait too; without one (the first norm,
+  // right after the embedding) it loads after.
+  if (delta && t < T)
+#pragma unroll
+    for (int k = 0; k < kNormMaxV; ++k)
+      if (lane + 32 * k < n4) xv[k] = xt[lane + 32 * k];
+  pdl_wait();
+  __syncthreads();
+  if (t >= T) return;
+  float* sq = sn + 2 * d + (size_t)warp * 2 * d + d;
 #pragma unroll
   for (int k = 0; k < kNormMaxV; ++k) {  // every load of this position issued before any is used
     const int i = lane + 32 * k;
     if (i < n4) {
-      xv[k] = xt[i];
       if (delta) dv[k] = ((const float4*)(delta + (size_t)t * d))[i];
+      else xv[k] = xt[i];
     }
   }
   auto sq4 = [](float4 v) { return make_float4(mul(v.x, v.x), mul(v.y, v.y), mul(v.z, v.z), mul(v.w, v.w)); };
