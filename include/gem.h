@@ -219,8 +219,9 @@ int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float
 int gem_head_full_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
                       float* logprob_dev, uint32_t* argmax_dev);
 /* Two-level head for `batch` hidden states; enqueued like gem_head_full_dev. Exact numerics: one launch
- * below 48 hidden states, the class logits as one product from 48 on (GEM_TL_PRODUCT_MIN sets the
- * switch point); both give the same results. */
+ * below 24 hidden states; from 24 on (GEM_TL_PRODUCT_MIN sets the switch point) the class logits as one
+ * product, then up to 128 states one launch for the blocks and argmax, above that four block kernels.
+ * Every route gives the same results. */
 int gem_head_twolevel_dev(gem_model* m, const float* h_dev, const uint32_t* targets_dev, int batch,
                           float* logprob_dev, uint32_t* argmax_dev);
 /* gem_head_full_dev for callers that cannot allocate device memory when they call it (a process whose

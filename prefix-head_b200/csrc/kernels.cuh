@@ -138,6 +138,7 @@ struct TwoLevelArgs {
   const uint32_t* targets;
   const StepCur* cur;
   float* cl;                 // [batch][k]
+  const float* cl_in;        // [batch][k] class logits already computed (k_tl_fused reads them), or null
   float* inner;              // [batch][per]
   float* lp_out;
   uint32_t* am_out;
@@ -180,10 +181,10 @@ void launch_attn_exact(const AttnArgs& A, float* qn, float* scores, int sstride,
 void launch_head_full_exact(const HeadArgs& H, int batch, int sms, cudaStream_t st);
 void launch_tl_stage1_exact(const TwoLevelArgs& T, int batch, int class_ctas, int block_ctas, cudaStream_t st);
 void launch_tl_top_exact(const TwoLevelArgs& T, int batch, const uint32_t* top_of, float* top_inner, cudaStream_t st);
-// The whole exact two-level head in one launch (cnt: batch counters, zero between launches).
-// The exact two-level head in one launch: P = tl_parts(...) CTAs per hidden state, cnt[batch] zero
-// between launches, part[batch][tl_part_floats(k, per)] floats of per-CTA partials; false (nothing
-// launched) when its staging area does not fit in shared memory.
+// The exact two-level head in one launch: P = tl_parts(...) CTAs per hidden state (ceil(per / 32) when
+// T.cl_in gives the class logits, [batch][k]), cnt[batch] zero between launches,
+// part[batch][tl_part_floats(k, per)] floats of per-CTA partials; false (nothing launched) when its
+// staging area does not fit in shared memory.
 int tl_parts(int k, int per, int batch, int sms);
 int tl_part_floats(int k, int per);
 bool launch_tl_fused(const TwoLevelArgs& T, int batch, int sms, int* cnt, float* part, cudaStream_t st);

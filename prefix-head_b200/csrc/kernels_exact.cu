@@ -822,9 +822,15 @@ __global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, 
   unsigned char* stage = smem_raw + tl_head_off(d);
   float* ssc = (float*)(stage + tl_stage_q(BITS, d, rows_b));                   // staged rows' scales
   uint32_t* sorder = (uint32_t*)(ssc + (size_t)max(rows_b, kTlGroups) * nb);  // the top block's token ids
-  const int tasks_max = T.k + T.per, tpc = (tasks_max + P - 1) / P;
-  const int t_begin = blockIdx.x * tpc;
+  // Tasks: the k class logits, then the target block's rows. With the class logits given (computed
+  // for many hidden states at once by a product), a CTA reads its slice [c_lo, c_hi) of them and takes
+  // only block rows as tasks.
+  const bool given = T.cl_in != nullptr;
+  const int tasks_max = T.k + T.per, tpc = given ? (T.per + P - 1) / P : (tasks_max + P - 1) / P;
+  const int t_begin = given ? T.k + blockIdx.x * tpc : blockIdx.x * tpc;
   int t_end = min(tasks_max, t_begin + tpc);
+  const int c_lo = given ? (int)((long long)T.k * blockIdx.x / P) : 0;
+  const int c_hi = given ? (int)((long long)T.k * (blockIdx.x + 1) / P) : 0;
   const uint32_t abar = smem_u32(&bar);
   // the first round's class rows: A depends on no earlier kernel, so its copy starts before the wait
   const int c0_end = min(min(t_begin + kTlGroups, t_end), T.k);
@@ -908,6 +914,17 @@ __global__ void __launch_bounds__(kTlThreads) k_tl_fused(TwoLevelArgs T, int P, 
         }
       }
     }
+  }
+  if (given) {  // this CTA's slice of the given class logits: a thread each, merged into group leaders
+    TlAcc vc = tl_acc0();
+    for (int c = c_lo + threadIdx.x; c < c_hi; c += kTlThreads) {
+      const float zc = T.cl_in[(size_t)bi * T.k + c];
+      vc.c = lse_add(vc.c, zc);
+      vc.bc = best_merge(vc.bc, Best{zc, (uint32_t)c});
+      if ((uint32_t)c == tg.ct) s_zcl = zc;
+    }
+    vc = tl_warp_merge(vc);
+    if (lane == 0) v = tl_merge(v, vc);  // lane 0 leads group 2 * warp
   }
   if (i == 0) red[g] = v;  // a group's partials sit in its first thread
   __syncthreads();
@@ -1090,12 +1107,13 @@ int tl_parts(int k, int per, int batch, int sms) {
 int tl_part_floats(int k, int per) { return (k + per + 15) / 16 * kTlPart; }
 
 bool launch_tl_fused(const TwoLevelArgs& T, int batch, int sms, int* cnt, float* part, cudaStream_t st) {
+  // with the class logits given, one round of block rows per CTA: ceil(per / 32) CTAs a hidden state
   constexpr size_t kMax = 200 * 1024;
   const int d = T.w.cols;
   int rows_b = T.per;  // the most likely class's block in one copy where it fits
   while (rows_b > 16 && tl_smem(T.w.bits, d, rows_b) > kMax) rows_b -= 16;
   if (d % 32 || tl_smem(T.w.bits, d, rows_b) > kMax) return false;
-  const int P = tl_parts(T.k, T.per, batch, sms);
+  const int P = T.cl_in ? std::max(1, (T.per + kTlGroups - 1) / kTlGroups) : tl_parts(T.k, T.per, batch, sms);
   const size_t sm = tl_smem(T.w.bits, d, rows_b);
 #define F(B, S)                                                                                     \
   do {                                                                                              \

@@ -550,24 +550,40 @@ struct gem_model {
     seq_cap = T;
   }
 
-  // Head over T final hidden states (s_h, s_haq, s_has) with targets[0..T); returns the kernels launched.
   // The exact two-level head over T hidden states (fp32 hh, quantized qa / sa) as the class logits'
   // tile product (every class row read once for all T) and the block kernels: target block, top
   // class, top block, argmax. Returns the kernels launched.
+  // one_launch_tail: up to kTlGivenMax states, the blocks, log-sum-exps and argmax by k_tl_fused reading
+  // the class logits (it quantizes hh itself) instead of the four block kernels; qa, sa may then be
+  // null. Above that, ceil(per / 32) CTAs a state with a last-CTA block pass each lose to the block
+  // kernels (256 states: 81 us against 69 us).
+  static constexpr int kTlGivenMax = 128;
   int twolevel_product(const int8_t* qa, const float* sa, const float* hh, const uint32_t* targets, int T, float* lpo,
-                       uint32_t* amo) {
+                       uint32_t* amo, bool one_launch_tail = false) {
     ensure_head_batch(T);
     launch_seq_class_logits(A, b, k, hh, d, T, cl, st);
     TwoLevelArgs TL = tl_args(qa, sa, hh, targets, lpo, amo);
+    if (one_launch_tail && T <= kTlGivenMax) {
+      TL.cl_in = cl;
+      if (launch_tl_fused(TL, T, sms, tl_cnt, tl_part, st)) return 2;
+      TL.cl_in = nullptr;
+    }
+    const bool quantize = !qa;  // the block kernels below need the quantized states
+    if (quantize) {
+      launch_quantize(hh, T * d, hb_q, hb_s, st);
+      TL.aq = hb_q, TL.as = hb_s;
+    }
     TL.class_ctas = 0;
     const int block_ctas = std::max(1, std::min(8, (per + 127) / 128));
     launch_tl_stage1_exact(TL, T, 0, block_ctas, st);
     launch_tl_select(TL, T, top_of, st);
     launch_tl_top_exact(TL, T, top_of, top_inner, st);
     launch_tl_argmax(TL, T, top_of, top_inner, st);
-    return 5;
+    return quantize ? 6 : 5;
   }
   int seq_head(int which, const uint32_t* targets, int T, float* lpo, uint32_t* amo) {
+    // the block kernels at every T: a sequence's log-probs stay bit-identical whether it is scored alone
+    // or in a batch (the one-launch tail merges the log-sum-exps in another order)
     if (which == 1) return twolevel_product(s_haq, s_has, s_h, targets, T, lpo, amo);
     if (comm) return seq_head_sharded(targets, T, lpo, amo);
     if (!full_head_gemm_supported()) {  // the per-position exact head kernels
@@ -1956,11 +1972,12 @@ int gem_matvec_dev(gem_model* m, int layer, int which, const float* x_dev, float
 
 constexpr int kHeadGemmMin = 12;  // ~30 us per streamed state vs ~0.37 ms per 32-state product tile
 // from this many hidden states on, the two-level head's class logits are one tile product (every class
-// row read once) instead of the one-launch kernel's per-state passes
+// row read once) instead of the one-launch kernel's per-state passes (2048 classes: 37.7 against
+// 43.1 us at 32 states, 33.8 against ~32 us at 16)
 static int two_level_product_min() {
   static const int v = [] {
     const char* e = std::getenv("GEM_TL_PRODUCT_MIN");
-    return e ? std::max(1, std::atoi(e)) : 48;
+    return e ? std::max(1, std::atoi(e)) : 24;
   }();
   return v;
 }
@@ -1976,12 +1993,12 @@ static int batch_head(gem_model* m, int which, const float* h_dev, const uint32_
   const bool product = which == 0 && m->exact && !m->comm && batch >= kHeadGemmMin && m->full_head_gemm_supported();
   const bool tl_product = which == 1 && m->exact && batch >= two_level_product_min();
   // the streamed full head and the one-launch two-level head quantize the hidden states in their CTAs
-  const bool self_quant = (which == 0 && m->exact && m->head_bulk_q && !product) || (which == 1 && m->exact && !tl_product);
+  const bool self_quant = (which == 0 && m->exact && m->head_bulk_q && !product) || (which == 1 && m->exact);
   if (!self_quant) launch_quantize(h_dev, batch * m->d, m->hb_q, m->hb_s, m->st);
   if (product)
     m->full_head_gemm(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
   else if (tl_product)
-    m->twolevel_product(m->hb_q, m->hb_s, h_dev, targets_dev, batch, lp_dev, am_dev);
+    m->twolevel_product(nullptr, nullptr, h_dev, targets_dev, batch, lp_dev, am_dev, true);
   else
     m->run_head(which, self_quant ? nullptr : m->hb_q, self_quant ? nullptr : m->hb_s, h_dev, targets_dev, batch,
                 lp_dev, am_dev);
