@@ -89,23 +89,66 @@ def hbm_peak():
 
 
 class Clocks:
-    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    """SM clock and throttle-reason samples while the timed region runs (reading only; nothing here
+    changes a clock or a setting). NVML is polled every 5 ms from a thread, because the default run's
+    timed region lasts ~0.1 s; where NVML cannot be opened, nvidia-smi's own loop (-lms 50) samples
+    the same fields. `nvml` replaces the pynvml module (a fake in the CPU tests)."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    # NVML clocks-event reason bits (nvmlClocksEventReason*), named as nvidia-smi names the fields
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+    PERIOD_S = 0.005
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, nvml=None):
         self.device = device
+        self.nvml = nvml
+        self.N = None
+        self.samples = []  # NVML: (sm MHz, max sm MHz, reason bits)
+        self.stop = threading.Event()
+        self.t = None
         self.proc = None
         self.lines = []
 
+    def _nvml_handle(self, N):
+        try:  # the CUDA ordinal and the NVML index need not agree: match by UUID
+            import torch
+            u = str(torch.cuda.get_device_properties(self.device).uuid)
+            return N.nvmlDeviceGetHandleByUUID(u if u.startswith("GPU-") else "GPU-" + u)
+        except Exception:
+            return N.nvmlDeviceGetHandleByIndex(self.device)
+
+    def _poll(self, h, mx):
+        N = self.N
+        try:
+            while not self.stop.is_set():
+                self.samples.append((float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)), mx,
+                                     int(N.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                self.stop.wait(self.PERIOD_S)
+        except Exception:
+            pass
+
     def __enter__(self):
+        try:
+            N = self.nvml
+            if N is None:
+                import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            h = self._nvml_handle(N)
+            mx = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._poll, args=(h, mx), daemon=True)
+            self.t.start()
+            while not self.samples and self.t.is_alive():  # the timed region starts once a sample is in
+                time.sleep(0.001)
+            return self
+        except Exception:
+            self._close_nvml()
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            threading.Thread(target=self._read, daemon=True).start()
             t0 = time.time()  # the timed region starts once the sampler is running
             while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
                 time.sleep(0.01)
@@ -118,7 +161,19 @@ class Clocks:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def _close_nvml(self):
+        if self.t:
+            self.stop.set()
+            self.t.join(timeout=5)
+        if self.N:
+            try:
+                self.N.nvmlShutdown()
+            except Exception:
+                pass
+            self.N = None
+
     def __exit__(self, *a):
+        self._close_nvml()
         if self.proc:
             self.proc.terminate()
             try:
@@ -128,22 +183,29 @@ class Clocks:
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
+        if self.samples:
+            for mhz, mx, bits in self.samples:
+                sm.append(mhz)
+                reasons.update(n for n, b in self.REASON_BITS.items() if bits & b)
+            source = "nvml"
+        else:
+            for ln in self.lines:
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+            source = "nvidia-smi"
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": source}
 
 
 def model_files():

@@ -84,3 +84,53 @@ def test_roofline_bytes_of_the_270m_geometry():
     want = body + classes + block + kv + vectors
     assert bench.bytes_per_token(info, npos, 0.0) == want == 121_609_728
     assert bench.bytes_per_token(info, npos, 1.0) == want + block  # the top class's block too
+
+
+class _FakeNvml:
+    """The NVML calls bench.Clocks makes, with a clock and reason bits that change between samples."""
+    NVML_CLOCK_SM = 1
+
+    def __init__(self):
+        self.n = 0
+        self.shut = False
+
+    def nvmlInit(self):
+        pass
+
+    def nvmlShutdown(self):
+        self.shut = True
+
+    def nvmlDeviceGetHandleByUUID(self, uuid):
+        raise RuntimeError("no CUDA device here")
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return ("gpu", i)
+
+    def nvmlDeviceGetMaxClockInfo(self, h, which):
+        return 1965
+
+    def nvmlDeviceGetClockInfo(self, h, which):
+        self.n += 1
+        return 1965 if self.n % 3 else 1800
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        return 0x4 if self.n % 2 else 0x1  # sw_power_cap on odd samples; gpu_idle (not reported) on even
+
+
+def test_clock_sampler_reads_nvml_during_the_region():
+    """The sampler polls NVML from a thread while the region runs and reports the median SM clock, the
+    maximum and the throttle reasons by nvidia-smi's field names; it only reads."""
+    import importlib
+    import time
+    sys.path.insert(0, str(ROOT))
+    bench = importlib.import_module("bench")
+    fake = _FakeNvml()
+    with bench.Clocks(0, nvml=fake) as clk:
+        time.sleep(0.1)
+    s = clk.summary()
+    assert s["source"] == "nvml" and s["samples"] >= 5 and fake.shut
+    assert s["sm_max_mhz"] == 1965 and s["sm_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"]
+    n = s["samples"]
+    time.sleep(0.05)
+    assert clk.summary()["samples"] == n  # nothing sampled after the region
