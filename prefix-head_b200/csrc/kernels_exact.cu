@@ -616,6 +616,9 @@ __global__ void k_tl_top_exact(TwoLevelArgs T, const uint32_t* top_of, float* to
 // of a hidden state (a per-item counter, zero between launches) merges them, stages the most likely
 // class's block in one copy (unless it is the target's, whose logits are already written) and takes
 // its first maximum: the greedy token.
+// With the class logits given (T.cl_in, [batch][k], from the tile product over many hidden states),
+// the tasks are the target block's rows alone, 32 a CTA, and each CTA also folds its slice of the
+// given logits (classes [k * x / P, k * (x + 1) / P) for CTA x) into its class partial.
 // ------------------------------------------------------------------------------------------------
 constexpr int kTlThreads = 512, kTlGroups = kTlThreads / 16, kTlPart = 12;
 static_assert(kTlGroups == 32, "k_tl_fused merges its groups' partials with one warp: one group per lane");
